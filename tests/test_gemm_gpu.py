@@ -1,0 +1,70 @@
+"""tcgen05 GEMM numerics against an fp32 PyTorch reference of the same product."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(a, b):
+    return a.float() @ b.float().t()
+
+
+def _check(out, ref, tol=2e-2):
+    err = (out.float() - ref).abs().max().item()
+    scale = ref.abs().max().item() + 1e-6
+    assert err / scale < tol, f"max rel err {err / scale:.3e}"
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 128), (1000, 1280, 1280),
+                                   (4096, 3840, 1280), (333, 200, 72), (64, 128, 8192)])
+def test_linear_fwd(cuda_device, M, N, K):
+    from trainium_frontier_b200.ops import gemm
+    from trainium_frontier_b200.ops._ext import check_errors
+    torch.manual_seed(0)
+    x = torch.randn(M, K, device=cuda_device, dtype=torch.bfloat16)
+    w = torch.randn(N, K, device=cuda_device, dtype=torch.bfloat16) * K ** -0.5
+    y = gemm.linear_fwd(x, w)
+    check_errors()
+    _check(y, _ref(x, w))
+    r = torch.randn(M, N, device=cuda_device, dtype=torch.bfloat16)
+    y2 = gemm.linear_fwd(x, w, residual=r)
+    _check(y2, _ref(x, w) + r.float())
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 512, 128), (2048, 5120, 1280), (200, 1000, 96)])
+def test_relu2_fwd_bwd(cuda_device, M, N, K):
+    from trainium_frontier_b200.ops import gemm
+    torch.manual_seed(1)
+    x = torch.randn(M, K, device=cuda_device, dtype=torch.bfloat16)
+    w = torch.randn(N, K, device=cuda_device, dtype=torch.bfloat16) * K ** -0.5
+    act, h = gemm.linear_relu2_fwd(x, w)
+    href = _ref(x, w)
+    _check(h, href)
+    _check(act, torch.relu(href) ** 2)
+    dy = torch.randn(M, K, device=cuda_device, dtype=torch.bfloat16)
+    # dh = (dy @ w) * 2 relu(h) with w viewed [N, K] -> here dact[M,N] = dy2[M,K'] @ W2[K',N]
+    w2 = torch.randn(K, N, device=cuda_device, dtype=torch.bfloat16) * N ** -0.5
+    dact_ref = dy.float() @ w2.float()
+    dh = gemm.linear_dx(dy, w2, relu2_h=h)
+    _check(dh, dact_ref * 2 * torch.relu(h.float()))
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 128), (4096, 1280, 1280), (8192, 1280, 5120), (300, 136, 72)])
+def test_linear_dx_dw(cuda_device, M, N, K):
+    from trainium_frontier_b200.ops import gemm
+    from trainium_frontier_b200.ops._ext import check_errors
+    torch.manual_seed(2)
+    dy = torch.randn(M, N, device=cuda_device, dtype=torch.bfloat16)
+    w = torch.randn(N, K, device=cuda_device, dtype=torch.bfloat16) * N ** -0.5
+    x = torch.randn(M, K, device=cuda_device, dtype=torch.bfloat16)
+    dx = gemm.linear_dx(dy, w)
+    _check(dx, dy.float() @ w.float())
+    g = torch.zeros(N, K, device=cuda_device, dtype=torch.float32)
+    gemm.linear_dw(dy, x, g, accumulate=True)
+    ref = dy.float().t() @ x.float()
+    _check(g, ref)
+    gemm.linear_dw(dy, x, g, accumulate=True)
+    _check(g, 2 * ref)
+    gemm.linear_dw(dy, x, g, accumulate=False, split_k=1)
+    _check(g, ref)
+    check_errors()

@@ -1,0 +1,49 @@
+// Python bindings of the sm_100a kernels (module trainium_frontier_b200._C).
+#include <torch/extension.h>
+
+namespace tfb {
+void gemm_bf16(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_mn, int64_t M, int64_t N, int64_t K,
+               torch::Tensor D, int64_t epi, double alpha, double beta, c10::optional<torch::Tensor> R,
+               c10::optional<torch::Tensor> D2, double tau, int64_t split_k, int64_t bn, torch::Tensor err,
+               c10::optional<torch::Tensor> alpha_t, double rcoef);
+void rmsnorm_fwd(torch::Tensor x, torch::Tensor y, c10::optional<torch::Tensor> rstd);
+void rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor rstd, c10::optional<torch::Tensor> dadd,
+                 torch::Tensor dx);
+void mix_norm_fwd(torch::Tensor x, torch::Tensor x0, torch::Tensor lr, torch::Tensor l0, torch::Tensor xm,
+                  torch::Tensor h, torch::Tensor rstd);
+void mix_norm_bwd(torch::Tensor dxm, torch::Tensor dh, torch::Tensor x, torch::Tensor x0, torch::Tensor xm,
+                  torch::Tensor rstd, torch::Tensor lr, torch::Tensor l0, torch::Tensor dx, torch::Tensor dx0_acc,
+                  bool dx0_init, torch::Tensor dlr, torch::Tensor dl0);
+void embed_norm_fwd(torch::Tensor idx, torch::Tensor wte, torch::Tensor out, torch::Tensor rstd);
+void embed_norm_bwd(torch::Tensor idx, torch::Tensor wte, torch::Tensor rstd, c10::optional<torch::Tensor> gacc,
+                    c10::optional<torch::Tensor> gb, torch::Tensor dwte);
+void rope_norm_fwd(torch::Tensor buf, int64_t head0, int64_t nheads, int64_t D, torch::Tensor cos,
+                   torch::Tensor sin, int64_t T, int64_t pos_offset, c10::optional<torch::Tensor> rstd,
+                   c10::optional<torch::Tensor> out);
+void rope_norm_bwd(torch::Tensor gbuf, torch::Tensor zbuf, int64_t head0, int64_t nheads, int64_t D,
+                   torch::Tensor cos, torch::Tensor sin, int64_t T, torch::Tensor rstd);
+void softcap_ce(torch::Tensor logits, torch::Tensor targets, int64_t T, c10::optional<torch::Tensor> row_w,
+                int64_t V, double S, double scale, torch::Tensor loss, bool write_grad);
+void adamw_multi(std::vector<torch::Tensor> params, std::vector<torch::Tensor> grads, std::vector<torch::Tensor> m,
+                 std::vector<torch::Tensor> v, torch::Tensor lr, double beta1, double beta2, double eps, double wd,
+                 std::vector<double> bc1, std::vector<double> bc2, bool cautious);
+}  // namespace tfb
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  namespace py = pybind11;
+  m.doc() = "trainium_frontier_b200 sm_100a kernels";
+  m.def("gemm_bf16", &tfb::gemm_bf16, "tcgen05 bf16 GEMM with fused epilogues", py::arg("A"), py::arg("a_mn"),
+        py::arg("B"), py::arg("b_mn"), py::arg("M"), py::arg("N"), py::arg("K"), py::arg("D"), py::arg("epi"),
+        py::arg("alpha"), py::arg("beta"), py::arg("R"), py::arg("D2"), py::arg("tau"), py::arg("split_k"),
+        py::arg("bn"), py::arg("err"), py::arg("alpha_t") = py::none(), py::arg("rcoef") = 1.0);
+  m.def("rmsnorm_fwd", &tfb::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &tfb::rmsnorm_bwd);
+  m.def("mix_norm_fwd", &tfb::mix_norm_fwd);
+  m.def("mix_norm_bwd", &tfb::mix_norm_bwd);
+  m.def("embed_norm_fwd", &tfb::embed_norm_fwd);
+  m.def("embed_norm_bwd", &tfb::embed_norm_bwd);
+  m.def("rope_norm_fwd", &tfb::rope_norm_fwd);
+  m.def("rope_norm_bwd", &tfb::rope_norm_bwd);
+  m.def("softcap_ce", &tfb::softcap_ce);
+  m.def("adamw_multi", &tfb::adamw_multi);
+}

@@ -1,0 +1,487 @@
+"""The GPT family (reference ``train.py:1407-1433``, ``train.py:2237-3485``).
+
+Plain member (default): untied ``wte``/``lm_head`` with vocab padded to a multiple of
+64; the embedding is RMS-normed and kept as ``x0``; each block mixes
+``x <- resid_lambda * x + x0_lambda * x0`` (learned per-block scalars), then pre-norm
+attention (RoPE followed by parameter-free QK RMSNorm, causal) and a relu^2 MLP; final
+norm, ``lm_head``, logit softcap ``S tanh(z / S)``.
+
+Module and parameter names are the reference's, so ``state_dict`` keys -- and therefore
+the ``out/final.pt`` payload -- are interchangeable (``transformer.wte.weight``,
+``transformer.h.{i}.attn.c_q.weight``, ..., ``transformer.h.{i}.resid_lambda``,
+``lm_head.weight``, ``value_embeds.{i}.weight``, ``ngram_embeds.b{i}.weight``).
+
+Optional members of the family, all off by default and all step-0 no-ops where the
+reference's are: value embeddings with input gates (``ve``), hashed bigram/trigram
+value embeddings (``ngram_ve``), depthwise causal conv (``local_conv``), causal Q/K
+token shift (``qk_shift``), per-head output gate (``head_gate``), output pooling of the
+last layers (``out_pool``), input-dependent x0 gate (``x0_gate``), MLP sandwich norm,
+shifted relu^2 (``relu2_tau``), gated / SwiGLU MLP, GQA (``n_kv_heads``), explicit
+attention scale, document masking and sliding-window layers, the output bigram table
+(``out_bigram``).
+
+Hot path: on CUDA with the plain configuration each block is five fused kernels plus
+attention: [mix + norm] -> [QKV GEMM] -> [RoPE + QK-norm + attention] -> [proj GEMM +
+residual] -> [norm] -> [fc GEMM + relu^2] -> [proj GEMM + residual].
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import asdict
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .. import ops
+from ..config import GPTConfig, RunConfig, parse_int_tuple
+
+
+class Linear(nn.Linear):
+    """Bias-free linear whose forward runs through ``ops.linear`` (the fp32 weight is
+    cast to the compute dtype; on the GPU a cached bf16 copy is used)."""
+
+    def __init__(self, in_features: int, out_features: int, bias: bool = False):
+        super().__init__(in_features, out_features, bias=False)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return ops.linear(x, self.weight)
+
+
+class CausalConv(nn.Module):
+    """Depthwise causal conv1d with K-1 left padding, zero-init (train.py:1316-1329)."""
+
+    def __init__(self, channels: int, kernel: int):
+        super().__init__()
+        self.kernel = kernel
+        self.weight = nn.Parameter(torch.zeros(channels, 1, kernel))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:  # [B, T, C]
+        xt = F.pad(x.transpose(1, 2), (self.kernel - 1, 0))
+        return F.conv1d(xt, self.weight.to(x.dtype), groups=x.shape[-1]).transpose(1, 2)
+
+
+def causal_shift_1(x: torch.Tensor) -> torch.Tensor:
+    return F.pad(x[:, :-1], (0, 0, 1, 0))
+
+
+def has_ve(layer_idx: int, n_layer: int) -> bool:
+    """Value embeddings on alternating layers, always including the last."""
+    return layer_idx % 2 == (n_layer - 1) % 2
+
+
+def _ngram_layers(spec: str, n_layer: int) -> set[int]:
+    if not spec:
+        return {i for i in range(n_layer) if has_ve(i, n_layer)}
+    out = set()
+    for v in parse_int_tuple(spec):
+        out.add(v % n_layer)
+    return out
+
+
+def _next_prime(n: int) -> int:
+    def is_prime(k):
+        if k < 2:
+            return False
+        if k % 2 == 0:
+            return k == 2
+        r = int(k ** 0.5)
+        for d in range(3, r + 1, 2):
+            if k % d == 0:
+                return False
+        return True
+    while not is_prime(n):
+        n += 1
+    return n
+
+
+def _largest_prime_below(n: int) -> int:
+    k = n
+    while k > 2:
+        if all(k % d for d in range(2, int(k ** 0.5) + 1)):
+            return k
+        k -= 1
+    return 2
+
+
+def _ngram_primes(layer_idx: int) -> tuple[int, int, int]:
+    """Layer-dependent multipliers, bounded so id * p fits int32 for ids < 2^14."""
+    base = 1000 + 97 * layer_idx
+    p1 = _next_prime(base * 31 + 7)
+    p2 = _next_prime(base * 53 + 11)
+    p3 = _next_prime(base * 71 + 13)
+    return p1, p2, p3
+
+
+class CausalSelfAttention(nn.Module):
+    def __init__(self, config: GPTConfig, rc: RunConfig, layer_idx: int):
+        super().__init__()
+        self.n_head = config.n_head
+        self.n_embd = config.n_embd
+        self.head_dim = config.n_embd // config.n_head
+        self.n_kv_heads = config.n_kv_heads or config.n_head
+        if self.n_head % self.n_kv_heads:
+            raise ValueError("n_kv_heads must divide n_head")
+        self.kv_repeat = self.n_head // self.n_kv_heads
+        self.c_q = Linear(config.n_embd, config.n_embd)
+        self.c_k = Linear(config.n_embd, self.n_kv_heads * self.head_dim)
+        self.c_v = Linear(config.n_embd, self.n_kv_heads * self.head_dim)
+        self.c_proj = Linear(config.n_embd, config.n_embd)
+        self.attn_scale = config.attn_scale if config.attn_scale > 0.0 else None
+        gc = rc.ve_gate_channels
+        self.gate_channels = gc
+        self.ve_gate = Linear(gc, self.n_head) if (rc.ve and has_ve(layer_idx, config.n_layer)) else None
+        ng = rc.ngram_ve and layer_idx in _ngram_layers(rc.ngram_ve_layers, config.n_layer)
+        self.ve_gate_bi = Linear(gc, self.n_head) if ng else None
+        self.ve_gate_tri = Linear(gc, self.n_head) if (ng and rc.ngram_ve_trigram) else None
+        if rc.head_gate:
+            lo = min(3 * gc, max(0, config.n_embd - rc.head_gate_channels))
+            self.head_gate_lo, self.head_gate_hi = lo, lo + rc.head_gate_channels
+            self.head_gate = Linear(rc.head_gate_channels, self.n_head)
+            self.head_gate_bias = nn.Parameter(torch.full((self.n_head,), float(rc.head_gate_bias)))
+        else:
+            self.head_gate = None
+        self.head_gate_norm = rc.head_gate_norm
+        self.head_gate_mul = rc.head_gate_mul
+
+    @property
+    def plain(self) -> bool:
+        return (self.ve_gate is None and self.ve_gate_bi is None and self.ve_gate_tri is None
+                and self.head_gate is None and self.kv_repeat == 1)
+
+    def forward(self, x_q, x_k, x_v, ve, cos, sin, attn_mask, ve_bi=None, ve_tri=None):
+        b, t, c = x_q.shape
+        if self.plain and attn_mask is None and x_q is x_k and x_k is x_v:
+            qkv = ops.linear_multi(x_q, [self.c_q.weight, self.c_k.weight, self.c_v.weight])
+            y = ops.attention_qkv(qkv, cos, sin, self.n_head, self.head_dim, self.attn_scale)
+            return y  # c_proj (+ residual) is applied by the block
+        q = ops.linear(x_q, self.c_q.weight).view(b, t, self.n_head, self.head_dim)
+        k = ops.linear(x_k, self.c_k.weight).view(b, t, self.n_kv_heads, self.head_dim)
+        v = ops.linear(x_v, self.c_v.weight).view(b, t, self.n_kv_heads, self.head_dim)
+        if self.kv_repeat > 1:
+            k = k.repeat_interleave(self.kv_repeat, dim=2).contiguous()
+            v = v.repeat_interleave(self.kv_repeat, dim=2).contiguous()
+        gc = self.gate_channels
+        if ve is not None:
+            gate = 2 * torch.sigmoid(ops.linear(x_v[..., :gc], self.ve_gate.weight))
+            v = v + gate.unsqueeze(-1) * ve.view(b, t, self.n_head, self.head_dim)
+        if ve_bi is not None:
+            g_bi = 2 * torch.sigmoid(ops.linear(x_v[..., gc:2 * gc], self.ve_gate_bi.weight))
+            v = v + g_bi.unsqueeze(-1) * ve_bi.view(b, t, self.n_head, self.head_dim)
+        if ve_tri is not None:
+            g_tri = 2 * torch.sigmoid(ops.linear(x_v[..., 2 * gc:3 * gc], self.ve_gate_tri.weight))
+            v = v + g_tri.unsqueeze(-1) * ve_tri.view(b, t, self.n_head, self.head_dim)
+        q = ops.rope_norm(q, cos, sin)
+        k = ops.rope_norm(k, cos, sin)
+        y = ops.attention(q, k, v, causal=attn_mask is None, scale=self.attn_scale,
+                          attn_mask=None if attn_mask is None else attn_mask[..., :t, :t].to(q.dtype))
+        y = y.reshape(b, t, c)
+        if self.head_gate is not None:
+            yh = y.view(b, t, self.n_head, self.head_dim)
+            if self.head_gate_norm:
+                yh = ops.norm(yh)
+            g = ops.linear(x_q[..., self.head_gate_lo:self.head_gate_hi], self.head_gate.weight)
+            g = self.head_gate_mul * torch.sigmoid(g + self.head_gate_bias.to(g.dtype))
+            y = (yh * g.unsqueeze(-1)).view(b, t, c)
+        return y
+
+
+class MLP(nn.Module):
+    def __init__(self, config: GPTConfig, rc: RunConfig):
+        super().__init__()
+        hidden = config.mlp_ratio * config.n_embd
+        self.swiglu_hidden = 0
+        if rc.coalesced_swiglu:
+            exact = (2.0 / 3.0) * config.mlp_ratio * config.n_embd
+            self.swiglu_hidden = max(128, int(round(exact / 128.0)) * 128)
+            hidden = self.swiglu_hidden
+        fc_out = 2 * hidden if self.swiglu_hidden else hidden
+        self.c_fc = Linear(config.n_embd, fc_out)
+        self.c_gate = Linear(config.n_embd, hidden) if rc.gated_mlp else None
+        self.c_proj = Linear(hidden, config.n_embd)
+        self.tau = rc.relu2_tau
+
+    @property
+    def plain(self) -> bool:
+        return not self.swiglu_hidden and self.c_gate is None
+
+    def forward(self, x, residual=None):
+        if self.plain:
+            return ops.mlp_relu2(x, self.c_fc.weight, self.c_proj.weight, residual, self.tau)
+        h = ops.linear(x, self.c_fc.weight)
+        if self.swiglu_hidden:
+            a = F.silu(h[..., :self.swiglu_hidden]) * h[..., self.swiglu_hidden:]
+        else:
+            a = h * F.silu(ops.linear(x, self.c_gate.weight))
+        return ops.linear(a, self.c_proj.weight, residual)
+
+
+class Block(nn.Module):
+    def __init__(self, config: GPTConfig, rc: RunConfig, layer_idx: int):
+        super().__init__()
+        self.attn = CausalSelfAttention(config, rc, layer_idx)
+        self.mlp = MLP(config, rc)
+        self.resid_lambda = nn.Parameter(torch.ones(1))
+        self.x0_lambda = nn.Parameter(torch.zeros(1))
+        self.x0_gate_s = nn.Parameter(torch.zeros(1)) if rc.x0_gate else None
+        self.local_conv = CausalConv(config.n_embd, rc.local_conv_kernel) if rc.local_conv else None
+        self.qk_shift_beta = (nn.Parameter(torch.full((config.n_embd,), float(rc.qk_shift_beta)),
+                                           requires_grad=not rc.qk_shift_freeze) if rc.qk_shift else None)
+        self.sandwich = rc.mlp_sandwich_norm
+
+    def forward(self, x, x0, ve, cos, sin, attn_mask, ve_bi=None, ve_tri=None):
+        fast = (self.x0_gate_s is None and self.local_conv is None and self.qk_shift_beta is None
+                and not self.sandwich and attn_mask is None and self.attn.plain)
+        if fast:
+            xm, h = ops.mix_norm(x, x0, self.resid_lambda, self.x0_lambda)
+            y = self.attn(h, h, h, None, cos, sin, None)
+            x = ops.linear(y, self.attn.c_proj.weight, residual=xm)
+            return self.mlp(ops.norm(x), residual=x)
+        if self.x0_gate_s is not None:
+            gate0 = 2.0 * torch.sigmoid(self.x0_gate_s * x.mean(dim=-1, keepdim=True))
+            x = self.resid_lambda * x + self.x0_lambda * (gate0 * x0)
+        else:
+            x = self.resid_lambda * x + self.x0_lambda * x0
+        x = x.to(x0.dtype)
+        q_in = k_in = v_in = x
+        if self.qk_shift_beta is not None:
+            q_in = k_in = x + self.qk_shift_beta.to(x.dtype) * causal_shift_1(x)
+        if self.local_conv is not None:
+            x = x + self.local_conv(ops.norm(x))
+            v_in = x if self.qk_shift_beta is None else v_in
+            if self.qk_shift_beta is None:
+                q_in = k_in = x
+        hq = ops.norm(q_in)
+        hk = hq if k_in is q_in else ops.norm(k_in)
+        hv = hq if v_in is q_in else ops.norm(v_in)
+        y = self.attn(hq, hk, hv, ve, cos, sin, attn_mask, ve_bi, ve_tri)
+        x = ops.linear(y, self.attn.c_proj.weight, residual=x)
+        if self.sandwich:
+            return x + ops.norm(self.mlp(ops.norm(x)))
+        return self.mlp(ops.norm(x), residual=x)
+
+
+def _build_window_mask(T: int, window: int) -> torch.Tensor:
+    i = torch.arange(T)[:, None]
+    j = torch.arange(T)[None, :]
+    keep = (j <= i) & (j > i - window)
+    m = torch.zeros(T, T)
+    m.masked_fill_(~keep, float("-inf"))
+    return m
+
+
+def doc_boundary_mask(idx: torch.Tensor, bos: int = 0) -> torch.Tensor:
+    """Additive [B, 1, T, T] mask blocking attention across BOS-delimited documents."""
+    doc = (idx == bos).cumsum(dim=1)
+    same = doc[:, :, None] == doc[:, None, :]
+    m = torch.zeros(same.shape, dtype=torch.float32, device=idx.device)
+    m.masked_fill_(~same, float("-inf"))
+    return m[:, None]
+
+
+class GPT(nn.Module):
+    def __init__(self, config: GPTConfig, rc: RunConfig | None = None):
+        super().__init__()
+        rc = rc or RunConfig()
+        self.config = config
+        self.rc = rc
+        V = config.padded_vocab_size
+        self.transformer = nn.ModuleDict({
+            "wte": nn.Embedding(V, config.n_embd),
+            "h": nn.ModuleList([Block(config, rc, i) for i in range(config.n_layer)]),
+        })
+        self.lm_head = Linear(config.n_embd, V)
+        self.value_embeds = nn.ModuleDict({str(i): nn.Embedding(V, config.n_embd)
+                                           for i in range(config.n_layer)
+                                           if rc.ve and has_ve(i, config.n_layer)})
+        self.ngram_rows = rc.ngram_ve_table_mult * V
+        self.ngram_dim = rc.ngram_ve_dim if rc.ngram_ve_dim > 0 else config.n_embd
+        tables = {}
+        if rc.ngram_ve:
+            self.ngram_mod = _largest_prime_below(self.ngram_rows) if self.ngram_rows < 5_000_000 else self.ngram_rows - 1
+            dt = torch.bfloat16 if rc.ngram_ve_bf16 else torch.float32
+            for i in sorted(_ngram_layers(rc.ngram_ve_layers, config.n_layer)):
+                tables[f"b{i}"] = nn.Embedding(self.ngram_rows, self.ngram_dim,
+                                               _weight=torch.zeros(self.ngram_rows, self.ngram_dim, dtype=dt))
+                if rc.ngram_ve_trigram:
+                    tables[f"t{i}"] = nn.Embedding(self.ngram_rows, self.ngram_dim,
+                                                   _weight=torch.zeros(self.ngram_rows, self.ngram_dim, dtype=dt))
+        self.ngram_embeds = nn.ModuleDict(tables)
+        self.ngram_proj = nn.ModuleDict({k: Linear(self.ngram_dim, config.n_embd) for k in tables}
+                                        if self.ngram_dim != config.n_embd else {})
+        self.ngram_pad_id = V
+        if rc.out_bigram:
+            self.out_bigram = nn.Embedding(V, V, _weight=torch.zeros(V, V))
+            self.out_bigram_gate = Linear(config.n_embd, 1)
+            self.out_bigram_gate_bias = nn.Parameter(torch.full((1,), float(rc.out_bigram_gate_bias)))
+        else:
+            self.out_bigram = None
+        self.out_pool_lambdas = (nn.Parameter(torch.zeros(min(rc.out_pool_layers, config.n_layer)))
+                                 if rc.out_pool else None)
+        cos, sin = self._precompute_rotary_embeddings(config.sequence_len, config.head_dim)
+        self.register_buffer("cos", cos, persistent=False)
+        self.register_buffer("sin", sin, persistent=False)
+        pattern = (rc.window_pattern * (config.n_layer // max(1, len(rc.window_pattern)) + 1))[:config.n_layer]
+        self.layer_is_short = [c == "S" for c in pattern]
+        if any(self.layer_is_short):
+            short = max(1, int(config.sequence_len * rc.short_window_frac))
+            self.register_buffer("mask_short", _build_window_mask(config.sequence_len, short), persistent=False)
+        self.compute_dtype = torch.float32
+
+    # ------------------------------------------------------------------ init
+    def _precompute_rotary_embeddings(self, seq_len: int, head_dim: int, base: float | None = None):
+        base = self.rc.rope_base if base is None else base
+        freqs = torch.arange(0, head_dim, 2, dtype=torch.float32)
+        inv_freq = 1.0 / (base ** (freqs / head_dim))
+        t = torch.arange(seq_len, dtype=torch.float32)
+        table = torch.outer(t, inv_freq)
+        dt = torch.bfloat16 if self.compute_dtype_hint() == torch.bfloat16 else torch.float32
+        return table.cos().to(dt)[None, :, None, :], table.sin().to(dt)[None, :, None, :]
+
+    def compute_dtype_hint(self) -> torch.dtype:
+        return getattr(self, "compute_dtype", torch.float32)
+
+    def set_compute_dtype(self, dtype: torch.dtype) -> None:
+        """bf16 on the GPU (the rotary tables follow), fp32 on the CPU oracle path."""
+        self.compute_dtype = dtype
+        cos, sin = self._precompute_rotary_embeddings(self.config.sequence_len, self.config.head_dim)
+        self.cos = cos.to(self.cos.device)
+        self.sin = sin.to(self.sin.device)
+
+    @torch.no_grad()
+    def init_weights(self) -> None:
+        """Same distributions and RNG draw order as train.py:2957-3085 for the modules
+        that exist (wte N(0, 0.8), lm_head N(0, 0.001), q/k/v U(+-s), attn c_proj
+        U(+-0.1 s), c_fc U(+-0.4 s), mlp c_proj 0, lambdas 1 / 0.05, gates 0)."""
+        rc = self.rc
+        torch.nn.init.normal_(self.transformer.wte.weight, mean=0.0, std=rc.wte_init_std)
+        torch.nn.init.normal_(self.lm_head.weight, mean=0.0, std=0.001)
+        s = rc.init_scale * math.sqrt(3.0) * self.config.n_embd ** -0.5
+        for block in self.transformer.h:
+            torch.nn.init.uniform_(block.attn.c_q.weight, -s, s)
+            torch.nn.init.uniform_(block.attn.c_k.weight, -s, s)
+            torch.nn.init.uniform_(block.attn.c_v.weight, -s, s)
+            if rc.attn_cproj_init_scale > 0.0:
+                b = rc.attn_cproj_init_scale * s
+                torch.nn.init.uniform_(block.attn.c_proj.weight, -b, b)
+            else:
+                torch.nn.init.zeros_(block.attn.c_proj.weight)
+            torch.nn.init.uniform_(block.mlp.c_fc.weight, -0.4 * s, 0.4 * s)
+            if block.mlp.c_gate is not None:
+                torch.nn.init.uniform_(block.mlp.c_gate.weight, -0.4 * s, 0.4 * s)
+            torch.nn.init.zeros_(block.mlp.c_proj.weight)
+            block.resid_lambda.fill_(1.0)
+            block.x0_lambda.fill_(0.05)
+            for g in (block.attn.ve_gate, block.attn.ve_gate_bi, block.attn.ve_gate_tri):
+                if g is not None:
+                    torch.nn.init.zeros_(g.weight)
+        for ve in self.value_embeds.values():
+            torch.nn.init.uniform_(ve.weight, -s, s)
+        for tbl in self.ngram_embeds.values():
+            torch.nn.init.zeros_(tbl.weight)
+        for proj in self.ngram_proj.values():
+            torch.nn.init.uniform_(proj.weight, -s, s)
+        if self.out_bigram is not None:
+            torch.nn.init.zeros_(self.out_bigram.weight)
+            torch.nn.init.zeros_(self.out_bigram_gate.weight)
+        if self.out_pool_lambdas is not None:
+            torch.nn.init.zeros_(self.out_pool_lambdas)
+        for block in self.transformer.h:
+            if block.attn.head_gate is not None:
+                torch.nn.init.zeros_(block.attn.head_gate.weight)
+        cos, sin = self._precompute_rotary_embeddings(self.config.sequence_len, self.config.head_dim)
+        self.cos = cos.to(self.cos.device)
+        self.sin = sin.to(self.sin.device)
+
+    # ------------------------------------------------------------------ helpers
+    def get_device(self) -> torch.device:
+        return self.transformer.wte.weight.device
+
+    def estimate_flops(self) -> int:
+        """6 * (matmul params) + 12 * L * H * D * T per token (train.py:3191-3214)."""
+        nparams = sum(p.numel() for p in self.parameters())
+        non_matmul = self.transformer.wte.weight.numel() + 2 * self.config.n_layer
+        non_matmul += sum(p.numel() for p in self.ngram_embeds.parameters())
+        if self.out_bigram is not None:
+            non_matmul += self.out_bigram.weight.numel()
+        h, d, t = self.config.n_head, self.config.head_dim, self.config.sequence_len
+        return 6 * (nparams - non_matmul) + self.config.n_layer * 12 * h * d * t
+
+    def _ngram_hash_indices(self, idx: torch.Tensor) -> dict[str, torch.Tensor]:
+        """Causal hashed n-gram ids: bigram (prev, cur), trigram (prev2, prev, cur);
+        missing history = pad id one past the padded vocab (train.py:3087-3140)."""
+        out = {}
+        pad = self.ngram_pad_id
+        cur = idx.long()
+        prev = F.pad(cur[:, :-1], (1, 0), value=pad)
+        prev2 = F.pad(cur[:, :-2], (2, 0), value=pad)
+        for key in self.ngram_embeds:
+            layer = int(key[1:])
+            p1, p2, p3 = _ngram_primes(layer)
+            if key[0] == "b":
+                hsh = (prev * p1) ^ (cur * p2)
+            else:
+                hsh = (prev2 * p1) ^ (prev * p2) ^ (cur * p3)
+            out[key] = (hsh % self.ngram_mod)
+        return out
+
+    def _ngram_lookup(self, key: str, ids: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+        rows = self.ngram_embeds[key].weight[ids].to(dtype)
+        if key in self.ngram_proj:
+            rows = ops.linear(rows, self.ngram_proj[key].weight)
+        return rows
+
+    # ------------------------------------------------------------------ forward
+    def hidden(self, idx: torch.Tensor) -> torch.Tensor:
+        """Final normed hidden states [B, T, C] (compute dtype)."""
+        _b, t = idx.shape
+        assert t <= self.config.sequence_len
+        dt = self.compute_dtype
+        cos, sin = self.cos[:, :t], self.sin[:, :t]
+        x = ops.embed_norm(idx, self.transformer.wte.weight, dt)
+        x0 = x
+        doc_mask = doc_boundary_mask(idx) if self.rc.doc_mask else None
+        ngram_idx = self._ngram_hash_indices(idx) if len(self.ngram_embeds) else None
+        pool_from = self.config.n_layer - self.out_pool_lambdas.numel() if self.out_pool_lambdas is not None else 1 << 30
+        pool_buf = []
+        for i, block in enumerate(self.transformer.h):
+            ve = self.value_embeds[str(i)](idx.long()).to(dt) if str(i) in self.value_embeds else None
+            ve_bi = ve_tri = None
+            if ngram_idx is not None:
+                if f"b{i}" in self.ngram_embeds:
+                    ve_bi = self._ngram_lookup(f"b{i}", ngram_idx[f"b{i}"], dt)
+                if f"t{i}" in self.ngram_embeds:
+                    ve_tri = self._ngram_lookup(f"t{i}", ngram_idx[f"t{i}"], dt)
+            if doc_mask is None and not self.layer_is_short[i]:
+                attn_mask = None
+            else:
+                static = self.mask_short[:t, :t] if self.layer_is_short[i] else torch.zeros(t, t, device=idx.device)
+                attn_mask = static.to(idx.device) + (doc_mask if doc_mask is not None else 0)
+            x = block(x, x0, ve, cos, sin, attn_mask, ve_bi, ve_tri)
+            if i >= pool_from:
+                pool_buf.append(x)
+        if self.out_pool_lambdas is not None:
+            for k, h in enumerate(pool_buf):
+                x = x + self.out_pool_lambdas[k].to(x.dtype) * h
+        return ops.norm(x)
+
+    def forward(self, idx: torch.Tensor, targets: torch.Tensor | None = None, loss_reduction: str = "mean",
+                row_weight: torch.Tensor | None = None):
+        x = self.hidden(idx)
+        V = self.config.vocab_size
+        S = self.rc.logit_softcap
+        if self.out_bigram is not None:
+            logits = F.linear(x, self.lm_head.weight.to(x.dtype))[..., :V].float()
+            g = torch.sigmoid(ops.linear(x, self.out_bigram_gate.weight) + self.out_bigram_gate_bias.to(x.dtype))
+            row = self.out_bigram.weight[idx.long()][..., :V]
+            logits = logits + (g * row.to(g.dtype)).float()
+            if targets is None:
+                return S * torch.tanh(logits / S)
+            return ops.ref.softcap_cross_entropy(logits, targets, S, loss_reduction,
+                                                 None if row_weight is None else row_weight.reshape(-1))
+        if targets is None:
+            return ops.softcap_logits(x, self.lm_head.weight, S, V)
+        return ops.lm_head_softcap_ce(x, self.lm_head.weight, targets, S, V, loss_reduction, row_weight)
+
+    def model_config_dict(self) -> dict:
+        return asdict(self.config)

@@ -1,0 +1,402 @@
+"""Autograd wrappers of the sm_100a kernels (CUDA path of every op in ``ops``).
+
+Weight gradients never go through autograd's AccumulateGrad: each linear's backward
+accumulates ``dW`` straight into the fp32 ``param.grad`` buffer from the GEMM epilogue
+(``linear_dw`` with beta = 1), and returns ``None`` for the parameter.  The bf16 copy
+of each fp32 master weight that the GEMMs read is cached on the parameter and
+re-cast only when the parameter's version counter moved (the optimizer's apply
+kernel writes the cache directly, so in training it is never re-cast here).
+
+The gradient of x0 (the normed embedding, an input of every block's residual mix) is
+accumulated in fp32 across layers through a side buffer owned by the embedding node,
+so 20+ bf16 partial sums are never rounded on the way.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+from torch.autograd import Function
+
+from . import gemm
+from ._ext import C
+
+BF16 = torch.bfloat16
+
+
+# --------------------------------------------------------------------------- helpers
+def w16(p: torch.Tensor) -> torch.Tensor:
+    """bf16 view of a (fp32) weight, cached on the parameter object."""
+    if p.dtype == BF16:
+        return p.detach()
+    cached = getattr(p, "_tfb_w16", None)
+    if cached is not None and getattr(p, "_tfb_w16_ver", -1) == p._version:
+        return cached
+    if cached is not None and cached.shape == p.shape:
+        cached.copy_(p.detach())
+    else:
+        cached = p.detach().to(BF16)
+        p._tfb_w16 = cached
+    p._tfb_w16_ver = p._version
+    return cached
+
+
+def set_w16(p: torch.Tensor, buf: torch.Tensor) -> None:
+    """Install an externally managed bf16 cache (e.g. a view of a fused buffer)."""
+    p._tfb_w16 = buf
+    p._tfb_w16_ver = -1
+
+
+def mark_w16_fresh(p: torch.Tensor) -> None:
+    p._tfb_w16_ver = p._version
+
+
+def grad_buf(p: torch.Tensor) -> torch.Tensor:
+    """The fp32 gradient accumulator of a parameter (created zeroed on first use)."""
+    if p.grad is None:
+        p.grad = torch.zeros_like(p, dtype=torch.float32, memory_format=torch.contiguous_format)
+    return p.grad
+
+
+def fused_group(ws: list[torch.Tensor]):
+    """(bf16 [sum N, K], fp32 grad [sum N, K]) views covering the weights ``ws`` if an
+    engine laid their caches and gradients out back to back, else None."""
+    lead = ws[0]
+    fg = getattr(lead, "_tfb_fused", None)
+    if fg is None or fg[2] != tuple(id(w) for w in ws):
+        return None
+    buf16, gview, _ = fg
+    if any(getattr(w, "_tfb_w16_ver", -1) != w._version for w in ws):
+        for w, part in zip(ws, buf16.split([w.shape[0] for w in ws], 0)):
+            part.copy_(w.detach())
+            w._tfb_w16_ver = w._version
+    return buf16, gview
+
+
+def _2d(t):
+    return t.reshape(-1, t.shape[-1])
+
+
+# --------------------------------------------------------------------------- norms
+class RMSNormFn(Function):
+    @staticmethod
+    def forward(ctx, x):
+        x2 = _2d(x.contiguous())
+        y = torch.empty_like(x2)
+        rstd = torch.empty(x2.shape[0], dtype=torch.float32, device=x.device)
+        C().rmsnorm_fwd(x2, y, rstd)
+        ctx.save_for_backward(x2, rstd)
+        ctx.shape = x.shape
+        return y.view(x.shape)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, rstd = ctx.saved_tensors
+        dx = torch.empty_like(x2)
+        C().rmsnorm_bwd(_2d(dy.contiguous()), x2, rstd, None, dx)
+        return dx.view(ctx.shape)
+
+
+class _X0Acc:
+    __slots__ = ("buf", "started")
+
+    def __init__(self):
+        self.buf = None
+        self.started = False
+
+
+class EmbedNormFn(Function):
+    @staticmethod
+    def forward(ctx, idx, wte):
+        B, T = idx.shape
+        Cd = wte.shape[1]
+        idx32 = idx if idx.dtype == torch.int32 else idx.to(torch.int32)
+        out = torch.empty((B, T, Cd), dtype=BF16, device=wte.device)
+        rstd = torch.empty(B * T, dtype=torch.float32, device=wte.device)
+        C().embed_norm_fwd(idx32, wte.detach(), out, rstd)
+        holder = _X0Acc()
+        ctx.holder = holder
+        ctx.wte = wte
+        ctx.save_for_backward(idx32, rstd)
+        out._tfb_x0acc = holder
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        idx32, rstd = ctx.saved_tensors
+        holder = ctx.holder
+        wte = ctx.wte
+        gacc = holder.buf if holder.started else None
+        gb = _2d(dout.contiguous()) if dout is not None else None
+        if gacc is None and gb is None:
+            return None, None
+        C().embed_norm_bwd(idx32, wte.detach(), rstd, gacc, gb, grad_buf(wte))
+        holder.buf = None
+        return None, None
+
+
+class MixNormFn(Function):
+    """xm = l_r * x + l_0 * x0 (bf16), h = norm(xm); returns (xm, h)."""
+
+    @staticmethod
+    def forward(ctx, x, x0, lam_r, lam_0):
+        holder = getattr(x0, "_tfb_x0acc", None)
+        x = x.contiguous()
+        xm = torch.empty_like(x)
+        h = torch.empty_like(x)
+        M = x.numel() // x.shape[-1]
+        rstd = torch.empty(M, dtype=torch.float32, device=x.device)
+        C().mix_norm_fwd(x, x0, lam_r.detach(), lam_0.detach(), xm, h, rstd)
+        ctx.holder = holder
+        ctx.save_for_backward(x, x0, xm, rstd, lam_r, lam_0)
+        return xm, h
+
+    @staticmethod
+    def backward(ctx, dxm, dh):
+        x, x0, xm, rstd, lam_r, lam_0 = ctx.saved_tensors
+        if dxm is None:
+            dxm = torch.zeros_like(xm)
+        if dh is None:
+            dh = torch.zeros_like(xm)
+        holder = ctx.holder
+        own = holder is None
+        if own:
+            holder = _X0Acc()
+        if holder.buf is None:
+            holder.buf = torch.empty(x.shape, dtype=torch.float32, device=x.device)
+            holder.started = False
+        dx = torch.empty_like(x)
+        dlr = torch.zeros(1, dtype=torch.float32, device=x.device)
+        dl0 = torch.zeros(1, dtype=torch.float32, device=x.device)
+        C().mix_norm_bwd(dxm.contiguous(), dh.contiguous(), x, x0, xm, rstd, lam_r.detach(), lam_0.detach(), dx,
+                         holder.buf, not holder.started, dlr, dl0)
+        holder.started = True
+        dx0 = holder.buf.to(BF16) if own else None
+        return dx, dx0, dlr.view_as(lam_r), dl0.view_as(lam_0)
+
+
+# --------------------------------------------------------------------------- linears
+class LinearFn(Function):
+    """y = x W^T (+ residual).  W's gradient goes straight into W.grad (fp32)."""
+
+    @staticmethod
+    def forward(ctx, x, w, residual):
+        x2 = gemm._c2(x)
+        wb = w16(w)
+        y = gemm.linear_fwd(x2, wb, residual=residual)
+        ctx.save_for_backward(x2)
+        ctx.w = w
+        ctx.has_res = residual is not None
+        ctx.shape = x.shape
+        return y.view(*x.shape[:-1], wb.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        (x2,) = ctx.saved_tensors
+        w = ctx.w
+        wb = w16(w)
+        dy2 = gemm._c2(dy)
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx = gemm.linear_dx(dy2, wb).view(ctx.shape)
+        if w.requires_grad:
+            gemm.linear_dw(dy2, x2, grad_buf(w))
+        return dx, None, (dy if ctx.has_res else None)
+
+
+class LinearMultiFn(Function):
+    """[y_1 | y_2 | ...] = x [W_1; W_2; ...]^T as one GEMM (fused QKV)."""
+
+    @staticmethod
+    def forward(ctx, x, *ws):
+        x2 = gemm._c2(x)
+        fg = fused_group(list(ws))
+        if fg is not None:
+            wb = fg[0]
+        else:
+            wb = torch.cat([w16(w) for w in ws], 0)
+        y = gemm.linear_fwd(x2, wb)
+        ctx.save_for_backward(x2)
+        ctx.ws = ws
+        ctx.shape = x.shape
+        return y.view(*x.shape[:-1], wb.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        (x2,) = ctx.saved_tensors
+        ws = list(ctx.ws)
+        fg = fused_group(ws)
+        dy2 = gemm._c2(dy)
+        if fg is not None:
+            wb, gview = fg
+            dx = gemm.linear_dx(dy2, wb).view(ctx.shape) if ctx.needs_input_grad[0] else None
+            for w in ws:
+                grad_buf(w)
+            gemm.linear_dw(dy2, x2, gview)
+        else:
+            wb = torch.cat([w16(w) for w in ws], 0)
+            dx = gemm.linear_dx(dy2, wb).view(ctx.shape) if ctx.needs_input_grad[0] else None
+            g = torch.zeros(wb.shape, dtype=torch.float32, device=dy.device)
+            gemm.linear_dw(dy2, x2, g, accumulate=False)
+            for w, part in zip(ws, g.split([w.shape[0] for w in ws], 0)):
+                if w.requires_grad:
+                    grad_buf(w).add_(part)
+        return (dx,) + (None,) * len(ws)
+
+
+class MLPRelu2Fn(Function):
+    """residual + relu(x W_fc^T - tau)^2 W_proj^T, h kept for the backward."""
+
+    @staticmethod
+    def forward(ctx, x, w_fc, w_proj, residual, tau):
+        x2 = gemm._c2(x)
+        act, h = gemm.linear_relu2_fwd(x2, w16(w_fc), tau=tau)
+        y = gemm.linear_fwd(act, w16(w_proj), residual=residual)
+        ctx.save_for_backward(x2, act, h)
+        ctx.w_fc, ctx.w_proj, ctx.tau = w_fc, w_proj, tau
+        ctx.has_res = residual is not None
+        ctx.shape = x.shape
+        return y.view(*x.shape[:-1], y.shape[-1])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, act, h = ctx.saved_tensors
+        dy2 = gemm._c2(dy)
+        wp, wf = w16(ctx.w_proj), w16(ctx.w_fc)
+        # dh = (dy W_proj) * 2 relu(h - tau)   (relu^2 backward fused in the epilogue)
+        dh = gemm.linear_dx(dy2, wp, relu2_h=h, tau=ctx.tau)
+        if ctx.w_proj.requires_grad:
+            gemm.linear_dw(dy2, act, grad_buf(ctx.w_proj))
+        dx = gemm.linear_dx(dh, wf).view(ctx.shape) if ctx.needs_input_grad[0] else None
+        if ctx.w_fc.requires_grad:
+            gemm.linear_dw(dh, x2, grad_buf(ctx.w_fc))
+        return dx, None, None, (dy if ctx.has_res else None), None
+
+
+# --------------------------------------------------------------------------- RoPE + QK norm
+class RopeNormFn(Function):
+    """norm(rope(x)) for x [B, T, H, D] (out of place)."""
+
+    @staticmethod
+    def forward(ctx, x, cos, sin, pos_offset=0):
+        B, T, H, D = x.shape
+        xc = x.contiguous()
+        out = torch.empty_like(xc)
+        rstd = torch.empty(B * T * H, dtype=torch.float32, device=x.device)
+        C().rope_norm_fwd(xc.view(B * T, H * D), 0, H, D, cos, sin, T, pos_offset, rstd, out.view(B * T, H * D))
+        ctx.save_for_backward(out, rstd, cos, sin)
+        ctx.dims = (B, T, H, D)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        out, rstd, cos, sin = ctx.saved_tensors
+        B, T, H, D = ctx.dims
+        gx = g.contiguous().clone()
+        C().rope_norm_bwd(gx.view(B * T, H * D), out.view(B * T, H * D), 0, H, D, cos, sin, T, rstd)
+        return gx, None, None, None
+
+
+def _flash_fwd(q, k, v, causal, scale):
+    out = torch.ops.aten._scaled_dot_product_flash_attention(q, k, v, 0.0, causal, False, scale=scale)
+    return out
+
+
+class AttnQKVFn(Function):
+    """Fused attention core of the plain block: RoPE + QK-norm of q and k from the
+    [M, 3C] projection buffer, causal attention, output [B, T, C]."""
+
+    @staticmethod
+    def forward(ctx, qkv, cos, sin, B, T, H, D, scale):
+        Cd = H * D
+        qkv2 = qkv.view(B * T, 3 * Cd)
+        qkn = torch.empty((B * T, 2 * Cd), dtype=BF16, device=qkv.device)
+        rstd = torch.empty(B * T * 2 * H, dtype=torch.float32, device=qkv.device)
+        C().rope_norm_fwd(qkv2, 0, 2 * H, D, cos, sin, T, 0, rstd, qkn)
+        q = qkn[:, :Cd].view(B, T, H, D).transpose(1, 2)
+        k = qkn[:, Cd:].view(B, T, H, D).transpose(1, 2)
+        v = qkv2[:, 2 * Cd:].view(B, T, H, D).transpose(1, 2)
+        res = _flash_fwd(q, k, v, True, scale)
+        o, lse = res[0], res[1]
+        ctx.save_for_backward(qkv2, qkn, rstd, cos, sin, o, lse, res[6], res[7])
+        ctx.meta = (B, T, H, D, scale, res[2], res[3], res[4], res[5])
+        return o.transpose(1, 2).reshape(B, T, Cd)
+
+    @staticmethod
+    def backward(ctx, dy):
+        qkv2, qkn, rstd, cos, sin, o, lse, seed, offset = ctx.saved_tensors
+        B, T, H, D, scale, cq, ck, mq, mk = ctx.meta
+        Cd = H * D
+        q = qkn[:, :Cd].view(B, T, H, D).transpose(1, 2)
+        k = qkn[:, Cd:].view(B, T, H, D).transpose(1, 2)
+        v = qkv2[:, 2 * Cd:].view(B, T, H, D).transpose(1, 2)
+        do = dy.view(B, T, H, D).transpose(1, 2)
+        dq, dk, dv = torch.ops.aten._scaled_dot_product_flash_attention_backward(
+            do, q, k, v, o, lse, cq, ck, mq, mk, 0.0, True, seed, offset, scale=scale)
+        dqkv = torch.empty((B * T, 3 * Cd), dtype=BF16, device=dy.device)
+        dqkv.view(B, T, 3, H, D)[:, :, 0].copy_(dq.transpose(1, 2))
+        dqkv.view(B, T, 3, H, D)[:, :, 1].copy_(dk.transpose(1, 2))
+        dqkv.view(B, T, 3, H, D)[:, :, 2].copy_(dv.transpose(1, 2))
+        C().rope_norm_bwd(dqkv, qkn, 0, 2 * H, D, cos, sin, T, rstd)
+        return dqkv.view(B, T, 3 * Cd), None, None, None, None, None, None, None
+
+
+# --------------------------------------------------------------------------- lm_head + CE
+class LMHeadSoftcapCEFn(Function):
+    """loss = CE(S tanh(x W^T / S)[:, :V], targets), forward and dlogits in one pass.
+
+    ``row_weight`` (fp32 per token, or None) gives the byte-weighted mean; targets < 0
+    are ignored.  dlogits are stored (bf16) in place of the logits; the upstream
+    gradient scalar is applied on the device inside the two backward GEMMs."""
+
+    @staticmethod
+    def forward(ctx, x, w, targets, softcap, vocab, row_weight, reduction):
+        x2 = gemm._c2(x)
+        wb = w16(w)
+        M = x2.shape[0]
+        logits = gemm.linear_fwd(x2, wb)
+        loss_rows = torch.empty(M, dtype=torch.float32, device=x.device)
+        tg = targets if targets.dim() == 2 else targets.view(1, -1)
+        T = tg.shape[1]
+        if tg.stride(1) != 1:
+            tg = tg.contiguous()
+        C().softcap_ce(logits, tg, T, row_weight, vocab, float(softcap), 1.0, loss_rows, True)
+        if row_weight is not None:
+            denom = (row_weight * (tg.reshape(-1) >= 0)).sum()
+        else:
+            denom = (tg >= 0).sum().to(torch.float32)
+        inv = 1.0 / denom.clamp_min(1.0)
+        loss = loss_rows.sum() * inv
+        ctx.save_for_backward(x2, logits, inv)
+        ctx.w = w
+        ctx.shape = x.shape
+        return loss
+
+    @staticmethod
+    def backward(ctx, g):
+        x2, dz, inv = ctx.saved_tensors
+        w = ctx.w
+        alpha_t = (g.float() * inv).reshape(1).contiguous()
+        wb = w16(w)
+        dx = gemm.linear_dx(dz, wb, alpha_t=alpha_t).view(ctx.shape)
+        if w.requires_grad:
+            gemm.linear_dw(dz, x2, grad_buf(w), alpha_t=alpha_t)
+        return dx, None, None, None, None, None, None
+
+
+def softcap_logits(x, w, softcap: float, vocab: int) -> torch.Tensor:
+    """Inference/eval logits: S tanh(z / S) of the bf16 lm_head product, fp32 [.., V]."""
+    x2 = gemm._c2(x)
+    z = gemm.linear_fwd(x2, w16(w))[:, :vocab].float()
+    z = softcap * torch.tanh(z / softcap)
+    return z.view(*x.shape[:-1], vocab)
+
+
+def softcap_ce_rows(x, w, targets, softcap: float, vocab: int) -> torch.Tensor:
+    """Per-token softcapped CE (no gradient), 0 where target < 0."""
+    x2 = gemm._c2(x)
+    logits = gemm.linear_fwd(x2, w16(w))
+    loss_rows = torch.empty(x2.shape[0], dtype=torch.float32, device=x.device)
+    tg = targets if targets.dim() == 2 else targets.view(1, -1)
+    C().softcap_ce(logits, tg.contiguous(), tg.shape[1], None, vocab, float(softcap), 1.0, loss_rows, False)
+    return loss_rows.view(targets.shape)

@@ -1,0 +1,14 @@
+"""Python front-end of the optimizer kernels (``csrc/kernels/optim_kernels.cu``)."""
+from __future__ import annotations
+
+import torch
+
+from ._ext import C
+
+
+def adamw_multi(params, grads, exp_avgs, exp_avg_sqs, lr: torch.Tensor, beta1: float, beta2: float,
+                eps: float, wd: float, bias1, bias2, cautious: bool = False) -> None:
+    """One multi-tensor launch for a whole AdamW group (fp32 params / grads / moments)."""
+    grads = [g if g.dtype == torch.float32 and g.is_contiguous() else g.float().contiguous() for g in grads]
+    C().adamw_multi([p.data for p in params], grads, exp_avgs, exp_avg_sqs, lr, float(beta1), float(beta2),
+                    float(eps), float(wd), [float(b) for b in bias1], [float(b) for b in bias2], bool(cautious))

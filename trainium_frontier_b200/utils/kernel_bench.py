@@ -1,0 +1,117 @@
+"""Kernel micro-benchmarks: CUDA-event timing of the hot kernels against the roofline.
+
+Usage: ``python -m trainium_frontier_b200.utils.kernel_bench [gemm|all] [--json PATH]``
+
+Each case: 3+ warm-up launches, then timed launches with an L2 flush (a write of a
+buffer larger than the 126 MB L2) between them, CUDA events on the launching stream
+with a synchronize on both sides.  Reports achieved TFLOP/s or GB/s and the fraction
+of the measured peaks in MEASURED_PEAKS.json (the torch cuBLAS GEMM is timed the same
+way alongside as a reference point).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def measured_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class Timer:
+    def __init__(self, device):
+        self.device = device
+        self.flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+
+    def time(self, fn, iters: int = 10, warmup: int = 3, flush: bool = True) -> float:
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize(self.device)
+        total = 0.0
+        for _ in range(iters):
+            if flush:
+                self.flush.fill_(1.0)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize(self.device)
+            total += s.elapsed_time(e)
+        return total / iters
+
+
+def bench_gemm(dev, peaks, shapes=None):
+    from ..ops import gemm
+    t = Timer(dev)
+    rows = []
+    shapes = shapes or [
+        ("d20 qkv fwd", "fwd", 65536, 3840, 1280),
+        ("d20 proj fwd", "fwd", 65536, 1280, 1280),
+        ("d20 fc fwd relu2", "relu2", 65536, 5120, 1280),
+        ("d20 mlp proj fwd", "fwd", 65536, 1280, 5120),
+        ("d20 lm_head fwd", "fwd", 65536, 8192, 1280),
+        ("d20 fc dx", "dx", 65536, 5120, 1280),
+        ("d20 fc dW", "dw", 65536, 5120, 1280),
+        ("d20 qkv dW", "dw", 65536, 3840, 1280),
+        ("square 8192", "fwd", 8192, 8192, 8192),
+    ]
+    for name, kind, M, N, K in shapes:
+        x = torch.randn(M, K, device=dev, dtype=torch.bfloat16)
+        w = torch.randn(N, K, device=dev, dtype=torch.bfloat16)
+        dy = torch.randn(M, N, device=dev, dtype=torch.bfloat16)
+        g = torch.zeros(N, K, device=dev, dtype=torch.float32)
+        if kind == "fwd":
+            ours = lambda: gemm.linear_fwd(x, w)
+            ref = lambda: torch.matmul(x, w.t())
+        elif kind == "relu2":
+            ours = lambda: gemm.linear_relu2_fwd(x, w)
+            ref = lambda: torch.relu(torch.matmul(x, w.t())).square()
+        elif kind == "dx":
+            ours = lambda: gemm.linear_dx(dy, w)
+            ref = lambda: torch.matmul(dy, w)
+        else:
+            ours = lambda: gemm.linear_dw(dy, x, g)
+            ref = lambda: g.add_(torch.matmul(dy.t(), x).float())
+        flops = 2.0 * M * N * K
+        t_ours = t.time(ours)
+        t_ref = t.time(ref)
+        rows.append(dict(name=name, M=M, N=N, K=K, ms=t_ours, tflops=flops / t_ours / 1e9,
+                         frac_of_measured=flops / t_ours / 1e9 / peaks["bf16_tflops"],
+                         torch_ms=t_ref, torch_tflops=flops / t_ref / 1e9))
+        del x, w, dy, g
+    return rows
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("what", nargs="?", default="gemm")
+    ap.add_argument("--json", default="")
+    args = ap.parse_args()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peaks = measured_peaks()
+    out = {"peaks": peaks}
+    if args.what in ("gemm", "all"):
+        out["gemm"] = bench_gemm(dev, peaks)
+        for r in out["gemm"]:
+            print(f"{r['name']:>20s}  {r['ms']:8.3f} ms  {r['tflops']:7.1f} TF/s ({r['frac_of_measured']:.2f} of "
+                  f"{peaks['source']})   torch {r['torch_ms']:8.3f} ms {r['torch_tflops']:7.1f} TF/s")
+    from ..ops._ext import check_errors
+    check_errors(dev)
+    if args.json:
+        with open(args.json, "w") as f:
+            json.dump(out, f, indent=1)
+
+
+if __name__ == "__main__":
+    main()
