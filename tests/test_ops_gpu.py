@@ -204,9 +204,10 @@ def test_newton_schulz(cuda_device):
         y = newton_schulz_gpu(x.to(BF), 5)
         yr = newton_schulz_reference(x.double(), 5)
         assert rel(y, yr) < 5e-2, shape
-        # orthogonality: singular values near 1
+        # same spectrum as the fp64 reference iteration (Polar Express is not exactly orthogonal)
         s = torch.linalg.svdvals(y.float())
-        assert s.max().item() < 1.3 and s.min().item() > 0.5
+        sr = torch.linalg.svdvals(yr.float())
+        assert (s - sr).abs().max().item() < 5e-2
 
 
 def test_model_cpu_vs_gpu(cuda_device):
@@ -234,9 +235,12 @@ def test_model_cpu_vs_gpu(cuda_device):
     lg.backward()
     assert abs(lc.item() - lg.item()) < 2e-2 * lc.item()
     pc = dict(cpu.named_parameters())
+    errs = {}
     for n, p in gpu.named_parameters():
         if pc[n].grad is None:
             continue
         assert p.grad is not None, n
-        r = rel(p.grad.cpu(), pc[n].grad)
-        assert r < 0.1, (n, r)
+        a, b = p.grad.cpu().float(), pc[n].grad.float()
+        errs[n] = ((a - b).norm() / (b.norm() + 1e-12)).item()
+    worst = sorted(errs.items(), key=lambda kv: -kv[1])[:5]
+    assert worst[0][1] < 0.05, worst

@@ -1,0 +1,81 @@
+"""One profiled optimizer step of a GPT config, for launch lists and kernel captures.
+
+    python -m trainium_frontier_b200.utils.profile_step --preset d20 --rows 16 [--accum 1]
+
+Runs ``--warmup`` steps, then brackets exactly one step with cudaProfilerStart/Stop
+(so ``ncu --profile-from-start off`` sees only that step) and NVTX ranges per phase.
+Without a profiler attached it prints the per-phase CUDA-event times of that step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--preset", default="d20")
+    ap.add_argument("--rows", type=int, default=16)
+    ap.add_argument("--accum", type=int, default=1)
+    ap.add_argument("--warmup", type=int, default=2)
+    ap.add_argument("--json", default="")
+    args = ap.parse_args()
+    from ..config import preset
+    from ..optim.schedules import apply_schedules
+    from ..train import Trainer
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg0 = preset(args.preset)
+    cfg = preset(args.preset, device_batch_size=args.rows, pack_factor=1, progress_mode="steps",
+                 num_steps=10 ** 6, total_batch_size=args.rows * cfg0.seq_len * args.accum)
+    tr = Trainer(cfg, dev)
+    batches = []
+    for _ in range(tr.grad_accum):
+        r = tr.loader.next().clone()
+        batches.append((r[:, :-1], r[:, 1:]))
+    ev = {k: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for k in ("fwd_bwd", "sync_clip", "optimizer")}
+
+    def step(profiled: bool):
+        e = ev
+        if profiled:
+            torch.cuda.nvtx.range_push("fwd_bwd")
+        e["fwd_bwd"][0].record()
+        tr.engine.forward_backward(batches)
+        e["fwd_bwd"][1].record()
+        if profiled:
+            torch.cuda.nvtx.range_pop()
+            torch.cuda.nvtx.range_push("sync_clip")
+        e["sync_clip"][0].record()
+        tr.engine.sync_and_clip()
+        e["sync_clip"][1].record()
+        if profiled:
+            torch.cuda.nvtx.range_pop()
+            torch.cuda.nvtx.range_push("optimizer")
+        apply_schedules(cfg, tr.opt, tr.step_idx, 0.0)
+        e["optimizer"][0].record()
+        tr.engine.optimizer_step()
+        e["optimizer"][1].record()
+        if profiled:
+            torch.cuda.nvtx.range_pop()
+        tr.step_idx += 1
+
+    for _ in range(args.warmup):
+        step(False)
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStart()
+    step(True)
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
+    out = {k: a.elapsed_time(b) for k, (a, b) in ev.items()}
+    out["tokens"] = tr.tokens_per_step
+    print(json.dumps(out))
+    if args.json:
+        with open(args.json, "w") as f:
+            json.dump(out, f)
+
+
+if __name__ == "__main__":
+    main()
