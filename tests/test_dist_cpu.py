@@ -1,0 +1,170 @@
+"""Multi-rank behaviour on CPU (gloo, world_size 2): gradient sync equivalence, loss
+parity with the reference at ws=2, and failure detection without any GPU fault
+(a rank that raises / leaves, a rank that reports a bad loss)."""
+import json
+import os
+import socket
+import sys
+import time
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+TESTS = os.path.join(ROOT, "tests")
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _init(rank, world, port, timeout_s=60):
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
+
+
+def _worker_sync(rank, world, port, out_dir):
+    sys.path.insert(0, ROOT)
+    torch.set_num_threads(2)
+    _init(rank, world, port)
+    from trainium_frontier_b200.config import preset
+    from trainium_frontier_b200.engine import TrainEngine
+    from trainium_frontier_b200.models.gpt import GPT
+    from trainium_frontier_b200.optim.muon_adamw import setup_optimizer
+    res = {}
+    for mode in ("per_param", "bucket"):
+        cfg = preset("tiny", grad_sync=mode, clip_order="global", grad_clip=0.0, bucket_layers=2)
+        torch.manual_seed(0)
+        m = GPT(cfg.model_config(), cfg)
+        m.init_weights()
+        opt = setup_optimizer(m, cfg, torch.float32)
+        eng = TrainEngine(m, opt, cfg, torch.device("cpu"), 1, mode)
+        g = torch.Generator().manual_seed(100 + rank)
+        x = torch.randint(1, 8192, (4, 257), generator=g)
+        eng.forward_backward([(x[:, :-1], x[:, 1:])])
+        eng.sync_and_clip()
+        res[mode] = eng.layout.grad.clone()
+    torch.save(res, os.path.join(out_dir, f"sync_{rank}.pt"))
+    dist.destroy_process_group()
+
+
+def test_bucket_sync_equals_per_param(tmp_path):
+    port = _port()
+    mp.spawn(_worker_sync, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    r0 = torch.load(tmp_path / "sync_0.pt")
+    r1 = torch.load(tmp_path / "sync_1.pt")
+    assert torch.allclose(r0["per_param"], r0["bucket"], atol=1e-7, rtol=1e-6)
+    assert torch.equal(r0["bucket"], r1["bucket"])  # identical on both ranks after the average
+
+
+def _worker_parity(rank, world, port, out_dir, n_steps):
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, TESTS)
+    torch.set_num_threads(2)
+    _init(rank, world, port)
+    from _refutil import build_reference_tiny, import_reference
+    from trainium_frontier_b200.config import preset
+    from trainium_frontier_b200.engine import TrainEngine
+    from trainium_frontier_b200.models.gpt import GPT
+    from trainium_frontier_b200.optim.muon_adamw import setup_optimizer
+    from trainium_frontier_b200.optim.schedules import muon_momentum
+    rtrain = import_reference()
+    ref = build_reference_tiny(rtrain)
+    cfg = preset("tiny", grad_sync="per_param", clip_order="local")
+    ours = GPT(cfg.model_config(), cfg)
+    ours.load_state_dict(ref.state_dict())
+    opt_r = ref.setup_optimizer()
+    opt_o = setup_optimizer(ours, cfg, torch.float32)
+    eng = TrainEngine(ours, opt_o, cfg, torch.device("cpu"), 1, "per_param")
+    g = torch.Generator().manual_seed(7 + rank)
+    hist = []
+    for step in range(n_steps):
+        x = torch.randint(1, 8192, (8, 257), generator=g)
+        xi, yi = x[:, :-1].contiguous(), x[:, 1:].contiguous()
+        opt_r.zero_grad(set_to_none=True)
+        lr_ = ref(xi, yi)
+        lr_.backward()
+        torch.nn.utils.clip_grad_norm_(list(ref.parameters()), rtrain.GRAD_CLIP, foreach=True)
+        rtrain.sync_gradients(ref)
+        prog = step / n_steps
+        for grp in opt_r.param_groups:
+            grp["lr"] = grp["initial_lr"]
+            if grp["kind"] == "muon":
+                grp["momentum"] = rtrain.muon_momentum(step, prog)
+                grp["weight_decay"] = rtrain.WEIGHT_DECAY * (1.0 - prog)
+        opt_r.step()
+        lo = eng.forward_backward([(xi, yi)])
+        eng.sync_and_clip()
+        for grp in opt_o.param_groups:
+            grp["lr"] = grp["initial_lr"]
+            if grp["kind"] == "muon":
+                grp["momentum"] = muon_momentum(cfg, step, prog)
+                grp["weight_decay"] = cfg.weight_decay * (1.0 - prog)
+        eng.optimizer_step()
+        hist.append((lr_.item(), lo.item()))
+    with open(os.path.join(out_dir, f"parity_{rank}.json"), "w") as f:
+        json.dump(hist, f)
+    dist.destroy_process_group()
+
+
+def test_loss_parity_with_reference_ws2(tmp_path):
+    port = _port()
+    mp.spawn(_worker_parity, args=(2, port, str(tmp_path), 10), nprocs=2, join=True)
+    for r in (0, 1):
+        hist = json.load(open(tmp_path / f"parity_{r}.json"))
+        for i, (a, b) in enumerate(hist):
+            assert abs(a - b) <= 2e-3 * abs(a), (r, i, a, b)
+
+
+def _worker_fail(rank, world, port, out_dir, mode):
+    sys.path.insert(0, ROOT)
+    _init(rank, world, port, timeout_s=10)
+    t0 = time.time()
+    outcome = "ok"
+    try:
+        if mode == "raise" and rank == 1:
+            raise RuntimeError("injected host-side failure on rank 1")
+        if mode == "badloss":
+            loss = float("nan") if rank == 1 else 3.0
+            control = torch.tensor([1 if (loss != loss or loss > 100) else 0, 0], dtype=torch.int32)
+            dist.all_reduce(control, op=dist.ReduceOp.MAX)
+            if int(control[0]):
+                raise RuntimeError(f"bad loss detected: {loss}")
+        else:
+            t = torch.ones(4)
+            dist.all_reduce(t)
+            dist.all_reduce(t)
+    except Exception as e:  # noqa: BLE001
+        outcome = f"error: {type(e).__name__}: {str(e)[:120]}"
+    with open(os.path.join(out_dir, f"fail_{mode}_{rank}.json"), "w") as f:
+        json.dump({"outcome": outcome, "seconds": time.time() - t0}, f)
+    try:
+        dist.destroy_process_group()
+    except Exception:
+        pass
+
+
+def test_failure_detection_rank_leaves(tmp_path):
+    port = _port()
+    mp.spawn(_worker_fail, args=(2, port, str(tmp_path), "raise"), nprocs=2, join=True)
+    r0 = json.load(open(tmp_path / "fail_raise_0.json"))
+    r1 = json.load(open(tmp_path / "fail_raise_1.json"))
+    assert r1["outcome"].startswith("error")
+    assert r0["outcome"].startswith("error"), r0  # the survivor's collective ends with an error
+    assert r0["seconds"] < 60
+
+
+def test_failure_detection_bad_loss_agreement(tmp_path):
+    port = _port()
+    mp.spawn(_worker_fail, args=(2, port, str(tmp_path), "badloss"), nprocs=2, join=True)
+    for r in (0, 1):
+        out = json.load(open(tmp_path / f"fail_badloss_{r}.json"))
+        assert "bad loss" in out["outcome"], out

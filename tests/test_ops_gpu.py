@@ -235,12 +235,20 @@ def test_model_cpu_vs_gpu(cuda_device):
     lg.backward()
     assert abs(lc.item() - lg.item()) < 2e-2 * lc.item()
     pc = dict(cpu.named_parameters())
-    errs = {}
+    errs, lam = {}, []
     for n, p in gpu.named_parameters():
         if pc[n].grad is None:
             continue
         assert p.grad is not None, n
         a, b = p.grad.cpu().float(), pc[n].grad.float()
+        if n.endswith("_lambda"):
+            lam.append((n, a.item(), b.item()))
+            continue
         errs[n] = ((a - b).norm() / (b.norm() + 1e-12)).item()
     worst = sorted(errs.items(), key=lambda kv: -kv[1])[:5]
     assert worst[0][1] < 0.05, worst
+    # The per-block scalars' gradients are dot products over the whole (bf16) residual
+    # stream with heavy cancellation: compare on the scale of the largest of them.
+    scale = max(abs(b) for _, _, b in lam)
+    for n, a, b in lam:
+        assert abs(a - b) < 0.15 * scale, (n, a, b, scale)

@@ -1,0 +1,739 @@
+// Causal flash attention, forward and backward, on the 5th-generation tensor cores.
+//
+// Layout: q, k, v are row views [B*T, *] with head h at columns [h*D, h*D + D) (the
+// projection buffers are read in place -- no transposes).  T % 128 == 0, D in {64, 128}.
+//
+// Forward: one CTA per (batch*head, 128-query tile), heaviest tiles first.
+//   warp 0   TMA: Q once, K/V tiles double-buffered
+//   warp 1   MMA: S_j = Q K_j^T -> TMEM (double-buffered), O += P_j V_j -> TMEM
+//   warps 2-5 softmax: one query row per thread (= TMEM lane).  Row max / exp2 / sum in
+//            registers, P written to shared memory in the 128B-swizzled K-major layout the
+//            P*V MMA reads; O is rescaled in TMEM (ld/st) only when a warp's max moved.
+//            Epilogue: O / l -> bf16, LSE (natural log) for the backward.
+// Backward: one CTA per (batch*head, 128-key tile), in the transposed frame so every
+//   per-row operation is again one TMEM lane per thread:
+//     S^T = K Q_i^T, dP^T = V dO_i^T                      (TMEM)
+//     P^T = exp(S^T * scale - LSE_i), dS^T = P^T (dP^T - Dvec_i)   (registers -> smem)
+//     dV += P^T dO_i, dK += dS^T Q_i                       (TMEM accumulators)
+//     dQ_i = dS K  -> fp32 vector atomics into a dQ accumulator
+// Every wait is bounded (see sm100_common.cuh); no TMA multicast.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "sm100_common.cuh"
+
+namespace tfb {
+
+CUtensorMap make_tmap_bf16(const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                           uint32_t box_inner, uint32_t box_outer, uint64_t batch, uint64_t batch_stride_elems);
+
+struct FaArgs {
+  int B, T, H, n_tiles, causal;
+  float scale, scale_log2;
+  __nv_bfloat16* O;
+  long long ldo;
+  float* lse;
+  const float* dvec;
+  float* dq_acc;
+  long long lddq;
+  __nv_bfloat16* dK;
+  long long lddk;
+  __nv_bfloat16* dV;
+  long long lddv;
+  int* err;
+};
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr uint32_t kPanel = 128u * 128u;  // one 64-column panel of 128 rows (bytes)
+
+template <int D>
+struct FaCfg {
+  static constexpr int PANELS = D / 64;
+  static constexpr uint32_t TILE = 128u * D * 2u;     // 128 rows x D bf16
+  static constexpr uint32_t PTILE = 128u * 128u * 2u;  // 128 x 128 bf16
+  static constexpr size_t FWD_SMEM = 1024 + TILE * 5 + PTILE + 16 * 8 + 16;
+  static constexpr size_t BWD_SMEM = 1024 + TILE * 4 + PTILE * 2 + 2 * 128 * 4 + 20 * 8 + 16;
+};
+
+// K-major operand tile with K = 128 elements (two 64-element panels): k-step kk of 16.
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t base, int kk) {
+  return umma_desc_sw128(base + (uint32_t)(kk >> 2) * kPanel + (uint32_t)(kk & 3) * 32u, 16, 1024);
+}
+// MN-major operand tile (MN in 64-element panels, K along the 128 rows): k-step kk of 16.
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t base, int kk) {
+  return umma_desc_sw128(base + (uint32_t)kk * 2048u, kPanel, 1024);
+}
+
+// Write 128 fp32 values (one row) as bf16 into a 128-row x 128-col swizzled tile.
+__device__ __forceinline__ void store_row_bf16_sw128(uint8_t* tile, int row, const float* v) {
+#pragma unroll
+  for (int c = 0; c < 16; ++c) {
+    uint4 u;
+    u.x = pack_bf16x2(v[8 * c + 0], v[8 * c + 1]);
+    u.y = pack_bf16x2(v[8 * c + 2], v[8 * c + 3]);
+    u.z = pack_bf16x2(v[8 * c + 4], v[8 * c + 5]);
+    u.w = pack_bf16x2(v[8 * c + 6], v[8 * c + 7]);
+    *reinterpret_cast<uint4*>(tile + (c >> 3) * kPanel + sw128_chunk_offset(row, c & 7)) = u;
+  }
+}
+
+__device__ __forceinline__ void store_row_bf16_global(__nv_bfloat16* dst, const float* v, int n) {
+  for (int c = 0; c < n / 8; ++c) {
+    uint4 u;
+    u.x = pack_bf16x2(v[8 * c + 0], v[8 * c + 1]);
+    u.y = pack_bf16x2(v[8 * c + 2], v[8 * c + 3]);
+    u.z = pack_bf16x2(v[8 * c + 4], v[8 * c + 5]);
+    u.w = pack_bf16x2(v[8 * c + 6], v[8 * c + 7]);
+    reinterpret_cast<uint4*>(dst)[c] = u;
+  }
+}
+
+// ================================================================================ forward
+template <int D>
+__global__ void __launch_bounds__(192, 1)
+    fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                  const __grid_constant__ CUtensorMap tmV, const FaArgs a) {
+  using Cfg = FaCfg<D>;
+  constexpr uint32_t TILE = Cfg::TILE;
+  constexpr uint32_t IDESC_S = umma_idesc_bf16(128, 128, false, false);
+  constexpr uint32_t IDESC_O = umma_idesc_bf16(128, D, false, true);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + TILE;
+  uint8_t* sV = sK + 2 * TILE;
+  uint8_t* sP = sV + 2 * TILE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + Cfg::PTILE);
+  uint64_t* bar_q = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* s_free = bars + 7;    // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* pv_done = bars + 10;
+  uint64_t* drain = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int BH = a.B * a.H;
+  const int qt = a.n_tiles - 1 - (int)(blockIdx.x / BH);
+  const int bh = (int)(blockIdx.x % BH);
+  const int b = bh / a.H, h = bh % a.H;
+  const int row0 = b * a.T + qt * 128;
+  const int n_kv = a.causal ? qt + 1 : a.n_tiles;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_q, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(pv_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS[2] = {tmem, tmem + 128};
+  const uint32_t tO = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      bool ok = true;
+      uint32_t out_valid = 0, out_parity = 0;
+      mbar_arrive_expect_tx(bar_q, TILE);
+#pragma unroll
+      for (int p = 0; p < Cfg::PANELS; ++p) tma_load_3d(sQ + p * kPanel, &tmQ, bar_q, h * D + p * 64, row0, 0);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int s = j & 1;
+        if (j >= 2 && !mbar_wait(&kv_empty[s], ((j - 2) >> 1) & 1, abort_flag, a.err, ERR_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&kv_full[s], 2 * TILE);
+        out_valid |= 1u << s;
+        out_parity = (out_parity & ~(1u << s)) | ((uint32_t)((j >> 1) & 1) << s);
+        const int krow = b * a.T + j * 128;
+#pragma unroll
+        for (int p = 0; p < Cfg::PANELS; ++p) {
+          tma_load_3d(sK + s * TILE + p * kPanel, &tmK, &kv_full[s], h * D + p * 64, krow, 0);
+          tma_load_3d(sV + s * TILE + p * kPanel, &tmV, &kv_full[s], h * D + p * 64, krow, 0);
+        }
+      }
+      if (!ok) {
+        for (int s = 0; s < 2; ++s) {
+          if (!((out_valid >> s) & 1u)) continue;
+          const unsigned long long t0 = globaltimer_ns();
+          while (!mbar_try_wait(&kv_full[s], (out_parity >> s) & 1u))
+            if (globaltimer_ns() - t0 > 100000000ull) break;
+        }
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(bar_q, 0))
+          if (globaltimer_ns() - t0 > 100000000ull) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = mbar_wait(bar_q, 0, abort_flag, a.err, ERR_TIMEOUT_MMA);
+      const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
+      auto issue_pv = [&](int jj) -> bool {
+        if (!mbar_wait(p_full, jj & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sV + (jj & 1) * TILE);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16(tO, desc_kmajor(p_addr, kk), desc_mnmajor(v_addr, kk), IDESC_O, (jj > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&kv_empty[jj & 1]);
+        umma_commit(pv_done);
+        return true;
+      };
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&kv_full[s], (j >> 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
+        if (j >= 2 && !mbar_wait(&s_free[s], ((j - 2) >> 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sK + s * TILE);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_bf16(tS[s], desc_kmajor(q_addr, kk), desc_kmajor(k_addr, kk), IDESC_S, kk > 0 ? 1u : 0u);
+        umma_commit(&s_full[s]);
+        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+      }
+      if (ok) ok = issue_pv(n_kv - 1);
+      if (!ok) {
+        umma_commit(drain);
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(drain, 0))
+          if (globaltimer_ns() - t0 > 100000000ull) break;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const int s = j & 1;
+      if (!mbar_wait_warp(&s_full[s], (j >> 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      tc_fence_after();
+      float x[128];
+      {
+        uint32_t* xr = reinterpret_cast<uint32_t*>(x);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          __syncwarp();
+          tmem_ld_32x32b_x32(tS[s] + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(xr + 32 * c));
+        }
+        tmem_ld_wait();
+      }
+      tc_fence_before();
+      mbar_arrive(&s_free[s]);
+      const bool diag = a.causal && (j == qt);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 128; ++i) {
+        float t = x[i] * a.scale_log2;
+        if (diag && i > r) t = -INFINITY;
+        x[i] = t;
+        mx = fmaxf(mx, t);
+      }
+      const float m_new = fmaxf(m, mx);
+      const float alpha = exp2f(m - m_new);
+      float sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < 128; ++i) {
+        const float pv = exp2f(x[i] - m_new);
+        x[i] = pv;
+        sum += pv;
+      }
+      l = l * alpha + sum;
+      m = m_new;
+      if (j >= 1) {
+        if (!mbar_wait_warp(pv_done, (j - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha < 1.f)) {
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            __syncwarp();
+            tmem_ld_32x32b_x32(tO + lane_off + c * 32, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st_32x32b_x32(tO + lane_off + c * 32, o);
+          }
+          tmem_st_wait();
+        }
+      }
+      store_row_bf16_sw128(sP, r, x);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && mbar_wait_warp(pv_done, (n_kv - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) {
+      tc_fence_after();
+      const float inv_l = 1.f / l;
+      __nv_bfloat16* dst = a.O + (long long)(row0 + r) * a.ldo + h * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(tO + lane_off + c * 32, o);
+        tmem_ld_wait();
+        float f[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(o[i]) * inv_l;
+        store_row_bf16_global(dst + c * 32, f, 32);
+      }
+      a.lse[(long long)bh * a.T + qt * 128 + r] = (m + log2f(l)) * kLn2;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ================================================================================ backward
+template <int D>
+__global__ void __launch_bounds__(192, 1)
+    fa_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                  const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO, const FaArgs a) {
+  using Cfg = FaCfg<D>;
+  constexpr uint32_t TILE = Cfg::TILE;
+  constexpr uint32_t IDESC_SS = umma_idesc_bf16(128, 128, false, false);  // S^T, dP^T
+  constexpr uint32_t IDESC_KV = umma_idesc_bf16(128, D, false, true);     // dV, dK
+  constexpr uint32_t IDESC_Q = umma_idesc_bf16(128, D, true, true);       // dQ
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + TILE;
+  uint8_t* sQ = sV + TILE;
+  uint8_t* sDO = sQ + TILE;
+  uint8_t* sP = sDO + TILE;
+  uint8_t* sDS = sP + Cfg::PTILE;
+  float* sLse = reinterpret_cast<float*>(sDS + Cfg::PTILE);
+  float* sDv = sLse + 128;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDv + 128);
+  uint64_t* bar_kv = bars + 0;
+  uint64_t* qdo_full = bars + 1;
+  uint64_t* qdo_empty = bars + 2;
+  uint64_t* s_full = bars + 3;
+  uint64_t* dp_full = bars + 4;
+  uint64_t* p_full = bars + 5;
+  uint64_t* ds_full = bars + 6;
+  uint64_t* dq_full = bars + 7;
+  uint64_t* dq_free = bars + 8;
+  uint64_t* dp_free = bars + 9;
+  uint64_t* kv_done = bars + 10;
+  uint64_t* drain = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int BH = a.B * a.H;
+  const int kt = (int)(blockIdx.x / BH);  // small key tiles have the most work: first
+  const int bh = (int)(blockIdx.x % BH);
+  const int b = bh / a.H, h = bh % a.H;
+  const int krow0 = b * a.T + kt * 128;
+  const int i0 = a.causal ? kt : 0;
+  const int n_it = a.n_tiles - i0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_kv, 1);
+    mbar_init(qdo_full, 1);
+    mbar_init(qdo_empty, 1);
+    mbar_init(s_full, 1);
+    mbar_init(dp_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(ds_full, 128);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 128);
+    mbar_init(dp_free, 128);
+    mbar_init(kv_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmDO);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tA = tmem;        // S^T, then dQ
+  const uint32_t tB = tmem + 128;  // dP^T
+  const uint32_t tDV = tmem + 256;
+  const uint32_t tDK = tmem + 256 + D;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      bool ok = true;
+      bool pending = false;
+      uint32_t pend_par = 0;
+      mbar_arrive_expect_tx(bar_kv, 2 * TILE);
+#pragma unroll
+      for (int p = 0; p < Cfg::PANELS; ++p) {
+        tma_load_3d(sK + p * kPanel, &tmK, bar_kv, h * D + p * 64, krow0, 0);
+        tma_load_3d(sV + p * kPanel, &tmV, bar_kv, h * D + p * 64, krow0, 0);
+      }
+      for (int it = 0; it < n_it && ok; ++it) {
+        if (it >= 1 && !mbar_wait(qdo_empty, (it - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_PRODUCER)) { ok = false; break; }
+        mbar_arrive_expect_tx(qdo_full, 2 * TILE + 2 * 512);
+        pending = true;
+        pend_par = it & 1;
+        const int qrow = b * a.T + (i0 + it) * 128;
+        bulk_load(sLse, a.lse + (long long)bh * a.T + (i0 + it) * 128, 512, qdo_full);
+        bulk_load(sDv, a.dvec + (long long)bh * a.T + (i0 + it) * 128, 512, qdo_full);
+#pragma unroll
+        for (int p = 0; p < Cfg::PANELS; ++p) {
+          tma_load_3d(sQ + p * kPanel, &tmQ, qdo_full, h * D + p * 64, qrow, 0);
+          tma_load_3d(sDO + p * kPanel, &tmDO, qdo_full, h * D + p * 64, qrow, 0);
+        }
+      }
+      if (!ok) {
+        const unsigned long long t0 = globaltimer_ns();
+        while (pending && !mbar_try_wait(qdo_full, pend_par))
+          if (globaltimer_ns() - t0 > 100000000ull) break;
+        while (!mbar_try_wait(bar_kv, 0))
+          if (globaltimer_ns() - t0 > 200000000ull) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = mbar_wait(bar_kv, 0, abort_flag, a.err, ERR_TIMEOUT_MMA);
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), q_addr = smem_u32(sQ), do_addr = smem_u32(sDO);
+      const uint32_t p_addr = smem_u32(sP), ds_addr = smem_u32(sDS);
+      for (int it = 0; it < n_it && ok; ++it) {
+        if (!mbar_wait(qdo_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
+        if (it >= 1 && !mbar_wait(dq_free, (it - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)  // S^T = K Q^T
+          umma_bf16(tA, desc_kmajor(k_addr, kk), desc_kmajor(q_addr, kk), IDESC_SS, kk > 0 ? 1u : 0u);
+        umma_commit(s_full);
+        if (it >= 1 && !mbar_wait(dp_free, (it - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)  // dP^T = V dO^T
+          umma_bf16(tB, desc_kmajor(v_addr, kk), desc_kmajor(do_addr, kk), IDESC_SS, kk > 0 ? 1u : 0u);
+        umma_commit(dp_full);
+        if (!mbar_wait(p_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // dV += P^T dO
+          umma_bf16(tDV, desc_kmajor(p_addr, kk), desc_mnmajor(do_addr, kk), IDESC_KV, (it > 0 || kk > 0) ? 1u : 0u);
+        if (!mbar_wait(ds_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // dK += dS^T Q
+          umma_bf16(tDK, desc_kmajor(ds_addr, kk), desc_mnmajor(q_addr, kk), IDESC_KV, (it > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // dQ = dS K
+          umma_bf16(tA, desc_mnmajor(ds_addr, kk), desc_mnmajor(k_addr, kk), IDESC_Q, kk > 0 ? 1u : 0u);
+        umma_commit(dq_full);
+        umma_commit(qdo_empty);
+      }
+      if (ok) umma_commit(kv_done);
+      else {
+        umma_commit(drain);
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(drain, 0))
+          if (globaltimer_ns() - t0 > 100000000ull) break;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax / epilogue
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int i = i0 + it;
+      // LSE / Dvec of this query tile arrive with Q and dO (same barrier)
+      if (!mbar_wait_warp(qdo_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      if (!mbar_wait_warp(s_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      tc_fence_after();
+      const bool diag = a.causal && (i == kt);
+      uint32_t pk[64];  // P^T row as packed bf16 pairs (kept for dS)
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t sv[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(tA + lane_off + c4 * 32, sv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const int c = c4 * 32 + e;
+          float p0 = exp2f(__uint_as_float(sv[e]) * a.scale_log2 - sLse[c] * kLog2e);
+          float p1 = exp2f(__uint_as_float(sv[e + 1]) * a.scale_log2 - sLse[c + 1] * kLog2e);
+          if (diag && c < r) p0 = 0.f;  // query c precedes key r: no attention
+          if (diag && c + 1 < r) p1 = 0.f;
+          pk[c >> 1] = pack_bf16x2(p0, p1);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const uint4 u = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        *reinterpret_cast<uint4*>(sP + (c >> 3) * kPanel + sw128_chunk_offset(r, c & 7)) = u;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+      if (!mbar_wait_warp(dp_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      tc_fence_after();
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t dv[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(tB + lane_off + c4 * 32, dv);
+        tmem_ld_wait();
+        uint32_t dsk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const int c = c4 * 32 + e;
+          const float2 pf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&pk[c >> 1]));
+          dsk[e >> 1] = pack_bf16x2(pf.x * (__uint_as_float(dv[e]) - sDv[c]),
+                                    pf.y * (__uint_as_float(dv[e + 1]) - sDv[c + 1]));
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int c = c4 * 4 + q;  // 16-byte chunk index within the 128-column row
+          *reinterpret_cast<uint4*>(sDS + (c >> 3) * kPanel + sw128_chunk_offset(r, c & 7)) =
+              make_uint4(dsk[4 * q], dsk[4 * q + 1], dsk[4 * q + 2], dsk[4 * q + 3]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(dp_free);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(ds_full);
+      if (!mbar_wait_warp(dq_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      tc_fence_after();
+      float* dq = a.dq_acc + (long long)(b * a.T + i * 128 + r) * a.lddq + h * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(tA + lane_off + c * 32, o);
+        tmem_ld_wait();
+#pragma unroll
+        for (int v = 0; v < 8; ++v)
+          atomicAdd(reinterpret_cast<float4*>(dq + c * 32) + v,
+                    make_float4(__uint_as_float(o[4 * v]) * a.scale, __uint_as_float(o[4 * v + 1]) * a.scale,
+                                __uint_as_float(o[4 * v + 2]) * a.scale, __uint_as_float(o[4 * v + 3]) * a.scale));
+      }
+      tc_fence_before();
+      mbar_arrive(dq_free);
+    }
+    if (ok && mbar_wait_warp(kv_done, 0, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) {
+      tc_fence_after();
+      __nv_bfloat16* dv = a.dV + (long long)(krow0 + r) * a.lddv + h * D;
+      __nv_bfloat16* dk = a.dK + (long long)(krow0 + r) * a.lddk + h * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        float f[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(tDV + lane_off + c * 32, o);
+        tmem_ld_wait();
+#pragma unroll
+        for (int v = 0; v < 32; ++v) f[v] = __uint_as_float(o[v]);
+        store_row_bf16_global(dv + c * 32, f, 32);
+        __syncwarp();
+        tmem_ld_32x32b_x32(tDK + lane_off + c * 32, o);
+        tmem_ld_wait();
+#pragma unroll
+        for (int v = 0; v < 32; ++v) f[v] = __uint_as_float(o[v]) * a.scale;
+        store_row_bf16_global(dk + c * 32, f, 32);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// Dvec[bh, t] = sum_d dO[t, h*D + d] * O[t, h*D + d]; one warp per (row, head).
+__global__ void fa_bwd_dot_kernel(const __nv_bfloat16* __restrict__ dO, long long lddo,
+                                  const __nv_bfloat16* __restrict__ O, long long ldo, float* __restrict__ dvec,
+                                  int B, int T, int H, int D) {
+  const long long w = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (w >= (long long)B * T * H) return;
+  const int row = (int)(w / H), h = (int)(w % H);
+  const __nv_bfloat16* g = dO + (long long)row * lddo + h * D;
+  const __nv_bfloat16* o = O + (long long)row * ldo + h * D;
+  float acc = 0.f;
+  for (int d = lane * 2; d < D; d += 64) {
+    const float2 gf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(g + d));
+    const float2 of = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(o + d));
+    acc += gf.x * of.x + gf.y * of.y;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) {
+    const int b = row / T, t = row % T;
+    dvec[((long long)b * H + h) * T + t] = acc;
+  }
+}
+
+// bf16 copy of an fp32 [rows, cols] accumulator into a strided bf16 destination.
+__global__ void f32_to_bf16_rows_kernel(const float* __restrict__ src, long long lds, __nv_bfloat16* __restrict__ dst,
+                                        long long ldd, int rows, int cols) {
+  const long long idx = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  const long long total = (long long)rows * cols;
+  if (idx >= total) return;
+  const int r = (int)(idx / cols), c = (int)(idx % cols);
+  const float4 a = *reinterpret_cast<const float4*>(src + r * lds + c);
+  const float4 bq = *reinterpret_cast<const float4*>(src + r * lds + c + 4);
+  uint4 u;
+  u.x = pack_bf16x2(a.x, a.y);
+  u.y = pack_bf16x2(a.z, a.w);
+  u.z = pack_bf16x2(bq.x, bq.y);
+  u.w = pack_bf16x2(bq.z, bq.w);
+  *reinterpret_cast<uint4*>(dst + r * ldd + c) = u;
+}
+
+// ------------------------------------------------------------------------------ host
+template <typename K>
+static void set_smem(K kern, size_t bytes) {
+  C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+}
+
+static void check_view(const torch::Tensor& t, const char* n, int64_t rows, int64_t cols) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 2, n, ": CUDA bf16 2-D view");
+  TORCH_CHECK(t.stride(1) == 1 && t.size(0) == rows && t.size(1) >= cols, n, ": [B*T, >= H*D] with unit inner stride");
+  TORCH_CHECK((t.stride(0) * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0, n, ": 16-byte aligned rows");
+}
+
+// q, k, v: [B*T, *] row views (head h at cols h*D); out: [B*T, >= H*D]; lse: fp32 [B*H*T]
+void fa_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, int64_t B, int64_t T, int64_t H, int64_t D,
+            double scale, bool causal, torch::Tensor out, torch::Tensor lse, torch::Tensor err) {
+  TORCH_CHECK(D == 64 || D == 128, "head_dim must be 64 or 128");
+  TORCH_CHECK(T % 128 == 0, "sequence length must be a multiple of 128");
+  const int64_t rows = B * T, cols = H * D;
+  check_view(q, "q", rows, cols);
+  check_view(k, "k", rows, cols);
+  check_view(v, "v", rows, cols);
+  check_view(out, "out", rows, cols);
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.numel() >= B * H * T, "lse fp32 [B*H*T]");
+  c10::cuda::CUDAGuard guard(q.device());
+  CUtensorMap tq = make_tmap_bf16(q.data_ptr(), cols, rows, q.stride(0), 64, 128, 1, 0);
+  CUtensorMap tk = make_tmap_bf16(k.data_ptr(), cols, rows, k.stride(0), 64, 128, 1, 0);
+  CUtensorMap tv = make_tmap_bf16(v.data_ptr(), cols, rows, v.stride(0), 64, 128, 1, 0);
+  FaArgs a{};
+  a.B = (int)B; a.T = (int)T; a.H = (int)H; a.n_tiles = (int)(T / 128); a.causal = causal ? 1 : 0;
+  a.scale = (float)scale; a.scale_log2 = (float)(scale * 1.4426950408889634);
+  a.O = reinterpret_cast<__nv_bfloat16*>(out.data_ptr()); a.ldo = out.stride(0);
+  a.lse = lse.data_ptr<float>();
+  a.err = err.data_ptr<int>();
+  const unsigned grid = (unsigned)(B * H * (T / 128));
+  auto s = at::cuda::getCurrentCUDAStream();
+  if (D == 128) {
+    static bool init = false;
+    if (!init) { set_smem(fa_fwd_kernel<128>, FaCfg<128>::FWD_SMEM); init = true; }
+    fa_fwd_kernel<128><<<grid, 192, FaCfg<128>::FWD_SMEM, s>>>(tq, tk, tv, a);
+  } else {
+    static bool init = false;
+    if (!init) { set_smem(fa_fwd_kernel<64>, FaCfg<64>::FWD_SMEM); init = true; }
+    fa_fwd_kernel<64><<<grid, 192, FaCfg<64>::FWD_SMEM, s>>>(tq, tk, tv, a);
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Gradients: dq_acc (fp32, zeroed here) accumulates dQ; dk / dv receive bf16 dK / dV;
+// dq_out (bf16 view) receives dQ.  dvec: fp32 scratch [B*H*T].
+void fa_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor dout, torch::Tensor lse,
+            int64_t B, int64_t T, int64_t H, int64_t D, double scale, bool causal, torch::Tensor dq_acc,
+            torch::Tensor dq_out, torch::Tensor dk, torch::Tensor dv, torch::Tensor dvec, torch::Tensor err) {
+  TORCH_CHECK(D == 64 || D == 128, "head_dim must be 64 or 128");
+  TORCH_CHECK(T % 128 == 0, "sequence length must be a multiple of 128");
+  const int64_t rows = B * T, cols = H * D;
+  check_view(q, "q", rows, cols);
+  check_view(k, "k", rows, cols);
+  check_view(v, "v", rows, cols);
+  check_view(o, "o", rows, cols);
+  check_view(dout, "dout", rows, cols);
+  check_view(dk, "dk", rows, cols);
+  check_view(dv, "dv", rows, cols);
+  check_view(dq_out, "dq_out", rows, cols);
+  TORCH_CHECK(dq_acc.scalar_type() == at::kFloat && dq_acc.dim() == 2 && dq_acc.size(0) == rows &&
+                  dq_acc.stride(1) == 1 && dq_acc.size(1) >= cols,
+              "dq_acc fp32 [B*T, >= H*D]");
+  c10::cuda::CUDAGuard guard(q.device());
+  auto s = at::cuda::getCurrentCUDAStream();
+  dq_acc.zero_();
+  {
+    const long long warps = rows * H;
+    fa_bwd_dot_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(
+        reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), dout.stride(0),
+        reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), o.stride(0), dvec.data_ptr<float>(), (int)B, (int)T,
+        (int)H, (int)D);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  CUtensorMap tq = make_tmap_bf16(q.data_ptr(), cols, rows, q.stride(0), 64, 128, 1, 0);
+  CUtensorMap tk = make_tmap_bf16(k.data_ptr(), cols, rows, k.stride(0), 64, 128, 1, 0);
+  CUtensorMap tv = make_tmap_bf16(v.data_ptr(), cols, rows, v.stride(0), 64, 128, 1, 0);
+  CUtensorMap tdo = make_tmap_bf16(dout.data_ptr(), cols, rows, dout.stride(0), 64, 128, 1, 0);
+  FaArgs a{};
+  a.B = (int)B; a.T = (int)T; a.H = (int)H; a.n_tiles = (int)(T / 128); a.causal = causal ? 1 : 0;
+  a.scale = (float)scale; a.scale_log2 = (float)(scale * 1.4426950408889634);
+  a.lse = lse.data_ptr<float>();
+  a.dvec = dvec.data_ptr<float>();
+  a.dq_acc = dq_acc.data_ptr<float>(); a.lddq = dq_acc.stride(0);
+  a.dK = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr()); a.lddk = dk.stride(0);
+  a.dV = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr()); a.lddv = dv.stride(0);
+  a.err = err.data_ptr<int>();
+  const unsigned grid = (unsigned)(B * H * (T / 128));
+  if (D == 128) {
+    static bool init = false;
+    if (!init) { set_smem(fa_bwd_kernel<128>, FaCfg<128>::BWD_SMEM); init = true; }
+    fa_bwd_kernel<128><<<grid, 192, FaCfg<128>::BWD_SMEM, s>>>(tq, tk, tv, tdo, a);
+  } else {
+    static bool init = false;
+    if (!init) { set_smem(fa_bwd_kernel<64>, FaCfg<64>::BWD_SMEM); init = true; }
+    fa_bwd_kernel<64><<<grid, 192, FaCfg<64>::BWD_SMEM, s>>>(tq, tk, tv, tdo, a);
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  {
+    const long long n8 = rows * cols / 8;
+    f32_to_bf16_rows_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(
+        dq_acc.data_ptr<float>(), dq_acc.stride(0), reinterpret_cast<__nv_bfloat16*>(dq_out.data_ptr()),
+        dq_out.stride(0), (int)rows, (int)cols);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+}
+
+}  // namespace tfb

@@ -27,6 +27,11 @@ void softcap_ce(torch::Tensor logits, torch::Tensor targets, int64_t T, c10::opt
 void adamw_multi(std::vector<torch::Tensor> params, std::vector<torch::Tensor> grads, std::vector<torch::Tensor> m,
                  std::vector<torch::Tensor> v, torch::Tensor lr, double beta1, double beta2, double eps, double wd,
                  std::vector<double> bc1, std::vector<double> bc2, bool cautious);
+void fa_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, int64_t B, int64_t T, int64_t H, int64_t D,
+            double scale, bool causal, torch::Tensor out, torch::Tensor lse, torch::Tensor err);
+void fa_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor dout, torch::Tensor lse,
+            int64_t B, int64_t T, int64_t H, int64_t D, double scale, bool causal, torch::Tensor dq_acc,
+            torch::Tensor dq_out, torch::Tensor dk, torch::Tensor dv, torch::Tensor dvec, torch::Tensor err);
 }  // namespace tfb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -46,4 +51,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_norm_bwd", &tfb::rope_norm_bwd);
   m.def("softcap_ce", &tfb::softcap_ce);
   m.def("adamw_multi", &tfb::adamw_multi);
+  m.def("fa_fwd", &tfb::fa_fwd, "tcgen05 causal flash attention forward");
+  m.def("fa_bwd", &tfb::fa_bwd, "tcgen05 causal flash attention backward");
 }

@@ -239,7 +239,7 @@ __global__ void __launch_bounds__(192, 1)
     for (int t = blockIdx.x; t < args.num_tiles; t += gridDim.x) {
       int mb, nb, ks, bi;
       decode_tile(t, args, mb, nb, ks, bi);
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, args.err, ERR_TIMEOUT_EPILOGUE)) break;
+      if (!mbar_wait_warp(&tfull[acc], acc_phase, abort_flag, args.err, ERR_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const int row = mb * BM + q * 32 + lane;
       const bool row_ok = row < args.M;

@@ -76,7 +76,14 @@ def rope_norm(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Te
 
 
 def attention(q, k, v, causal: bool = True, scale: float | None = None, attn_mask=None):
-    """q, k, v [B, T, H, D] -> [B, T, H, D]."""
+    """q, k, v [B, T, H, D] -> [B, T, H, D].  CUDA: tcgen05 flash attention (causal or
+    full, T % 128 == 0, head_dim 64 / 128); additive masks (document / sliding-window
+    variants of the family) use the reference composition."""
+    if _cuda(q) and q.dtype == torch.bfloat16 and attn_mask is None:
+        from .attention import FlashAttnFn, supported
+        B, T, H, D = q.shape
+        if supported(T, D):
+            return FlashAttnFn.apply(q, k, v, causal, scale if scale is not None else D ** -0.5)
     return ref.attention(q, k, v, causal, scale, attn_mask)
 
 
@@ -84,7 +91,8 @@ def attention_qkv(qkv: torch.Tensor, cos, sin, n_head: int, head_dim: int, scale
     """Plain-block attention core from the fused projection [B, T, 3C]:
     RoPE + QK-norm on q, k, then causal attention.  Returns [B, T, C]."""
     B, T, C3 = qkv.shape
-    if _cuda(qkv) and qkv.dtype == torch.bfloat16:
+    from .attention import supported
+    if _cuda(qkv) and qkv.dtype == torch.bfloat16 and supported(T, head_dim):
         from .fused import AttnQKVFn
         c2 = cos.reshape(-1, cos.shape[-1])[:T].contiguous()
         s2 = sin.reshape(-1, sin.shape[-1])[:T].contiguous()

@@ -297,46 +297,34 @@ class RopeNormFn(Function):
         return gx, None, None, None
 
 
-def _flash_fwd(q, k, v, causal, scale):
-    out = torch.ops.aten._scaled_dot_product_flash_attention(q, k, v, 0.0, causal, False, scale=scale)
-    return out
-
-
 class AttnQKVFn(Function):
     """Fused attention core of the plain block: RoPE + QK-norm of q and k from the
-    [M, 3C] projection buffer, causal attention, output [B, T, C]."""
+    [M, 3C] projection buffer, causal tcgen05 flash attention, output [B, T, C].
+    The backward writes dq / dk / dv straight into one [M, 3C] gradient buffer and
+    applies the RoPE + QK-norm backward in place on its q / k columns."""
 
     @staticmethod
     def forward(ctx, qkv, cos, sin, B, T, H, D, scale):
+        from .attention import flash_fwd
         Cd = H * D
         qkv2 = qkv.view(B * T, 3 * Cd)
         qkn = torch.empty((B * T, 2 * Cd), dtype=BF16, device=qkv.device)
         rstd = torch.empty(B * T * 2 * H, dtype=torch.float32, device=qkv.device)
         C().rope_norm_fwd(qkv2, 0, 2 * H, D, cos, sin, T, 0, rstd, qkn)
-        q = qkn[:, :Cd].view(B, T, H, D).transpose(1, 2)
-        k = qkn[:, Cd:].view(B, T, H, D).transpose(1, 2)
-        v = qkv2[:, 2 * Cd:].view(B, T, H, D).transpose(1, 2)
-        res = _flash_fwd(q, k, v, True, scale)
-        o, lse = res[0], res[1]
-        ctx.save_for_backward(qkv2, qkn, rstd, cos, sin, o, lse, res[6], res[7])
-        ctx.meta = (B, T, H, D, scale, res[2], res[3], res[4], res[5])
-        return o.transpose(1, 2).reshape(B, T, Cd)
+        o, lse = flash_fwd(qkn[:, :Cd], qkn[:, Cd:], qkv2[:, 2 * Cd:], B, T, H, D, scale, True)
+        ctx.save_for_backward(qkv2, qkn, rstd, cos, sin, o, lse)
+        ctx.meta = (B, T, H, D, scale)
+        return o.view(B, T, Cd)
 
     @staticmethod
     def backward(ctx, dy):
-        qkv2, qkn, rstd, cos, sin, o, lse, seed, offset = ctx.saved_tensors
-        B, T, H, D, scale, cq, ck, mq, mk = ctx.meta
+        from .attention import flash_bwd
+        qkv2, qkn, rstd, cos, sin, o, lse = ctx.saved_tensors
+        B, T, H, D, scale = ctx.meta
         Cd = H * D
-        q = qkn[:, :Cd].view(B, T, H, D).transpose(1, 2)
-        k = qkn[:, Cd:].view(B, T, H, D).transpose(1, 2)
-        v = qkv2[:, 2 * Cd:].view(B, T, H, D).transpose(1, 2)
-        do = dy.view(B, T, H, D).transpose(1, 2)
-        dq, dk, dv = torch.ops.aten._scaled_dot_product_flash_attention_backward(
-            do, q, k, v, o, lse, cq, ck, mq, mk, 0.0, True, seed, offset, scale=scale)
         dqkv = torch.empty((B * T, 3 * Cd), dtype=BF16, device=dy.device)
-        dqkv.view(B, T, 3, H, D)[:, :, 0].copy_(dq.transpose(1, 2))
-        dqkv.view(B, T, 3, H, D)[:, :, 1].copy_(dk.transpose(1, 2))
-        dqkv.view(B, T, 3, H, D)[:, :, 2].copy_(dv.transpose(1, 2))
+        flash_bwd(qkn[:, :Cd], qkn[:, Cd:], qkv2[:, 2 * Cd:], o, dy.reshape(B * T, Cd), lse, B, T, H, D, scale,
+                  True, dq=dqkv[:, :Cd], dk=dqkv[:, Cd:2 * Cd], dv=dqkv[:, 2 * Cd:])
         C().rope_norm_bwd(dqkv, qkn, 0, 2 * H, D, cos, sin, T, rstd)
         return dqkv.view(B, T, 3 * Cd), None, None, None, None, None, None, None
 
