@@ -168,3 +168,47 @@ def test_failure_detection_bad_loss_agreement(tmp_path):
     for r in (0, 1):
         out = json.load(open(tmp_path / f"fail_badloss_{r}.json"))
         assert "bad loss" in out["outcome"], out
+
+
+def _worker_dist_muon(rank, world, port, out_dir, steps):
+    sys.path.insert(0, ROOT)
+    torch.set_num_threads(2)
+    _init(rank, world, port)
+    from trainium_frontier_b200.config import preset
+    from trainium_frontier_b200.engine import TrainEngine
+    from trainium_frontier_b200.models.gpt import GPT
+    from trainium_frontier_b200.optim.muon_adamw import setup_optimizer
+    out = {}
+    for mode in ("bucket", "dist_muon"):
+        cfg = preset("tiny", grad_sync=mode, clip_order="global", bucket_layers=2)
+        torch.manual_seed(0)
+        m = GPT(cfg.model_config(), cfg)
+        m.init_weights()
+        opt = setup_optimizer(m, cfg, torch.float32)
+        eng = TrainEngine(m, opt, cfg, torch.device("cpu"), 1, mode)
+        g = torch.Generator().manual_seed(300 + rank)
+        losses = []
+        for _ in range(steps):
+            x = torch.randint(1, 8192, (4, 257), generator=g)
+            losses.append(eng.forward_backward([(x[:, :-1], x[:, 1:])]).item())
+            eng.sync_and_clip()
+            eng.optimizer_step()
+        out[mode] = {"losses": losses, "state": {k: v.detach().clone() for k, v in m.state_dict().items()}}
+    torch.save(out, os.path.join(out_dir, f"dm_{rank}.pt"))
+    dist.destroy_process_group()
+
+
+def test_dist_muon_matches_allreduce(tmp_path):
+    port = _port()
+    mp.spawn(_worker_dist_muon, args=(2, port, str(tmp_path), 3), nprocs=2, join=True)
+    r0 = torch.load(tmp_path / "dm_0.pt")
+    r1 = torch.load(tmp_path / "dm_1.pt")
+    for a, b in zip(r0["bucket"]["losses"], r0["dist_muon"]["losses"]):
+        assert abs(a - b) < 1e-3 * abs(a), (a, b)
+    for k, v in r0["dist_muon"]["state"].items():
+        assert torch.equal(v, r1["dist_muon"]["state"][k]), k  # replicas identical
+        ref = r0["bucket"]["state"][k]
+        if k.endswith("weight") and v.dim() == 2 and ".h." in k:   # Muon matrices
+            assert torch.allclose(v, ref, rtol=1e-2, atol=1e-4), k
+        else:  # AdamW tensors: eps=1e-10 turns rounding-level gradient noise into +-lr steps
+            assert (v - ref).abs().mean() <= 2e-2 * ref.abs().mean() + 1e-6, k

@@ -1,0 +1,59 @@
+"""Multi-GPU data parallelism (NCCL, one process per GPU), launched with torchrun.
+Skipped on boxes with fewer than two GPUs."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+WORKER = r'''
+import json, os, sys, torch, torch.distributed as dist
+sys.path.insert(0, os.environ["TFB_ROOT"])
+from trainium_frontier_b200.config import preset
+from trainium_frontier_b200.runtime import init_runtime
+from trainium_frontier_b200.train import Trainer
+ddp, rank, local, world, dev = init_runtime("cuda", 0, timeout_s=120)
+mode = os.environ["TFB_MODE"]
+cfg = preset("tiny", depth=4, n_embd=256, head_dim=128, seq_len=256, device_batch_size=4, pack_factor=1,
+             total_batch_size=4 * 256 * world, grad_sync=mode, clip_order="global", progress_mode="steps",
+             num_steps=20, bucket_layers=2)
+tr = Trainer(cfg, dev, rank, world)
+losses = [tr.train_step() for _ in range(6)]
+flat = tr.engine.layout.data
+chk = torch.stack([flat.double().sum(), flat.double().square().sum()])
+allc = [torch.zeros_like(chk) for _ in range(world)]
+dist.all_gather(allc, chk)
+from trainium_frontier_b200.ops._ext import check_errors
+check_errors(dev)
+if rank == 0:
+    print("RESULT " + json.dumps({"losses": losses, "checks": [c.tolist() for c in allc]}))
+dist.destroy_process_group()
+'''
+
+
+def _run(mode, n, tmp_path):
+    script = tmp_path / "worker.py"
+    script.write_text(WORKER)
+    env = dict(os.environ, TFB_ROOT=ROOT, TFB_MODE=mode, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
+           "--master-addr", "127.0.0.1", "--master-port", "29517", str(script)]
+    p = subprocess.run(["timeout", "-k", "30", "300"] + cmd, env=env, capture_output=True, text=True)
+    assert p.returncode == 0, p.stderr[-3000:]
+    line = [ln for ln in p.stdout.splitlines() if ln.startswith("RESULT ")][-1]
+    return json.loads(line[len("RESULT "):])
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("mode", ["dist_muon", "bucket"])
+def test_dp2_replicas_identical_and_learning(mode, tmp_path):
+    res = _run(mode, 2, tmp_path)
+    assert res["losses"][-1] < res["losses"][0]
+    c0 = res["checks"][0]
+    for c in res["checks"][1:]:
+        assert c == c0  # fp32 masters bit-identical on every rank

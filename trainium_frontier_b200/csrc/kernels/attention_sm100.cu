@@ -16,7 +16,7 @@
 //     P^T = exp(S^T * scale - LSE_i), dS^T = P^T (dP^T - Dvec_i)   (registers -> smem)
 //     dV += P^T dO_i, dK += dS^T Q_i                       (TMEM accumulators)
 //     dQ_i = dS K  -> fp32 vector atomics into a dQ accumulator
-// Every wait is bounded (see sm100_common.cuh); no TMA multicast.
+// Every wait is bounded (see sm100_common.cuh); every TMA load is a plain per-CTA load.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>

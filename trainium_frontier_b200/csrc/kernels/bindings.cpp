@@ -19,7 +19,13 @@ void embed_norm_bwd(torch::Tensor idx, torch::Tensor wte, torch::Tensor rstd, c1
                     c10::optional<torch::Tensor> gb, torch::Tensor dwte);
 void rope_norm_fwd(torch::Tensor buf, int64_t head0, int64_t nheads, int64_t D, torch::Tensor cos,
                    torch::Tensor sin, int64_t T, int64_t pos_offset, c10::optional<torch::Tensor> rstd,
-                   c10::optional<torch::Tensor> out);
+                   c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> pos_t);
+void decode_attn(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache, torch::Tensor len, int64_t H,
+                 int64_t D, double scale, torch::Tensor out);
+void kv_append(torch::Tensor k, torch::Tensor v, torch::Tensor kcache, torch::Tensor vcache, torch::Tensor pos);
+void step_advance(torch::Tensor counters);
+void argmax_rows(torch::Tensor logits, int64_t V, torch::Tensor idx_out, c10::optional<torch::Tensor> tokens,
+                 torch::Tensor counters, int64_t start);
 void rope_norm_bwd(torch::Tensor gbuf, torch::Tensor zbuf, int64_t head0, int64_t nheads, int64_t D,
                    torch::Tensor cos, torch::Tensor sin, int64_t T, torch::Tensor rstd);
 void softcap_ce(torch::Tensor logits, torch::Tensor targets, int64_t T, c10::optional<torch::Tensor> row_w,
@@ -32,6 +38,7 @@ void fa_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, int64_t B, int64_
 void fa_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor dout, torch::Tensor lse,
             int64_t B, int64_t T, int64_t H, int64_t D, double scale, bool causal, torch::Tensor dq_acc,
             torch::Tensor dq_out, torch::Tensor dk, torch::Tensor dv, torch::Tensor dvec, torch::Tensor err);
+void muon_apply(torch::Tensor w, torch::Tensor g, torch::Tensor lr, torch::Tensor lrwd);
 }  // namespace tfb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -47,10 +54,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mix_norm_bwd", &tfb::mix_norm_bwd);
   m.def("embed_norm_fwd", &tfb::embed_norm_fwd);
   m.def("embed_norm_bwd", &tfb::embed_norm_bwd);
-  m.def("rope_norm_fwd", &tfb::rope_norm_fwd);
+  m.def("rope_norm_fwd", &tfb::rope_norm_fwd, py::arg("buf"), py::arg("head0"), py::arg("nheads"), py::arg("D"),
+        py::arg("cos"), py::arg("sin"), py::arg("T"), py::arg("pos_offset"), py::arg("rstd"), py::arg("out"),
+        py::arg("pos_t") = py::none());
+  m.def("decode_attn", &tfb::decode_attn);
+  m.def("kv_append", &tfb::kv_append);
+  m.def("step_advance", &tfb::step_advance);
+  m.def("argmax_rows", &tfb::argmax_rows);
   m.def("rope_norm_bwd", &tfb::rope_norm_bwd);
   m.def("softcap_ce", &tfb::softcap_ce);
   m.def("adamw_multi", &tfb::adamw_multi);
+  m.def("muon_apply", &tfb::muon_apply);
   m.def("fa_fwd", &tfb::fa_fwd, "tcgen05 causal flash attention forward");
   m.def("fa_bwd", &tfb::fa_bwd, "tcgen05 causal flash attention backward");
 }

@@ -1,0 +1,194 @@
+// Inference kernels for KV-cache decoding (one new token per sequence per step).
+//
+// decode_attn: single-query attention over a KV cache laid out like the projection
+// buffers, [B, T_max, H*D] (head h at columns h*D), valid length read from device
+// memory so a whole decode step can be captured once in a CUDA graph and replayed.
+//   one CTA (128 threads) per (batch, head):
+//   phase 1  thread-per-key scores q.k (16-byte loads of the key row) into shared
+//            memory, block max / sum of exp;
+//   phase 2  thread-per-dimension output o[d] = sum_k p_k v_k[d] / l (coalesced rows).
+// kv_append: writes this step's k and v rows into the caches at the device-side
+// position; step_advance: increments the device-side position / length counters.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "sm100_common.cuh"
+
+namespace tfb {
+
+constexpr int kDecThreads = 128;
+
+template <int D>
+__global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
+    const __nv_bfloat16* __restrict__ q, long long ldq, const __nv_bfloat16* __restrict__ kc,
+    const __nv_bfloat16* __restrict__ vc, long long cache_ld, long long cache_bstride, const int* __restrict__ len_ptr,
+    int len_max, __nv_bfloat16* __restrict__ out, long long ldo, int H, float scale) {
+  extern __shared__ float s_scores[];
+  __shared__ float red[kDecThreads / 32];
+  __shared__ __align__(16) float s_q[D];
+  const int bh = blockIdx.x;
+  const int b = bh / H, h = bh % H;
+  const int tid = threadIdx.x;
+  int L = *len_ptr;
+  L = L < 1 ? 1 : (L > len_max ? len_max : L);
+  for (int d = tid; d < D; d += kDecThreads) s_q[d] = __bfloat162float(q[(long long)b * ldq + h * D + d]) * scale;
+  __syncthreads();
+  const __nv_bfloat16* kb = kc + (long long)b * cache_bstride + h * D;
+  const __nv_bfloat16* vb = vc + (long long)b * cache_bstride + h * D;
+  float mx = -INFINITY;
+  for (int k = tid; k < L; k += kDecThreads) {
+    const uint4* kr = reinterpret_cast<const uint4*>(kb + (long long)k * cache_ld);
+    float acc = 0.f;
+#pragma unroll
+    for (int c = 0; c < D / 8; ++c) {
+      const uint4 u = kr[c];
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h2[j]);
+        acc += f.x * s_q[c * 8 + 2 * j] + f.y * s_q[c * 8 + 2 * j + 1];
+      }
+    }
+    s_scores[k] = acc;
+    mx = fmaxf(mx, acc);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((tid & 31) == 0) red[tid >> 5] = mx;
+  __syncthreads();
+  float m = red[0];
+#pragma unroll
+  for (int w = 1; w < kDecThreads / 32; ++w) m = fmaxf(m, red[w]);
+  __syncthreads();
+  float sum = 0.f;
+  for (int k = tid; k < L; k += kDecThreads) {
+    const float p = __expf(s_scores[k] - m);
+    s_scores[k] = p;
+    sum += p;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if ((tid & 31) == 0) red[tid >> 5] = sum;
+  __syncthreads();
+  float l = 0.f;
+#pragma unroll
+  for (int w = 0; w < kDecThreads / 32; ++w) l += red[w];
+  const float inv_l = 1.f / l;
+  for (int d = tid; d < D; d += kDecThreads) {
+    float acc = 0.f;
+    for (int k = 0; k < L; ++k) acc += s_scores[k] * __bfloat162float(vb[(long long)k * cache_ld + d]);
+    out[(long long)b * ldo + h * D + d] = __float2bfloat16_rn(acc * inv_l);
+  }
+}
+
+// cache[b, pos, :] = src[b, :] for k and v (pos read from device memory).
+__global__ void kv_append_kernel(const __nv_bfloat16* __restrict__ ksrc, long long ldk,
+                                 const __nv_bfloat16* __restrict__ vsrc, long long ldv, __nv_bfloat16* __restrict__ kc,
+                                 __nv_bfloat16* __restrict__ vc, long long cache_ld, long long cache_bstride,
+                                 const int* __restrict__ pos_ptr, int len_max, int B, int C) {
+  const int pos = *pos_ptr;
+  if (pos < 0 || pos >= len_max) return;
+  const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (i >= (long long)B * C) return;
+  const int b = (int)(i / C), c = (int)(i % C);
+  const long long dst = (long long)b * cache_bstride + (long long)pos * cache_ld + c;
+  *reinterpret_cast<uint4*>(kc + dst) = *reinterpret_cast<const uint4*>(ksrc + (long long)b * ldk + c);
+  *reinterpret_cast<uint4*>(vc + dst) = *reinterpret_cast<const uint4*>(vsrc + (long long)b * ldv + c);
+}
+
+// counters[0] = position of the next token, counters[1] = valid cache length.
+__global__ void step_advance_kernel(int* counters) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    counters[0] += 1;
+    counters[1] += 1;
+  }
+}
+
+// Greedy pick over softcapped logits: argmax of the first V columns of bf16 rows; writes
+// the token into idx_out[b] and into tokens[b * ld_tok + (counters[0] - start)].
+__global__ void argmax_rows_kernel(const __nv_bfloat16* __restrict__ logits, long long ld, int V,
+                                   int* __restrict__ idx_out, int* __restrict__ tokens, long long ld_tok,
+                                   const int* __restrict__ counters, int start, int max_new) {
+  const int b = blockIdx.x;
+  const __nv_bfloat16* row = logits + (long long)b * ld;
+  float best = -INFINITY;
+  int arg = 0;
+  for (int j = threadIdx.x; j < V; j += blockDim.x) {
+    const float v = __bfloat162float(row[j]);
+    if (v > best) { best = v; arg = j; }
+  }
+  __shared__ float sv[32];
+  __shared__ int si[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, arg, o);
+    if (ov > best || (ov == best && oi < arg)) { best = ov; arg = oi; }
+  }
+  if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = best; si[threadIdx.x >> 5] = arg; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+      if (sv[w] > best || (sv[w] == best && si[w] < arg)) { best = sv[w]; arg = si[w]; }
+    idx_out[b] = arg;
+    const int slot = counters[0] - start;
+    if (tokens && slot >= 0 && slot < max_new) tokens[(long long)b * ld_tok + slot] = arg;
+  }
+}
+
+void decode_attn(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache, torch::Tensor len, int64_t H,
+                 int64_t D, double scale, torch::Tensor out) {
+  TORCH_CHECK(kcache.dim() == 3 && kcache.is_contiguous() && vcache.is_contiguous(), "caches [B, Tmax, H*D]");
+  TORCH_CHECK(D == 64 || D == 128, "head_dim 64 or 128");
+  const int B = (int)kcache.size(0), Tmax = (int)kcache.size(1);
+  TORCH_CHECK(kcache.size(2) == H * D && q.stride(-1) == 1 && out.stride(-1) == 1, "layout");
+  c10::cuda::CUDAGuard g(q.device());
+  const size_t smem = (size_t)Tmax * sizeof(float);
+  auto s = at::cuda::getCurrentCUDAStream();
+  auto* qp = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  auto* kp = reinterpret_cast<const __nv_bfloat16*>(kcache.data_ptr());
+  auto* vp = reinterpret_cast<const __nv_bfloat16*>(vcache.data_ptr());
+  auto* op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  if (D == 128) {
+    if (smem > 48 * 1024) C10_CUDA_CHECK(cudaFuncSetAttribute(decode_attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    decode_attn_kernel<128><<<B * H, kDecThreads, smem, s>>>(qp, q.stride(0), kp, vp, kcache.stride(1), kcache.stride(0),
+                                                              len.data_ptr<int>(), Tmax, op, out.stride(0), (int)H, (float)scale);
+  } else {
+    if (smem > 48 * 1024) C10_CUDA_CHECK(cudaFuncSetAttribute(decode_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    decode_attn_kernel<64><<<B * H, kDecThreads, smem, s>>>(qp, q.stride(0), kp, vp, kcache.stride(1), kcache.stride(0),
+                                                             len.data_ptr<int>(), Tmax, op, out.stride(0), (int)H, (float)scale);
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void kv_append(torch::Tensor k, torch::Tensor v, torch::Tensor kcache, torch::Tensor vcache, torch::Tensor pos) {
+  const int B = (int)kcache.size(0), C = (int)kcache.size(2);
+  TORCH_CHECK(C % 8 == 0 && k.stride(-1) == 1 && v.stride(-1) == 1, "rows");
+  c10::cuda::CUDAGuard g(k.device());
+  const long long n8 = (long long)B * C / 8;
+  kv_append_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(k.data_ptr()), k.stride(0), reinterpret_cast<const __nv_bfloat16*>(v.data_ptr()),
+      v.stride(0), reinterpret_cast<__nv_bfloat16*>(kcache.data_ptr()), reinterpret_cast<__nv_bfloat16*>(vcache.data_ptr()),
+      kcache.stride(1), kcache.stride(0), pos.data_ptr<int>(), (int)kcache.size(1), B, C);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void step_advance(torch::Tensor counters) {
+  step_advance_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(counters.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void argmax_rows(torch::Tensor logits, int64_t V, torch::Tensor idx_out, c10::optional<torch::Tensor> tokens,
+                 torch::Tensor counters, int64_t start) {
+  const int B = (int)logits.size(0);
+  int* tk = tokens.has_value() ? tokens->data_ptr<int>() : nullptr;
+  const long long ldt = tokens.has_value() ? tokens->stride(0) : 0;
+  const int max_new = tokens.has_value() ? (int)tokens->size(1) : 0;
+  argmax_rows_kernel<<<B, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), logits.stride(0), (int)V, idx_out.data_ptr<int>(), tk,
+      ldt, counters.data_ptr<int>(), (int)start, max_new);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace tfb

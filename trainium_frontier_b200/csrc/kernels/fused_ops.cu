@@ -345,13 +345,13 @@ template <int PPL>  // pairs per lane: D = 64 * PPL
 __global__ void rope_norm_fwd_kernel(__nv_bfloat16* __restrict__ buf, long long ld_tok, int head0, int nheads,
                                      const __nv_bfloat16* __restrict__ cosb, const __nv_bfloat16* __restrict__ sinb,
                                      int T, int pos_offset, float* __restrict__ rstd, int M,
-                                     __nv_bfloat16* __restrict__ out, long long ld_out) {
+                                     __nv_bfloat16* __restrict__ out, long long ld_out, const int* __restrict__ pos_ptr) {
   constexpr int D = 64 * PPL, HALF = D / 2;
   const long long w = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (w >= (long long)M * nheads) return;
   const int row = (int)(w / nheads), hh = (int)(w % nheads);
-  const int pos = row % T + pos_offset;
+  const int pos = row % T + (pos_ptr ? *pos_ptr : pos_offset);
   __nv_bfloat16* src = buf + (long long)row * ld_tok + (long long)(head0 + hh) * D;
   __nv_bfloat16* dst = out ? out + (long long)row * ld_out + (long long)(head0 + hh) * D : src;
   float y1[PPL], y2[PPL];
@@ -612,7 +612,7 @@ void embed_norm_bwd(torch::Tensor idx, torch::Tensor wte, torch::Tensor rstd, c1
 // buf: [M, ld_tok] bf16, heads [head0, head0+nheads) of width D are rotated+normed.
 void rope_norm_fwd(torch::Tensor buf, int64_t head0, int64_t nheads, int64_t D, torch::Tensor cos,
                    torch::Tensor sin, int64_t T, int64_t pos_offset, c10::optional<torch::Tensor> rstd,
-                   c10::optional<torch::Tensor> out) {
+                   c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> pos_t) {
   check_bf16_rows(buf, "buf");
   TORCH_CHECK(cos.is_contiguous() && sin.is_contiguous() && cos.scalar_type() == at::kBFloat16, "cos/sin bf16");
   const long long ld = buf.stride(-2);
@@ -628,9 +628,10 @@ void rope_norm_fwd(torch::Tensor buf, int64_t head0, int64_t nheads, int64_t D, 
   auto* b = reinterpret_cast<__nv_bfloat16*>(buf.data_ptr());
   auto* cp = reinterpret_cast<const __nv_bfloat16*>(cos.data_ptr());
   auto* sp = reinterpret_cast<const __nv_bfloat16*>(sin.data_ptr());
-  if (D == 128) rope_norm_fwd_kernel<2><<<grid, wpb * 32, 0, s>>>(b, ld, (int)head0, (int)nheads, cp, sp, (int)T, (int)pos_offset, r, M, o, ldo);
-  else if (D == 64) rope_norm_fwd_kernel<1><<<grid, wpb * 32, 0, s>>>(b, ld, (int)head0, (int)nheads, cp, sp, (int)T, (int)pos_offset, r, M, o, ldo);
-  else if (D == 256) rope_norm_fwd_kernel<4><<<grid, wpb * 32, 0, s>>>(b, ld, (int)head0, (int)nheads, cp, sp, (int)T, (int)pos_offset, r, M, o, ldo);
+  const int* pp = pos_t.has_value() ? pos_t->data_ptr<int>() : nullptr;
+  if (D == 128) rope_norm_fwd_kernel<2><<<grid, wpb * 32, 0, s>>>(b, ld, (int)head0, (int)nheads, cp, sp, (int)T, (int)pos_offset, r, M, o, ldo, pp);
+  else if (D == 64) rope_norm_fwd_kernel<1><<<grid, wpb * 32, 0, s>>>(b, ld, (int)head0, (int)nheads, cp, sp, (int)T, (int)pos_offset, r, M, o, ldo, pp);
+  else if (D == 256) rope_norm_fwd_kernel<4><<<grid, wpb * 32, 0, s>>>(b, ld, (int)head0, (int)nheads, cp, sp, (int)T, (int)pos_offset, r, M, o, ldo, pp);
   else TORCH_CHECK(false, "head_dim must be 64, 128 or 256");
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -21,7 +21,7 @@
 //   EPI_RELU2_BWD D = bf16(bf16(alpha * acc) * 2 relu(R - tau))   (R = h)
 //   EPI_F32       D(f32) = alpha * acc (+ D if beta)        weight gradients (fp32, split-K via
 //                                                          vector atomics into the gradient)
-// No TMA multicast is used anywhere; operands may live on this GPU only.
+// Every TMA load is a plain per-CTA load of this GPU's own memory.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>

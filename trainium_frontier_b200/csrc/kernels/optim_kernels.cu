@@ -88,4 +88,33 @@ void adamw_multi(std::vector<torch::Tensor> params, std::vector<torch::Tensor> g
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// Muon apply (the reference's last line of the Muon step), elementwise over a stack:
+//   t = bf16(bf16(lr) * g)          (0-dim fp32 lr times a bf16 g computes in bf16)
+//   w = w - (t + lrwd * w * [g * w >= 0])
+// Used by every rank on the gathered bf16 updates of distributed Muon.
+__global__ void muon_apply_kernel(float* __restrict__ w, const __nv_bfloat16* __restrict__ g, long long n,
+                                  const float* __restrict__ lr_ptr, const float* __restrict__ lrwd_ptr) {
+  const float lr_b = __bfloat162float(__float2bfloat16_rn(*lr_ptr));
+  const float lrwd = *lrwd_ptr;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const float gv = __bfloat162float(g[i]);
+    const float wv = w[i];
+    const float t = __bfloat162float(__float2bfloat16_rn(lr_b * gv));
+    const float mask = (gv * wv >= 0.f) ? 1.f : 0.f;  // bf16 g times fp32 w promotes to fp32
+    w[i] = wv - (t + lrwd * wv * mask);
+  }
+}
+
+void muon_apply(torch::Tensor w, torch::Tensor g, torch::Tensor lr, torch::Tensor lrwd) {
+  TORCH_CHECK(w.is_cuda() && w.scalar_type() == at::kFloat && w.is_contiguous(), "w fp32 contiguous");
+  TORCH_CHECK(g.scalar_type() == at::kBFloat16 && g.is_contiguous() && g.numel() == w.numel(), "g bf16 like w");
+  c10::cuda::CUDAGuard guard(w.device());
+  const long long n = w.numel();
+  const int blocks = (int)std::min<long long>((n + 255) / 256, 148 * 16);
+  muon_apply_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      w.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), n, lr.data_ptr<float>(),
+      lrwd.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 }  // namespace tfb

@@ -61,12 +61,17 @@ class _GradReady(Function):
 
 
 class ParamLayout:
-    def __init__(self, model, optimizer: MuonAdamW, device: torch.device, bucket_layers: int = 4):
+    def __init__(self, model, optimizer: MuonAdamW, device: torch.device, bucket_layers: int = 4,
+                 dist_world: int = 0):
         self.model = model
         self.device = device
         blocks = list(model.transformer.h)
         L = len(blocks)
         self.bucket_layers = max(1, bucket_layers)
+        self.dist_plans = None
+        if dist_world > 1:
+            self._build_dist(model, optimizer, device, dist_world)
+            return
         layer_of: dict[int, int] = {}
         for i, b in enumerate(blocks):
             for p in b.parameters():
@@ -137,6 +142,64 @@ class ParamLayout:
         self.mat_params = [p for p in ordered if p.dim() == 2 and p.shape[0] % 8 == 0 and p.shape[1] % 8 == 0]
         self._install_bf16_cache(model, device)
 
+    def _place(self, ordered_offsets, total, model, device):
+        """Allocate the flat buffers and re-point parameters at their offsets."""
+        self.total = total + ((-total) % 64)
+        self.data = torch.zeros(self.total, dtype=torch.float32, device=device)
+        self.grad = torch.zeros(self.total, dtype=torch.float32, device=device)
+        self.offsets = {}
+        frozen = [p for p in model.parameters() if not p.requires_grad]
+        with torch.no_grad():
+            for p, o in ordered_offsets:
+                n = p.numel()
+                self.offsets[id(p)] = (o, n)
+                view = self.data[o:o + n].view(p.shape)
+                view.copy_(p.detach().to(device=device, dtype=torch.float32))
+                p.data = view
+                p.grad = self.grad[o:o + n].view(p.shape)
+            for p in frozen:
+                p.data = p.data.to(device)
+        model.to(device)
+
+    def _build_dist(self, model, optimizer, device, world):
+        """Rank-major layout of every bucket (see parallel.dist_muon)."""
+        from .parallel.dist_muon import plan_buckets
+        muon_ids = {id(p) for g in optimizer.param_groups if g["kind"] == "muon" for p in g["params"]}
+        plans = plan_buckets(model, muon_ids, world, self.bucket_layers)
+        placed: list[tuple[torch.nn.Parameter, int]] = []
+        seen: set[int] = set()
+        off = 0
+        self.dist_bucket_range = []
+        self.buckets = []
+        for bi, plan in enumerate(plans):
+            start = off
+            for r in range(world):
+                local = 0
+                for u in plan.owners[r]:
+                    for p in u.params:
+                        placed.append((p, start + r * plan.seg_numel + local))
+                        seen.add(id(p))
+                        local += p.numel()
+            off = start + world * plan.seg_numel
+            self.dist_bucket_range.append((start, off))
+            self.buckets.append(Bucket(bi, start, off, plan.layers))
+        rest_start = off
+        for p in model.parameters():
+            if p.requires_grad and id(p) not in seen:
+                off += (-off) % 4
+                placed.append((p, off))
+                seen.add(id(p))
+                off += p.numel()
+        off += (-off) % 64
+        self.rest_range = (rest_start, off)
+        self.buckets.append(Bucket(len(self.buckets), rest_start, off, ()))
+        self.dist_plans = plans
+        self._place(placed, off, model, device)
+        self.params = [p for p, _ in placed]
+        self.first_layer_bucket = {b.layers[0]: b.index for b in self.buckets if b.layers}
+        self.mat_params = [p for p in self.params if p.dim() == 2 and p.shape[0] % 8 == 0 and p.shape[1] % 8 == 0]
+        self._install_bf16_cache(model, device)
+
     def _install_bf16_cache(self, model, device):
         from .ops import fused
         lin_ids = set()
@@ -201,11 +264,12 @@ class TrainEngine:
         self.grad_accum = grad_accum
         self.rank, self.world = world()
         if grad_sync == "auto":
-            grad_sync = "bucket" if self.world > 1 else "none"
+            grad_sync = "dist_muon" if self.world > 1 else "none"
         if self.world == 1:
             grad_sync = "none"
         self.grad_sync = grad_sync
-        self.layout = ParamLayout(model, optimizer, device, cfg.bucket_layers)
+        self.layout = ParamLayout(model, optimizer, device, cfg.bucket_layers,
+                                  dist_world=self.world if grad_sync == "dist_muon" else 0)
         self.comm_stream = torch.cuda.Stream(device) if device.type == "cuda" else None
         self._sync_now = False
         self.clip_params = None

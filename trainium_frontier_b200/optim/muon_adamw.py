@@ -71,6 +71,31 @@ def _muon_math(w, g, mb, second, mom, one_mom, lr, lrwd, ns_steps: int, red_dim:
     w.sub_(lr_g + lrwd * w * mask)
 
 
+@torch.no_grad()
+def muon_direction(opt, group, w, g, mb, second, to_bf16: bool) -> torch.Tensor:
+    """The Muon update direction of one stack (momentum, Nesterov, Newton-Schulz,
+    NorMuon scaling) without applying it -- the owner's half of distributed Muon."""
+    shape = w.shape[1:]
+    red_dim = -1 if shape[-2] >= shape[-1] else -2
+    ratio = max(1.0, shape[-2] / shape[-1]) ** 0.5
+    _lr, _lrwd, mom_t, one_mom_t, one_b2_t = opt._muon_scalars(group, w, ratio)
+    one_b2 = one_b2_t if group.get("beta2_tensor") else 1 - group["beta2"]
+    ns_steps = min(group["ns_steps"], len(POLAR_EXPRESS_COEFFS))
+    mb.lerp_(g, one_mom_t)
+    gn = torch.lerp(g, mb, mom_t)
+    x = gn.bfloat16() if to_bf16 else gn
+    x = x / (x.norm(dim=(-2, -1), keepdim=True) * 1.01 + 1e-6)
+    gq = ns.newton_schulz(x, ns_steps)
+    v_mean = gq.float().square().mean(dim=red_dim, keepdim=True)
+    red_size = gq.size(red_dim)
+    v_norm = (v_mean.sum(dim=(-2, -1), keepdim=True) * red_size).sqrt()
+    second.lerp_(v_mean, one_b2)
+    step_size = second.clamp_min(1e-10).rsqrt()
+    scaled = (v_mean * red_size) * step_size.square()
+    v_norm_new = scaled.sum(dim=(-2, -1), keepdim=True).sqrt()
+    return gq * (step_size * (v_norm / v_norm_new.clamp_min(1e-10))).to(gq.dtype)
+
+
 class MuonAdamW(torch.optim.Optimizer):
     def __init__(self, param_groups, muon_lr_fp32: bool = False, compute_dtype: torch.dtype | None = None):
         super().__init__(param_groups, defaults={})

@@ -1,0 +1,289 @@
+"""Distributed Muon: each rank orthogonalises only the matrices it owns.
+
+Per gradient bucket (a chunk of ``bucket_layers`` transformer blocks):
+
+1. ownership: the chunk's Muon matrices are grouped into units (c_q/c_k/c_v of a block
+   stay together so the fused QKV GEMM keeps reading one [3C, C] view; c_proj, c_fc and
+   the MLP projection are units of one) and assigned to ranks largest-first onto the
+   least-loaded rank.  The flat buffers of the chunk are laid out rank-major -- rank 0's
+   units, rank 1's units, ... each segment padded to the largest -- so
+2. one ``reduce_scatter`` (AVG) of the chunk delivers to every rank the averaged
+   gradient of exactly the matrices it owns; it is launched on a side stream the
+   moment backward leaves the chunk (overlapped with the rest of backward);
+3. the owner runs momentum / Nesterov / Newton-Schulz / NorMuon on its matrices and
+   writes the final bf16 update ``g`` (what the reference subtracts after scaling);
+4. one ``all_gather`` of the bf16 updates gives every rank every matrix's ``g``, and
+   every rank applies ``w -= lr g + lr wd w [g w >= 0]`` itself (identical inputs ->
+   identical fp32 masters on all ranks, at half the bytes of gathering fp32 weights).
+
+Everything outside the blocks' Muon matrices (embeddings, lm_head, scalars, gates)
+is all-reduced and updated with AdamW on every rank.  Gradient clipping uses the global
+norm of the averaged gradient (owner partial sums of squares + the all-reduced rest,
+one scalar all-reduce).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+import torch.distributed as dist
+
+from ..config import POLAR_EXPRESS_COEFFS
+
+
+@dataclass
+class Unit:
+    params: list          # parameters kept adjacent (same shape)
+    numel: int
+
+
+@dataclass
+class BucketPlan:
+    layers: tuple
+    owners: list = field(default_factory=list)       # per rank: list[Unit]
+    seg_numel: int = 0                                 # padded segment size (elements)
+
+
+def plan_buckets(model, muon_param_ids: set[int], world: int, bucket_layers: int) -> list[BucketPlan]:
+    blocks = list(model.transformer.h)
+    L = len(blocks)
+    plans = []
+    for c in range(math.ceil(L / bucket_layers)):
+        lay = tuple(range(c * bucket_layers, min(L, (c + 1) * bucket_layers)))
+        units: list[Unit] = []
+        for li in lay:
+            blk = blocks[li]
+            a = blk.attn
+            qkv = [a.c_q.weight, a.c_k.weight, a.c_v.weight]
+            if all(id(w) in muon_param_ids for w in qkv) and all(w.shape == qkv[0].shape for w in qkv):
+                units.append(Unit(qkv, sum(w.numel() for w in qkv)))
+                taken = {id(w) for w in qkv}
+            else:
+                taken = set()
+            for p in blk.parameters():
+                if id(p) in muon_param_ids and id(p) not in taken:
+                    units.append(Unit([p], p.numel()))
+        loads = [0] * world
+        owners: list[list[Unit]] = [[] for _ in range(world)]
+        for u in sorted(units, key=lambda u: -u.numel):
+            r = min(range(world), key=lambda i: loads[i])
+            owners[r].append(u)
+            loads[r] += u.numel
+        # inside a rank: group by shape so each (rank, shape) run is one contiguous stack
+        for r in range(world):
+            owners[r].sort(key=lambda u: (tuple(u.params[0].shape), -len(u.params)))
+        seg = max(loads) if loads else 0
+        seg += (-seg) % 64
+        plans.append(BucketPlan(lay, owners, seg))
+    return plans
+
+
+class DistMuon:
+    """Owner-sharded Muon + DP sync for a TrainEngine whose layout follows ``plans``."""
+
+    def __init__(self, engine, optimizer):
+        self.engine = engine
+        self.opt = optimizer
+        self.rank, self.world = dist.get_rank(), dist.get_world_size()
+        lay = engine.layout
+        self.plans = lay.dist_plans
+        dev = lay.grad.device
+        self.device = dev
+        # per-bucket receive (fp32 averaged owned grads) and gather (bf16 updates) buffers
+        self.recv = [torch.zeros(p.seg_numel, dtype=torch.float32, device=dev) for p in self.plans]
+        self.gath = [torch.zeros(p.seg_numel * self.world, dtype=torch.bfloat16, device=dev) for p in self.plans]
+        self.works = [None] * len(self.plans)
+        self.rest_work = None
+        self.comm = engine.comm_stream
+        # optimizer group of every Muon parameter
+        self.group_of: dict[int, dict] = {}
+        for g in optimizer.param_groups:
+            if g["kind"] == "muon":
+                for i, p in enumerate(g["params"]):
+                    self.group_of[id(p)] = g
+        # owner state: momentum / second moment per owned matrix
+        self.state: dict[int, dict] = {}
+        self.clip_coef = None
+
+    # ------------------------------------------------------------------ grads
+    def _bucket_view(self, b: int) -> torch.Tensor:
+        s, e = self.engine.layout.dist_bucket_range[b]
+        return self.engine.layout.grad[s:e]
+
+    def on_bucket_ready(self, bucket) -> None:
+        b = bucket.index
+        if b >= len(self.plans):
+            return
+        self._launch_rs(b)
+
+    def _launch_rs(self, b: int) -> None:
+        if self.works[b] is not None:
+            return
+        src = self._bucket_view(b)
+        if self.comm is not None:
+            self.comm.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(self.comm):
+                self.works[b] = dist.reduce_scatter_tensor(self.recv[b], src, op=dist.ReduceOp.AVG, async_op=True)
+        else:
+            self.works[b] = dist.reduce_scatter_tensor(self.recv[b], src, op=dist.ReduceOp.AVG, async_op=True)
+
+    def finish_grad_sync(self) -> None:
+        lay = self.engine.layout
+        for b in range(len(self.plans)):
+            self._launch_rs(b)
+        rs, re_ = lay.rest_range
+        rest = lay.grad[rs:re_]
+        if self.comm is not None:
+            self.comm.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(self.comm):
+                self.rest_work = dist.all_reduce(rest, op=dist.ReduceOp.AVG, async_op=True)
+        else:
+            self.rest_work = dist.all_reduce(rest, op=dist.ReduceOp.AVG, async_op=True)
+        for b in range(len(self.plans)):
+            self.works[b].wait()
+            self.works[b] = None
+        self.rest_work.wait()
+        self.rest_work = None
+        if self.comm is not None:
+            torch.cuda.current_stream(self.device).wait_stream(self.comm)
+        # global norm of the averaged gradient
+        clip = self.engine.cfg.grad_clip
+        self.clip_coef = None
+        if clip > 0:
+            sq = torch.zeros(1, dtype=torch.float32, device=self.device)
+            for b in range(len(self.plans)):
+                sq += self.recv[b].square().sum()
+            sq_all = sq.clone()
+            dist.all_reduce(sq_all, op=dist.ReduceOp.SUM)
+            total = (sq_all + rest.square().sum()).sqrt()
+            coef = torch.clamp(clip / (total + 1e-6), max=1.0)
+            rest.mul_(coef)
+            self.clip_coef = coef
+
+    # ------------------------------------------------------------------ step
+    def _owned_runs(self, b: int):
+        """(shape, [params], offset in the rank segment) runs of this rank's matrices."""
+        runs = []
+        off = 0
+        cur_shape, cur, cur_off = None, [], 0
+        for u in self.plans[b].owners[self.rank]:
+            for p in u.params:
+                shp = tuple(p.shape)
+                if shp != cur_shape:
+                    if cur:
+                        runs.append((cur_shape, cur, cur_off))
+                    cur_shape, cur, cur_off = shp, [], off
+                cur.append(p)
+                off += p.numel()
+        if cur:
+            runs.append((cur_shape, cur, cur_off))
+        return runs
+
+    def _all_runs(self, b: int):
+        """Per rank, (shape, [params], offset) runs -- for applying gathered updates."""
+        out = []
+        for r in range(self.world):
+            off = 0
+            cur_shape, cur, cur_off = None, [], 0
+            runs = []
+            for u in self.plans[b].owners[r]:
+                for p in u.params:
+                    shp = tuple(p.shape)
+                    if shp != cur_shape:
+                        if cur:
+                            runs.append((cur_shape, cur, cur_off))
+                        cur_shape, cur, cur_off = shp, [], off
+                    cur.append(p)
+                    off += p.numel()
+            if cur:
+                runs.append((cur_shape, cur, cur_off))
+            out.append(runs)
+        return out
+
+    @torch.no_grad()
+    def step(self, update_adamw: bool = True) -> None:
+        from ..optim.muon_adamw import muon_direction
+        lay = self.engine.layout
+        opt = self.opt
+        to_bf16 = lay.grad.is_cuda
+        # AdamW / RMSProp groups: redundant on every rank (grads already averaged)
+        for g in opt.param_groups:
+            if g["kind"] == "adamw" and update_adamw:
+                opt._adamw_step(g)
+            elif g["kind"] == "rmsprop" and update_adamw:
+                opt._rmsprop_step(g)
+        works = []
+        for b in range(len(self.plans)):
+            seg = self.recv[b]
+            upd = torch.zeros(self.plans[b].seg_numel, dtype=torch.bfloat16, device=self.device)
+            for shape, params, off in self._owned_runs(b):
+                K = len(params)
+                n = K * params[0].numel()
+                grp = self.group_of[id(params[0])]
+                g = seg[off:off + n].view(K, *shape)
+                if self.clip_coef is not None:
+                    g = g * self.clip_coef
+                w = torch.stack([p.detach() for p in params]) if not _adjacent(params) else _stack_view(params)
+                st = self._state(params, grp)
+                gq = muon_direction(opt, grp, w, g, st["mb"], st["second"], to_bf16)
+                upd[off:off + n].copy_(gq.reshape(-1).to(torch.bfloat16))
+            out = self.gath[b]
+            if self.comm is not None:
+                self.comm.wait_stream(torch.cuda.current_stream(self.device))
+                with torch.cuda.stream(self.comm):
+                    works.append(dist.all_gather_into_tensor(out, upd, async_op=True))
+                    upd.record_stream(self.comm)
+            else:
+                works.append(dist.all_gather_into_tensor(out, upd, async_op=True))
+        for b in range(len(self.plans)):
+            works[b].wait()
+            if self.comm is not None:
+                torch.cuda.current_stream(self.device).wait_stream(self.comm)
+            S = self.plans[b].seg_numel
+            for r, runs in enumerate(self._all_runs(b)):
+                for shape, params, off in runs:
+                    K = len(params)
+                    n = K * params[0].numel()
+                    grp = self.group_of[id(params[0])]
+                    gq = self.gath[b][r * S + off:r * S + off + n].view(K, *shape)
+                    w = _stack_view(params)
+                    _apply_update(opt, grp, w, gq, params)
+
+    def _state(self, params, grp):
+        key = id(params[0])
+        st = self.state.get(key)
+        if st is None:
+            K = len(params)
+            shape = params[0].shape
+            red_dim = -1 if shape[-2] >= shape[-1] else -2
+            sshape = (K, shape[-2], 1) if red_dim == -1 else (K, 1, shape[-1])
+            st = {"mb": torch.zeros(K, *shape, dtype=torch.float32, device=self.device),
+                  "second": torch.zeros(sshape, dtype=torch.float32, device=self.device)}
+            self.state[key] = st
+        return st
+
+
+def _adjacent(params) -> bool:
+    from ..optim.muon_adamw import _stacked_view
+    return _stacked_view(list(params)) is not None
+
+
+def _stack_view(params):
+    from ..optim.muon_adamw import _stacked_view
+    v = _stacked_view(list(params))
+    assert v is not None, "owned run is not contiguous"
+    return v
+
+
+def _apply_update(opt, grp, w, gq, params) -> None:
+    """w -= lr g + lr wd w [g w >= 0]  (the reference's apply, lr cast to g's dtype)."""
+    shape = params[0].shape
+    ratio = max(1.0, shape[-2] / shape[-1]) ** 0.5
+    lr_t, lrwd_t, _, _, _ = opt._muon_scalars(grp, params[0], ratio)
+    if w.is_cuda:
+        from ..ops.optim_kernels import muon_apply
+        muon_apply(w, gq, lr_t, lrwd_t, params)
+        return
+    mask = (gq * w) >= 0
+    w.sub_(lr_t.to(gq.dtype) * gq + lrwd_t * w * mask)
