@@ -298,7 +298,7 @@ def run_reference(args) -> dict:
     return {
         "metric": METRIC, "value": tok / (ms / 1000.0), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16 (reference code path; see notes)",
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp32 blocks (the reference's shape-[1] fp32 lambdas promote its residual stream to fp32 on CUDA, so every block matmul runs in fp32; embeddings / rotary tables bf16)",
         "data": "synthetic (seeded Zipf(1.1) token stream; random-init weights)",
         "config": dict(CONFIG, parallelism=f"dp{world}", micro_batch_rows=rows_micro, grad_accum=grad_accum,
                        path="reference train.py: torch.compile(inductor) + SDPA + eager Muon + per-param all_reduce"),

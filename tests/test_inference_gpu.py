@@ -1,0 +1,55 @@
+"""KV-cache greedy decoding (prefill + graph-captured decode) vs full recomputation."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _model(dev, depth=2, n_embd=256, head_dim=128, seq=512):
+    from trainium_frontier_b200.config import preset
+    from trainium_frontier_b200.models.gpt import GPT
+    cfg = preset("tiny", depth=depth, n_embd=n_embd, head_dim=head_dim, seq_len=seq)
+    torch.manual_seed(5)
+    m = GPT(cfg.model_config(), cfg)
+    m.init_weights()
+    with torch.no_grad():  # a non-degenerate random model (zero-init projections otherwise)
+        for b in m.transformer.h:
+            b.mlp.c_proj.weight.normal_(0, 0.02)
+        m.lm_head.weight.normal_(0, 0.05)
+    m.set_compute_dtype(torch.bfloat16)
+    return m.to(dev).eval()
+
+
+@pytest.mark.parametrize("use_graph", [False, True])
+def test_cached_decode_matches_recompute(cuda_device, use_graph):
+    from trainium_frontier_b200.inference.generate import Generator, generate_reference
+    from trainium_frontier_b200.ops._ext import check_errors
+    m = _model(cuda_device)
+    B, T, N = 4, 128, 16
+    prompts = torch.randint(1, 8192, (B, T), device=cuda_device, dtype=torch.int32)
+    ref = generate_reference(m, prompts, N)
+    gen = Generator(m, B, T + N + 8)
+    out = gen.generate(prompts, N, use_graph=use_graph)
+    check_errors()
+    agree = (out.long() == ref.long()).float().mean().item()
+    # bf16 logits of two different kernel paths may break near-ties differently late in the
+    # sequence; the first tokens must agree exactly
+    assert torch.equal(out[:, :4].long(), ref[:, :4].long())
+    assert agree > 0.9, agree
+
+
+def test_decode_attention_kernel(cuda_device):
+    from trainium_frontier_b200.ops._ext import C
+    torch.manual_seed(0)
+    B, Tm, H, D, L = 3, 300, 4, 128, 257
+    q = torch.randn(B, H * D, device=cuda_device).to(torch.bfloat16)
+    kc = torch.randn(B, Tm, H * D, device=cuda_device).to(torch.bfloat16)
+    vc = torch.randn(B, Tm, H * D, device=cuda_device).to(torch.bfloat16)
+    ln = torch.tensor([L], dtype=torch.int32, device=cuda_device)
+    out = torch.empty(B, H * D, dtype=torch.bfloat16, device=cuda_device)
+    C().decode_attn(q, kc, vc, ln, H, D, D ** -0.5, out)
+    qf = q.float().view(B, H, 1, D)
+    kf = kc[:, :L].float().view(B, L, H, D).transpose(1, 2)
+    vf = vc[:, :L].float().view(B, L, H, D).transpose(1, 2)
+    ref = torch.softmax(qf @ kf.transpose(-1, -2) * D ** -0.5, -1) @ vf
+    assert (out.float().view(B, H, D) - ref.squeeze(2)).abs().max().item() < 2e-2
