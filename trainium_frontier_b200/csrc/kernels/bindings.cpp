@@ -39,6 +39,12 @@ void fa_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, 
             int64_t B, int64_t T, int64_t H, int64_t D, double scale, bool causal, torch::Tensor dq_acc,
             torch::Tensor dq_out, torch::Tensor dk, torch::Tensor dv, torch::Tensor dvec, torch::Tensor err);
 void muon_apply(torch::Tensor w, torch::Tensor g, torch::Tensor lr, torch::Tensor lrwd);
+void symm_barrier(std::vector<int64_t> pad_ptrs, int64_t rank, int64_t epoch, torch::Tensor err);
+void symm_rs(std::vector<int64_t> peer_ptrs, int64_t src_off, int64_t n, torch::Tensor out, double inv,
+             c10::optional<torch::Tensor> sumsq, int64_t mc_ptr);
+void muon_pre(torch::Tensor g, torch::Tensor mb, torch::Tensor x, c10::optional<torch::Tensor> coef, torch::Tensor mom,
+              torch::Tensor one_mom, torch::Tensor fro);
+void symm_ag_apply(std::vector<int64_t> upd_ptrs, torch::Tensor runs_i64);
 }  // namespace tfb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -65,6 +71,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("softcap_ce", &tfb::softcap_ce);
   m.def("adamw_multi", &tfb::adamw_multi);
   m.def("muon_apply", &tfb::muon_apply);
+  m.def("symm_barrier", &tfb::symm_barrier);
+  m.def("symm_rs", &tfb::symm_rs);
+  m.def("muon_pre", &tfb::muon_pre);
+  m.def("symm_ag_apply", &tfb::symm_ag_apply);
   m.def("fa_fwd", &tfb::fa_fwd, "tcgen05 causal flash attention forward");
   m.def("fa_bwd", &tfb::fa_bwd, "tcgen05 causal flash attention backward");
 }

@@ -178,12 +178,28 @@ __global__ void symm_ag_apply_kernel(PeerBf16 upd, const ApplyRun* __restrict__ 
   const __nv_bfloat16* src = upd.p[r.owner] + r.src_off;
   const float lr_b = __bfloat162float(__float2bfloat16_rn(*r.lr));
   const float lrwd = *r.lrwd;
-  for (long long i = start + threadIdx.x * 8; i < end; i += blockDim.x * 8) {
-    const uint4 gu = *reinterpret_cast<const uint4*>(src + i);
-    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gu);
-    float4 w0 = *reinterpret_cast<const float4*>(r.w + i);
-    float4 w1 = *reinterpret_cast<const float4*>(r.w + i + 4);
-    float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+  // Two 8-element groups per thread, all loads issued before any math (memory-level
+  // parallelism for the peer loads, which see NVLink latency).
+  constexpr int kPer = kApplyChunk / 2;
+  uint4 gu[2];
+  float4 wl[2][2];
+  bool ok[2];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const long long i = start + u * kPer + threadIdx.x * 8;
+    ok[u] = i < end;
+    if (ok[u]) {
+      gu[u] = *reinterpret_cast<const uint4*>(src + i);
+      wl[u][0] = *reinterpret_cast<const float4*>(r.w + i);
+      wl[u][1] = *reinterpret_cast<const float4*>(r.w + i + 4);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    if (!ok[u]) continue;
+    const long long i = start + u * kPer + threadIdx.x * 8;
+    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gu[u]);
+    float wv[8] = {wl[u][0].x, wl[u][0].y, wl[u][0].z, wl[u][0].w, wl[u][1].x, wl[u][1].y, wl[u][1].z, wl[u][1].w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float2 gf = __bfloat1622float2(g2[j]);
@@ -199,12 +215,12 @@ __global__ void symm_ag_apply_kernel(PeerBf16 upd, const ApplyRun* __restrict__ 
     *reinterpret_cast<float4*>(r.w + i) = make_float4(wv[0], wv[1], wv[2], wv[3]);
     *reinterpret_cast<float4*>(r.w + i + 4) = make_float4(wv[4], wv[5], wv[6], wv[7]);
     if (r.w16) {
-      uint4 u;
-      u.x = pack_bf16x2(wv[0], wv[1]);
-      u.y = pack_bf16x2(wv[2], wv[3]);
-      u.z = pack_bf16x2(wv[4], wv[5]);
-      u.w = pack_bf16x2(wv[6], wv[7]);
-      *reinterpret_cast<uint4*>(r.w16 + i) = u;
+      uint4 q;
+      q.x = pack_bf16x2(wv[0], wv[1]);
+      q.y = pack_bf16x2(wv[2], wv[3]);
+      q.z = pack_bf16x2(wv[4], wv[5]);
+      q.w = pack_bf16x2(wv[6], wv[7]);
+      *reinterpret_cast<uint4*>(r.w16 + i) = q;
     }
   }
 }
@@ -255,28 +271,55 @@ void muon_pre(torch::Tensor g, torch::Tensor mb, torch::Tensor x, c10::optional<
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-// runs: int64 [nruns, 8] = owner, src_off, w_ptr, w16_ptr, n, lr_ptr, lrwd_ptr, unused
+// runs: int64 [nruns, 8] = owner, src_off, w_ptr, w16_ptr, n, lr_ptr, lrwd_ptr, unused.
+// Runs are cut into pieces of kApplyPiece elements and the pieces are dealt round-robin
+// over owners, so at every point of the grid the blocks in flight read a balanced mix of
+// local and peer updates (the local half is HBM-bound, the peer half NVLink-bound; run
+// back to back the two phases would not overlap).
+constexpr long long kApplyPiece = 64LL * kApplyChunk;
+
 void symm_ag_apply(std::vector<int64_t> upd_ptrs, torch::Tensor runs_i64) {
   TORCH_CHECK(runs_i64.scalar_type() == at::kLong && runs_i64.dim() == 2 && runs_i64.size(1) == 8 &&
                   runs_i64.device().is_cpu(),
               "runs table int64 [n, 8] on the host");
   auto upd = peers_of<PeerBf16, const __nv_bfloat16*>(upd_ptrs);
   const int nr = (int)runs_i64.size(0);
-  std::vector<ApplyRun> host(nr);
   const int64_t* t = runs_i64.data_ptr<int64_t>();
-  long long blocks = 0;
+  std::vector<std::vector<ApplyRun>> by_owner(kMaxRanks);
   for (int i = 0; i < nr; ++i) {
     const int64_t* r = t + i * 8;
     TORCH_CHECK(r[4] % 8 == 0 && r[1] % 8 == 0, "runs must be multiples of 8 elements");
-    host[i] = ApplyRun{(int)r[0], r[1], reinterpret_cast<float*>(r[2]), reinterpret_cast<__nv_bfloat16*>(r[3]), r[4],
-                       reinterpret_cast<const float*>(r[5]), reinterpret_cast<const float*>(r[6]), blocks};
-    blocks += (r[4] + kApplyChunk - 1) / kApplyChunk;
+    TORCH_CHECK(r[0] >= 0 && r[0] < (int64_t)upd_ptrs.size(), "owner rank out of range");
+    for (long long o = 0; o < r[4]; o += kApplyPiece) {
+      const long long len = std::min<long long>(kApplyPiece, r[4] - o);
+      by_owner[r[0]].push_back(ApplyRun{(int)r[0], r[1] + o, reinterpret_cast<float*>(r[2]) + o,
+                                        r[3] ? reinterpret_cast<__nv_bfloat16*>(r[3]) + o : nullptr, len,
+                                        reinterpret_cast<const float*>(r[5]), reinterpret_cast<const float*>(r[6]), 0});
+    }
   }
-  auto tab = torch::empty({(long long)(nr * sizeof(ApplyRun))}, torch::dtype(torch::kUInt8).pinned_memory(true));
-  memcpy(tab.data_ptr(), host.data(), nr * sizeof(ApplyRun));
+  std::vector<ApplyRun> host;
+  long long blocks = 0;
+  for (size_t k = 0;; ++k) {
+    bool any = false;
+    for (auto& v : by_owner) {
+      if (k < v.size()) {
+        any = true;
+        ApplyRun a = v[k];
+        a.blk0 = blocks;
+        blocks += (a.n + kApplyChunk - 1) / kApplyChunk;
+        host.push_back(a);
+      }
+    }
+    if (!any) break;
+  }
+  if (host.empty()) return;
+  const size_t bytes = host.size() * sizeof(ApplyRun);
+  auto tab = torch::empty({(long long)bytes}, torch::dtype(torch::kUInt8).pinned_memory(true));
+  memcpy(tab.data_ptr(), host.data(), bytes);
   auto s = at::cuda::getCurrentCUDAStream();
   auto dtab = tab.to(torch::Device(torch::kCUDA, c10::cuda::current_device()), /*non_blocking=*/true);
-  symm_ag_apply_kernel<<<(unsigned)blocks, 256, 0, s>>>(upd, reinterpret_cast<const ApplyRun*>(dtab.data_ptr()), nr);
+  symm_ag_apply_kernel<<<(unsigned)blocks, 256, 0, s>>>(upd, reinterpret_cast<const ApplyRun*>(dtab.data_ptr()),
+                                                        (int)host.size());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

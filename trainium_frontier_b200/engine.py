@@ -62,9 +62,10 @@ class _GradReady(Function):
 
 class ParamLayout:
     def __init__(self, model, optimizer: MuonAdamW, device: torch.device, bucket_layers: int = 4,
-                 dist_world: int = 0):
+                 dist_world: int = 0, symm: bool = False):
         self.model = model
         self.device = device
+        self.symm = symm
         blocks = list(model.transformer.h)
         L = len(blocks)
         self.bucket_layers = max(1, bucket_layers)
@@ -143,10 +144,18 @@ class ParamLayout:
         self._install_bf16_cache(model, device)
 
     def _place(self, ordered_offsets, total, model, device):
-        """Allocate the flat buffers and re-point parameters at their offsets."""
+        """Allocate the flat buffers and re-point parameters at their offsets.  With
+        ``symm`` the gradient buffer is a symmetric allocation peers can read."""
         self.total = total + ((-total) % 64)
         self.data = torch.zeros(self.total, dtype=torch.float32, device=device)
-        self.grad = torch.zeros(self.total, dtype=torch.float32, device=device)
+        self.grad_handle = None
+        if self.symm:
+            import torch.distributed._symmetric_memory as symm_mem
+            self.grad = symm_mem.empty(self.total, dtype=torch.float32, device=device)
+            self.grad.zero_()
+            self.grad_handle = symm_mem.rendezvous(self.grad, dist.group.WORLD)
+        else:
+            self.grad = torch.zeros(self.total, dtype=torch.float32, device=device)
         self.offsets = {}
         frozen = [p for p in model.parameters() if not p.requires_grad]
         with torch.no_grad():
@@ -265,18 +274,21 @@ class TrainEngine:
         self.rank, self.world = world()
         if grad_sync == "auto":
             grad_sync = "dist_muon" if self.world > 1 else "none"
+        if grad_sync == "fused" and (device.type != "cuda" or self.world < 2):
+            grad_sync = "dist_muon" if self.world > 1 else "none"
         if self.world == 1:
             grad_sync = "none"
         self.grad_sync = grad_sync
         self.layout = ParamLayout(model, optimizer, device, cfg.bucket_layers,
-                                  dist_world=self.world if grad_sync == "dist_muon" else 0)
+                                  dist_world=self.world if grad_sync in ("dist_muon", "fused") else 0,
+                                  symm=grad_sync == "fused")
         self.comm_stream = torch.cuda.Stream(device) if device.type == "cuda" else None
         self._sync_now = False
         self.clip_params = None
         self.dist_muon = None
-        if grad_sync == "dist_muon":
+        if grad_sync in ("dist_muon", "fused"):
             from .parallel.dist_muon import DistMuon
-            self.dist_muon = DistMuon(self, optimizer)
+            self.dist_muon = DistMuon(self, optimizer, fused=grad_sync == "fused")
         self._install_markers()
 
     # ------------------------------------------------------------------ bucket hooks
@@ -288,7 +300,7 @@ class TrainEngine:
                 blk._tfb_marker_hook.remove()
 
             def pre_hook(module, args, kwargs, _b=bidx):
-                if not torch.is_grad_enabled() or engine.grad_sync not in ("bucket", "dist_muon"):
+                if not torch.is_grad_enabled() or engine.grad_sync not in ("bucket", "dist_muon", "fused"):
                     return None
                 x = args[0]
                 return (_GradReady.apply(x, engine, _b),) + tuple(args[1:]), kwargs
@@ -304,7 +316,7 @@ class TrainEngine:
         b.ready = True
         if self.grad_sync == "bucket" and self.cfg.clip_order == "global":
             self._launch_allreduce(b)
-        elif self.grad_sync == "dist_muon":
+        elif self.grad_sync in ("dist_muon", "fused"):
             self.dist_muon.on_bucket_ready(b)
 
     def _launch_allreduce(self, b: Bucket) -> None:
@@ -331,7 +343,7 @@ class TrainEngine:
                     b.work = None
             if self.comm_stream is not None:
                 torch.cuda.current_stream(self.device).wait_stream(self.comm_stream)
-        elif self.grad_sync == "dist_muon":
+        elif self.grad_sync in ("dist_muon", "fused"):
             self.dist_muon.finish_grad_sync()
 
     # ------------------------------------------------------------------ step
@@ -353,8 +365,11 @@ class TrainEngine:
         inv = 1.0 / len(batches)
         total = torch.zeros((), dtype=torch.float32, device=self.device)
         local_clip = self.cfg.clip_order == "local" and self.cfg.grad_clip > 0
+        if self.dist_muon is not None:
+            self.dist_muon.begin_step()
         for i, (x, y) in enumerate(batches):
-            self._sync_now = (i == len(batches) - 1) and self.grad_sync in ("bucket", "dist_muon") and not local_clip
+            self._sync_now = (i == len(batches) - 1) and self.grad_sync in ("bucket", "dist_muon", "fused") \
+                and not local_clip
             loss = self.model(x, y)
             (loss * (inv * loss_scale)).backward()
             total += loss.detach()

@@ -80,11 +80,19 @@ def plan_buckets(model, muon_param_ids: set[int], world: int, bucket_layers: int
 
 
 class DistMuon:
-    """Owner-sharded Muon + DP sync for a TrainEngine whose layout follows ``plans``."""
+    """Owner-sharded Muon + DP sync for a TrainEngine whose layout follows ``plans``.
 
-    def __init__(self, engine, optimizer):
+    ``fused=False``: NCCL reduce_scatter / all_gather (the baseline collectives).
+    ``fused=True``:  the buffers are symmetric allocations and the collectives are this
+    framework's own kernels over NVLink peer memory (``csrc/kernels/symm_sm100.cu``):
+    a bounded device barrier per bucket, a P2P (or NVSwitch multimem) reduce-scatter
+    that also produces the norm partial, a fused momentum / Nesterov / bf16 / Frobenius
+    prologue, and a gather + apply kernel writing fp32 masters and bf16 caches."""
+
+    def __init__(self, engine, optimizer, fused: bool = False):
         self.engine = engine
         self.opt = optimizer
+        self.fused = fused
         self.rank, self.world = dist.get_rank(), dist.get_world_size()
         lay = engine.layout
         self.plans = lay.dist_plans
@@ -105,6 +113,48 @@ class DistMuon:
         # owner state: momentum / second moment per owned matrix
         self.state: dict[int, dict] = {}
         self.clip_coef = None
+        self.sumsq = torch.zeros(1, dtype=torch.float32, device=dev)
+        self.goff = []
+        off = 0
+        for p in self.plans:
+            self.goff.append(off)
+            off += self.world * p.seg_numel
+        if fused:
+            self._init_symm(off)
+
+    # ------------------------------------------------------------------ symmetric memory
+    def _init_symm(self, upd_numel: int) -> None:
+        import os
+        import torch.distributed._symmetric_memory as symm_mem
+        from ..ops._ext import C, err_word
+        self.C = C()
+        self.err = err_word(self.device)
+        lay = self.engine.layout
+        h = lay.grad_handle
+        base = h.buffer_ptrs[self.rank]
+        goff_bytes = lay.grad.data_ptr() - base
+        self.grad_peers = [int(p) + goff_bytes for p in h.buffer_ptrs]
+        self.pads = [int(p) for p in h.signal_pad_ptrs]
+        use_nvls = os.environ.get("TFB_NVLS", "0") == "1" and os.environ.get("NCCL_NVLS_ENABLE", "1") != "0"
+        mc = int(getattr(h, "multicast_ptr", 0) or 0)
+        self.grad_mc = (mc + goff_bytes) if (use_nvls and mc) else 0
+        self.upd = symm_mem.empty(max(upd_numel, 64), dtype=torch.bfloat16, device=self.device)
+        self.upd.zero_()
+        self.upd_handle = symm_mem.rendezvous(self.upd, dist.group.WORLD)
+        ubase = self.upd_handle.buffer_ptrs[self.rank]
+        uoff = self.upd.data_ptr() - ubase
+        self.upd_peers = [int(p) + uoff for p in self.upd_handle.buffer_ptrs]
+        self.epoch = 0
+        self._runs_tables = {}
+        torch.cuda.synchronize(self.device)
+        dist.barrier()
+
+    def _barrier(self) -> None:
+        self.epoch += 1
+        self.C.symm_barrier(self.pads, self.rank, self.epoch, self.err)
+
+    def begin_step(self) -> None:
+        self.sumsq.zero_()
 
     # ------------------------------------------------------------------ grads
     def _bucket_view(self, b: int) -> torch.Tensor:
@@ -119,6 +169,17 @@ class DistMuon:
 
     def _launch_rs(self, b: int) -> None:
         if self.works[b] is not None:
+            return
+        if self.fused:
+            s0, _ = self.engine.layout.dist_bucket_range[b]
+            S = self.plans[b].seg_numel
+            stream = self.comm if self.comm is not None else torch.cuda.current_stream(self.device)
+            stream.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(stream):
+                self._barrier()   # every rank has finished this bucket's backward
+                self.C.symm_rs(self.grad_peers, s0 + self.rank * S, S, self.recv[b], 1.0 / self.world,
+                               self.sumsq, self.grad_mc)
+            self.works[b] = "fused"
             return
         src = self._bucket_view(b)
         if self.comm is not None:
@@ -141,7 +202,8 @@ class DistMuon:
         else:
             self.rest_work = dist.all_reduce(rest, op=dist.ReduceOp.AVG, async_op=True)
         for b in range(len(self.plans)):
-            self.works[b].wait()
+            if self.works[b] != "fused":
+                self.works[b].wait()
             self.works[b] = None
         self.rest_work.wait()
         self.rest_work = None
@@ -151,9 +213,12 @@ class DistMuon:
         clip = self.engine.cfg.grad_clip
         self.clip_coef = None
         if clip > 0:
-            sq = torch.zeros(1, dtype=torch.float32, device=self.device)
-            for b in range(len(self.plans)):
-                sq += self.recv[b].square().sum()
+            if self.fused:
+                sq = self.sumsq
+            else:
+                sq = torch.zeros(1, dtype=torch.float32, device=self.device)
+                for b in range(len(self.plans)):
+                    sq += self.recv[b].square().sum()
             sq_all = sq.clone()
             dist.all_reduce(sq_all, op=dist.ReduceOp.SUM)
             total = (sq_all + rest.square().sum()).sqrt()
@@ -203,6 +268,8 @@ class DistMuon:
 
     @torch.no_grad()
     def step(self, update_adamw: bool = True) -> None:
+        if self.fused:
+            return self._step_fused(update_adamw)
         from ..optim.muon_adamw import muon_direction
         lay = self.engine.layout
         opt = self.opt
@@ -287,3 +354,82 @@ def _apply_update(opt, grp, w, gq, params) -> None:
         return
     mask = (gq * w) >= 0
     w.sub_(lr_t.to(gq.dtype) * gq + lrwd_t * w * mask)
+
+
+def _fused_owner_direction(dm, grp, g, st, coef):
+    """Owner half on the GPU: fused prologue kernel, Newton-Schulz, NorMuon scaling."""
+    from ..ops import newton_schulz as ns
+    opt = dm.opt
+    K = g.shape[0]
+    shape = g.shape[1:]
+    red_dim = -1 if shape[-2] >= shape[-1] else -2
+    ratio = max(1.0, shape[-2] / shape[-1]) ** 0.5
+    _lr, _lrwd, mom_t, one_mom_t, _ = opt._muon_scalars(grp, g, ratio)
+    x = torch.empty(g.shape, dtype=torch.bfloat16, device=g.device)
+    fro = torch.zeros(K, dtype=torch.float32, device=g.device)
+    dm.C.muon_pre(g, st["mb"], x, coef, mom_t.reshape(1), one_mom_t.reshape(1), fro)
+    x.mul_((1.0 / (fro.sqrt() * 1.01 + 1e-6)).to(torch.bfloat16).view(K, 1, 1))
+    gq = ns.newton_schulz(x, min(grp["ns_steps"], len(POLAR_EXPRESS_COEFFS)))
+    v_mean = gq.float().square().mean(dim=red_dim, keepdim=True)
+    red_size = gq.size(red_dim)
+    v_norm = (v_mean.sum(dim=(-2, -1), keepdim=True) * red_size).sqrt()
+    st["second"].lerp_(v_mean, 1 - grp["beta2"])
+    step_size = st["second"].clamp_min(1e-10).rsqrt()
+    scaled = (v_mean * red_size) * step_size.square()
+    v_norm_new = scaled.sum(dim=(-2, -1), keepdim=True).sqrt()
+    return gq * (step_size * (v_norm / v_norm_new.clamp_min(1e-10))).to(gq.dtype)
+
+
+def _step_fused(self, update_adamw: bool = True) -> None:
+    opt = self.opt
+    for g in opt.param_groups:
+        if g["kind"] == "adamw" and update_adamw:
+            opt._adamw_step(g)
+        elif g["kind"] == "rmsprop" and update_adamw:
+            opt._rmsprop_step(g)
+    coef = self.clip_coef.reshape(1) if self.clip_coef is not None else None
+    for b in range(len(self.plans)):
+        S = self.plans[b].seg_numel
+        seg = self.recv[b]
+        base = self.goff[b] + self.rank * S
+        for shape, params, off in self._owned_runs(b):
+            K = len(params)
+            n = K * params[0].numel()
+            grp = self.group_of[id(params[0])]
+            g = seg[off:off + n].view(K, *shape)
+            gq = _fused_owner_direction(self, grp, g, self._state(params, grp), coef)
+            self.upd[base + off:base + off + n].copy_(gq.reshape(-1))
+    # scalars of every group (lr*ratio, lr*ratio*wd) for the apply kernel
+    for g in opt.param_groups:
+        if g["kind"] == "muon":
+            shape = g["params"][0].shape
+            opt._muon_scalars(g, g["params"][0], max(1.0, shape[-2] / shape[-1]) ** 0.5)
+    self._barrier()  # every owner's updates are in its update buffer
+    for b in range(len(self.plans)):
+        self.C.symm_ag_apply(self.upd_peers, self._runs_table(b))
+    self._barrier()  # peers are done reading this rank's gradient and update buffers
+
+
+def _runs_table(self, b: int) -> torch.Tensor:
+    tab = self._runs_tables.get(b)
+    if tab is not None:
+        return tab
+    rows = []
+    S = self.plans[b].seg_numel
+    for r, runs in enumerate(self._all_runs(b)):
+        for shape, params, off in runs:
+            K = len(params)
+            n = K * params[0].numel()
+            grp = self.group_of[id(params[0])]
+            dev_scalars = self.opt._scalar_cache[id(grp)]["muon"][1]
+            w16 = getattr(params[0], "_tfb_w16", None)
+            rows.append([r, self.goff[b] + r * S + off, params[0].data_ptr(),
+                         w16.data_ptr() if w16 is not None else 0, n,
+                         dev_scalars[0:1].data_ptr(), dev_scalars[1:2].data_ptr(), 0])
+    tab = torch.tensor(rows, dtype=torch.int64)
+    self._runs_tables[b] = tab
+    return tab
+
+
+DistMuon._step_fused = _step_fused
+DistMuon._runs_table = _runs_table

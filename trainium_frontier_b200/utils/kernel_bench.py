@@ -92,20 +92,73 @@ def bench_gemm(dev, peaks, shapes=None):
     return rows
 
 
+def bench_attention(dev, peaks, B=16, T=2048, H=10, D=128):
+    """Causal flash attention fwd / bwd at the d20 shape (FLOPs counted causally)."""
+    from ..ops.attention import flash_bwd, flash_fwd
+    t = Timer(dev)
+    M = B * T
+    q, k, v, do = (torch.randn(M, H * D, device=dev, dtype=torch.bfloat16) for _ in range(4))
+    o, lse = flash_fwd(q, k, v, B, T, H, D, D ** -0.5, True)
+    fl_fwd = 4.0 * B * H * T * T * D / 2
+    t_f = t.time(lambda: flash_fwd(q, k, v, B, T, H, D, D ** -0.5, True))
+    t_b = t.time(lambda: flash_bwd(q, k, v, o, do, lse, B, T, H, D, D ** -0.5, True))
+    qs, ks, vs = (x.view(B, T, H, D).transpose(1, 2) for x in (q, k, v))
+    t_ref = t.time(lambda: torch.nn.functional.scaled_dot_product_attention(qs, ks, vs, is_causal=True))
+    rows = [dict(name="flash fwd", ms=t_f, tflops=fl_fwd / t_f / 1e9, torch_sdpa_ms=t_ref),
+            dict(name="flash bwd", ms=t_b, tflops=2.5 * fl_fwd / t_b / 1e9)]
+    for r in rows:
+        r["frac_of_measured"] = r["tflops"] / peaks["bf16_tflops"]
+    return rows
+
+
+def one_kernel(case: str, dev):
+    """A single small launch after three warm-ups (for ncu captures of one kernel)."""
+    from ..ops import gemm
+    from ..ops.attention import flash_bwd, flash_fwd
+    if case == "gemm":
+        x = torch.randn(16384, 1280, device=dev, dtype=torch.bfloat16)
+        w = torch.randn(5120, 1280, device=dev, dtype=torch.bfloat16)
+        fn = lambda: gemm.linear_fwd(x, w)
+    elif case == "gemm_dw":
+        dy = torch.randn(16384, 5120, device=dev, dtype=torch.bfloat16)
+        x = torch.randn(16384, 1280, device=dev, dtype=torch.bfloat16)
+        g = torch.zeros(5120, 1280, device=dev)
+        fn = lambda: gemm.linear_dw(dy, x, g)
+    else:
+        B, T, H, D = 4, 2048, 10, 128
+        M = B * T
+        q, k, v, do = (torch.randn(M, H * D, device=dev, dtype=torch.bfloat16) for _ in range(4))
+        o, lse = flash_fwd(q, k, v, B, T, H, D, D ** -0.5, True)
+        fn = (lambda: flash_fwd(q, k, v, B, T, H, D, D ** -0.5, True)) if case == "fa_fwd" else \
+            (lambda: flash_bwd(q, k, v, o, do, lse, B, T, H, D, D ** -0.5, True))
+    for _ in range(4):
+        fn()
+    torch.cuda.synchronize(dev)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("what", nargs="?", default="gemm")
+    ap.add_argument("--one", default="", help="run one small case: gemm | gemm_dw | fa_fwd | fa_bwd")
     ap.add_argument("--json", default="")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     peaks = measured_peaks()
+    if args.one:
+        one_kernel(args.one, dev)
+        return
     out = {"peaks": peaks}
     if args.what in ("gemm", "all"):
         out["gemm"] = bench_gemm(dev, peaks)
         for r in out["gemm"]:
             print(f"{r['name']:>20s}  {r['ms']:8.3f} ms  {r['tflops']:7.1f} TF/s ({r['frac_of_measured']:.2f} of "
                   f"{peaks['source']})   torch {r['torch_ms']:8.3f} ms {r['torch_tflops']:7.1f} TF/s")
+    if args.what in ("attn", "all"):
+        out["attention"] = bench_attention(dev, peaks)
+        for r in out["attention"]:
+            print(f"{r['name']:>20s}  {r['ms']:8.3f} ms  {r['tflops']:7.1f} TF/s ({r['frac_of_measured']:.2f} of "
+                  f"{peaks['source']})" + (f"   torch sdpa fwd {r['torch_sdpa_ms']:.3f} ms" if 'torch_sdpa_ms' in r else ""))
     from ..ops._ext import check_errors
     check_errors(dev)
     if args.json:
