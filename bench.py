@@ -39,8 +39,15 @@ sys.path.insert(0, ROOT)
 
 BASELINE_TOKS = None  # the reference publishes no B200 number for this config
 METRIC = "train tok/s (max over ranks) at 1/2/4/8 B200; step ms; held-out bpb at fixed budget"
-CONFIG = {"model": "d20 GPT (20L, d1280, 10x128 heads, relu2 MLP 5120, vocab 8192)",
-          "global_batch": 524288, "seq_len": 2048}
+CONFIGS = {
+    "d20": {"model": "d20 GPT (20L, d1280, 10x128 heads, relu2 MLP 5120, vocab 8192)",
+            "global_batch": 524288, "seq_len": 2048},
+    "d12": {"model": "d12 GPT (12L, d768, 6x128 heads, relu2 MLP 3072, vocab 8192)",
+            "global_batch": 524288, "seq_len": 2048},
+    "d26": {"model": "d26 GPT (26L, d1664, 13x128 heads, relu2 MLP 6656, vocab 8192)",
+            "global_batch": 1048576, "seq_len": 4096},
+}
+CONFIG = CONFIGS["d20"]
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -136,10 +143,11 @@ def run_ours(args) -> dict:
     from trainium_frontier_b200.ops import _ext
     from trainium_frontier_b200.train import Trainer
     rank, world, local, dev = dist_setup(args.gpus)
+    CONFIG = CONFIGS[args.preset]
     per_gpu_tokens = CONFIG["global_batch"] // world
     rows_micro = min(args.micro_rows, per_gpu_tokens // CONFIG["seq_len"])
-    cfg = preset("d20", device_batch_size=rows_micro, pack_factor=1, progress_mode="steps",
-                 num_steps=10 ** 6, grad_sync=args.grad_sync, clip_order="global", seed=1234)
+    cfg = preset(args.preset, device_batch_size=rows_micro, pack_factor=1, progress_mode="steps",
+                 num_steps=10 ** 6, grad_sync=args.grad_sync, clip_order="global", seed=1234, tp=args.tp)
     tr = Trainer(cfg, dev, rank, world)
     n_params = sum(p.numel() for p in tr.model.parameters())
     # device-resident inputs for the kernel-only timing
@@ -190,7 +198,8 @@ def run_ours(args) -> dict:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded Zipf(1.1) token stream, BOS=0 docs of geometric mean length 200; random-init weights)",
-        "config": dict(CONFIG, parallelism=f"dp{world}", micro_batch_rows=rows_micro, grad_accum=tr.grad_accum,
+        "config": dict(CONFIG, parallelism=f"dp{world}" if args.tp == 1 else f"tp{args.tp}xdp{world // args.tp}",
+                       micro_batch_rows=rows_micro, grad_accum=tr.grad_accum,
                        grad_sync=tr.engine.grad_sync, n_params=n_params,
                        l2="inputs larger than L2 (multi-GB activations per micro-step); no flush"),
         "e2e": {"value": tok / (e2e_ms / 1000.0), "unit": "tokens/s", "ms_per_step": e2e_ms,
@@ -218,9 +227,9 @@ def run_reference(args) -> dict:
     import train as rtrain  # noqa: E402
     sys.argv = saved_argv
     from trainium_frontier_b200.data.loader import PackedRowLoader
-    # the plain family at the d20 shape, through the reference's own globals / API
-    rtrain.DEPTH = 20
-    rtrain.N_EMBD = 1280
+    CONFIG = CONFIGS[args.preset]
+    # the plain family at the preset's shape, through the reference's own globals / API
+    rtrain.DEPTH, rtrain.N_EMBD = {"d20": (20, 1280), "d12": (12, 768), "d26": (26, 1664)}[args.preset]
     rtrain.SEQ_LEN = CONFIG["seq_len"]
     rtrain.TOTAL_BATCH_SIZE = CONFIG["global_batch"]
     rtrain.USE_VE = False
@@ -316,10 +325,15 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--micro-rows", type=int, default=32, help="sequences per micro-step per GPU")
+    ap.add_argument("--micro-rows", type=int, default=0,
+                    help="sequences per micro-step per GPU (default: 32 at seq 2048, 4 for d26 at seq 4096)")
     ap.add_argument("--ref-micro-rows", type=int, default=4, help="reference arm sequences per micro-step")
     ap.add_argument("--grad-sync", default="auto")
+    ap.add_argument("--preset", default="d20", choices=sorted(CONFIGS), help="model / batch configuration")
+    ap.add_argument("--tp", type=int, default=1, help="tensor-parallel degree (ours; DP = N / tp)")
     args = ap.parse_args()
+    if args.micro_rows <= 0:
+        args.micro_rows = 4 if args.preset == "d26" else 32
     if args.warmup < 3:
         args.warmup = 3
     try:

@@ -300,6 +300,8 @@ def validate(cfg: RunConfig) -> None:
         raise ValueError("--coalesced-swiglu and --gated-mlp are mutually exclusive")
     if cfg.adam_every_n < 1:
         raise ValueError("--adam-every-n must be >= 1")
+    if cfg.tp < 1:
+        raise ValueError("--tp must be >= 1")
     if cfg.ve_gate_channels * 3 > max(cfg.model_config().n_embd, 1) and cfg.ngram_ve:
         raise ValueError("n_embd too small for three value-embedding gate slices")
 

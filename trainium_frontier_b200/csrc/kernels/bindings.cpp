@@ -6,6 +6,12 @@ void gemm_bf16(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_mn, int64_t M
                torch::Tensor D, int64_t epi, double alpha, double beta, c10::optional<torch::Tensor> R,
                c10::optional<torch::Tensor> D2, double tau, int64_t split_k, int64_t bn, torch::Tensor err,
                c10::optional<torch::Tensor> alpha_t, double rcoef);
+void gemm_tp(int64_t mode, torch::Tensor A, torch::Tensor B, bool b_mn, int64_t M, int64_t N, int64_t K,
+             torch::Tensor D, int64_t epi, c10::optional<torch::Tensor> R, c10::optional<torch::Tensor> D2,
+             double tau, double rcoef, int64_t rank, int64_t world, int64_t rows_per_rank, int64_t epoch,
+             std::vector<int64_t> ag_src, std::vector<int64_t> ag_ready, c10::optional<torch::Tensor> claim,
+             c10::optional<torch::Tensor> done, std::vector<int64_t> rs_recv, std::vector<int64_t> rs_flag,
+             torch::Tensor sched, int64_t bn, torch::Tensor err);
 void rmsnorm_fwd(torch::Tensor x, torch::Tensor y, c10::optional<torch::Tensor> rstd);
 void rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor rstd, c10::optional<torch::Tensor> dadd,
                  torch::Tensor dx);
@@ -54,6 +60,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("B"), py::arg("b_mn"), py::arg("M"), py::arg("N"), py::arg("K"), py::arg("D"), py::arg("epi"),
         py::arg("alpha"), py::arg("beta"), py::arg("R"), py::arg("D2"), py::arg("tau"), py::arg("split_k"),
         py::arg("bn"), py::arg("err"), py::arg("alpha_t") = py::none(), py::arg("rcoef") = 1.0);
+  m.def("gemm_tp", &tfb::gemm_tp);
   m.def("rmsnorm_fwd", &tfb::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &tfb::rmsnorm_bwd);
   m.def("mix_norm_fwd", &tfb::mix_norm_fwd);

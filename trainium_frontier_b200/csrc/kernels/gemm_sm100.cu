@@ -21,6 +21,26 @@
 //   EPI_RELU2_BWD D = bf16(bf16(alpha * acc) * 2 relu(R - tau))   (R = h)
 //   EPI_F32       D(f32) = alpha * acc (+ D if beta)        weight gradients (fp32, split-K via
 //                                                          vector atomics into the gradient)
+// Modes (the tensor-parallel collectives fused into the GEMM, over NVLink peer memory):
+//   MODE_PLAIN    the GEMM above.
+//   MODE_AG       all-gather -> GEMM.  A is the [M, K] gather buffer of which every rank
+//                 of the tensor-parallel group owns rows_per_rank rows (its sequence
+//                 shard, written there by the producing kernel).  Two extra copy warps
+//                 pull the peers' rows over NVLink into this GPU's buffer, 128 rows at
+//                 a time, while the MMAs start on the local rows; the TMA producer waits
+//                 (bounded) on a per-m-block "copied" word before loading a remote
+//                 m-block.  Every remote byte crosses NVLink once, and TMA only ever
+//                 reads this GPU's own memory.
+//   MODE_RS       GEMM -> reduce-scatter.  D = sum over ranks of the partial products,
+//                 scattered by row owner.  Tiles of the peers' rows come first: their
+//                 fp32 partials are stored straight into the owner's receive buffer
+//                 (P2P stores) and announced per tile and TMEM lane quarter with a
+//                 release flag; tiles of this rank's rows come last and add the peers'
+//                 partials (acquire-waited, bounded) and the residual in the epilogue.
+// In the TP modes tiles are handed out dynamically (an atomic counter read by the
+// producer, passed to the MMA and epilogue warps through a 4-slot ring in shared
+// memory), so a tile that waits is only ever claimed after every tile that others wait
+// for has been claimed by a running CTA: no wait depends on co-residency.
 // Every TMA load is a plain per-CTA load of this GPU's own memory.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -31,6 +51,26 @@
 namespace tfb {
 
 enum GemmEpi : int { EPI_BF16 = 0, EPI_RELU2 = 1, EPI_RELU2_BWD = 2, EPI_F32 = 3 };
+enum GemmMode : int { MODE_PLAIN = 0, MODE_AG = 1, MODE_RS = 2 };
+
+constexpr int kTpMaxRanks = 8;
+
+struct TpArgs {
+  int rank, world, rows_per_rank;  // rows of the full M range owned by each rank (multiple of 128)
+  uint32_t epoch;                  // call index, identical on every rank of the group
+  // all-gather side
+  const uint8_t* ag_src[kTpMaxRanks];  // every rank's gather buffer
+  uint8_t* ag_dst;                     // this rank's gather buffer
+  long long ag_ld_bytes;               // row stride of the gather buffers (bytes)
+  int ag_row_bytes;                    // bytes copied per row (K * 2)
+  uint32_t* ag_ready[kTpMaxRanks];     // every rank's ready pad; word s is written by rank s
+  uint32_t* ag_claim;                  // local claim word per remote m-block job
+  uint32_t* ag_done;                   // local "copied" word per m-block
+  // reduce-scatter side
+  float* rs_recv[kTpMaxRanks];         // every rank's receive buffer [world][rows_per_rank][N] fp32
+  uint32_t* rs_flag[kTpMaxRanks];      // every rank's flags [world][tiles per rank][4]
+  uint32_t* sched;                     // local [2]: tile counter, finished-CTA counter
+};
 
 struct GemmArgs {
   int M, N, K;
@@ -44,6 +84,7 @@ struct GemmArgs {
   const __nv_bfloat16* R;
   long long ldr, r_bstride;
   int* err;
+  TpArgs tp;
 };
 
 template <int BN>
@@ -53,10 +94,24 @@ struct GemmCfg {
   static constexpr uint32_t A_BYTES = BM * BK * 2;
   static constexpr uint32_t B_BYTES = BN * BK * 2;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
-  static constexpr size_t SMEM = 1024 + STAGES * (A_BYTES + B_BYTES) + (2 * STAGES + 5) * 8 + 16;
+  static constexpr int QSLOTS = 4;  // tile-id ring
+  static constexpr size_t SMEM = 1024 + STAGES * (A_BYTES + B_BYTES) + (2 * STAGES + 5 + 2 * QSLOTS) * 8 + 64;
 };
 
+template <int MODE>
 __device__ __forceinline__ void decode_tile(int t, const GemmArgs& a, int& mb, int& nb, int& ks, int& bi) {
+  if constexpr (MODE != MODE_PLAIN) {
+    // m-major raster in rank order: AG starts at this rank's rows, RS at the next rank's
+    // (own rows last); no split-K, no batch.
+    const int mr = a.tp.rows_per_rank >> 7;
+    const int first = MODE == MODE_AG ? a.tp.rank : (a.tp.rank + 1) % a.tp.world;
+    const int m0 = t / a.tiles_n;
+    nb = t - m0 * a.tiles_n;
+    mb = (m0 + first * mr) % a.tiles_m;
+    ks = 0;
+    bi = 0;
+    return;
+  }
   const int per_split = a.tiles_m * a.tiles_n;
   const int per_batch = per_split * a.split_k;
   bi = t / per_batch;
@@ -73,12 +128,57 @@ __device__ __forceinline__ void decode_tile(int t, const GemmArgs& a, int& mb, i
   nb = rr / gm;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(192, 1)
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* addr, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_release_gpu_u32(uint32_t* addr, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* addr) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_acquire_gpu_u32(const uint32_t* addr) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+// Bounded wait until *flag has reached `epoch` (wrap-safe).  sys scope for words written
+// by peers, gpu scope for words written by other CTAs of this kernel.
+template <bool SYS>
+__device__ __forceinline__ bool wait_epoch(const uint32_t* flag, uint32_t epoch, volatile int* abort_flag, int* err,
+                                           int code) {
+  const unsigned long long t0 = globaltimer_ns();
+  uint32_t it = 0;
+  while (true) {
+    const uint32_t v = SYS ? ld_acquire_sys_u32(flag) : ld_acquire_gpu_u32(flag);
+    if ((int)(v - epoch) >= 0) return true;
+    if ((++it & 15u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+        *abort_flag = 1;
+        if (err) atomicOr(err, code);
+        return false;
+      }
+    }
+  }
+}
+
+template <int MODE>
+struct ModeThreads {
+  static constexpr int value = MODE == MODE_AG ? 256 : 192;
+};
+
+template <int BN, bool A_MN, bool B_MN, int EPI, int MODE>
+__global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const GemmArgs args) {
+                     const __grid_constant__ GemmArgs args) {
   using C = GemmCfg<BN>;
-  constexpr int BM = C::BM, BK = C::BK, STAGES = C::STAGES;
+  constexpr int BM = C::BM, BK = C::BK, STAGES = C::STAGES, QS = C::QSLOTS;
   constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN, A_MN, B_MN);
 
   extern __shared__ uint8_t smem_raw[];
@@ -90,8 +190,12 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* qfull = drain + 1;
+  uint64_t* qempty = qfull + QS;
+  int* qtile = reinterpret_cast<int*>(qempty + QS);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(qtile + QS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* copy_word = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -104,6 +208,10 @@ __global__ void __launch_bounds__(192, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
       mbar_init(&tempty[i], 128);
+    }
+    for (int i = 0; i < QS; ++i) {
+      mbar_init(&qfull[i], 1);
+      mbar_init(&qempty[i], 5);  // MMA thread + one lane of each epilogue warp
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -121,15 +229,48 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ TMA producer + tile source
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
+      int qs = 0;
+      uint32_t qph = 0;
       bool ok = true;
       uint32_t out_valid = 0, out_parity = 0;  // per-stage: a load is in flight / its phase parity
-      for (int t = blockIdx.x; t < args.num_tiles && ok; t += gridDim.x) {
+      int ready_mb = -1;
+      int static_t = blockIdx.x;
+      while (ok) {
+        int t;
+        if constexpr (MODE == MODE_PLAIN) {
+          t = static_t;
+          static_t += gridDim.x;
+        } else {
+          t = (int)atomicAdd(args.tp.sched, 1u);
+        }
+        if (t >= args.num_tiles) t = -1;
+        if (!mbar_wait(&qempty[qs], qph ^ 1u, abort_flag, args.err, ERR_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        qtile[qs] = t;
+        mbar_arrive(&qfull[qs]);
+        if (++qs == QS) {
+          qs = 0;
+          qph ^= 1u;
+        }
+        if (t < 0) break;
         int mb, nb, ks, bi;
-        decode_tile(t, args, mb, nb, ks, bi);
+        decode_tile<MODE>(t, args, mb, nb, ks, bi);
+        if constexpr (MODE == MODE_AG) {
+          if (mb / (args.tp.rows_per_rank >> 7) != args.tp.rank && mb != ready_mb) {
+            if (!wait_epoch<false>(args.tp.ag_done + mb, args.tp.epoch, abort_flag, args.err, ERR_TIMEOUT_PRODUCER)) {
+              ok = false;
+              break;
+            }
+            fence_proxy_async_global();  // generic-proxy copies -> this thread's TMA reads
+            ready_mb = mb;
+          }
+        }
         const int kb0 = ks * args.kb_per_split;
         const int kb1 = min(kb0 + args.kb_per_split, args.kb_total);
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -161,6 +302,7 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
       if (!ok) {
+        *abort_flag = 1;
         // Drain: wait (bounded) until every load issued into a stage has landed, so no
         // bulk copy is still writing shared memory when the CTA exits.
         for (int s = 0; s < STAGES; ++s) {
@@ -179,10 +321,23 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
+      int qs = 0;
+      uint32_t qph = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < args.num_tiles && ok; t += gridDim.x) {
+      while (ok) {
+        if (!mbar_wait(&qfull[qs], qph, abort_flag, args.err, ERR_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        const int t = qtile[qs];
+        mbar_arrive(&qempty[qs]);
+        if (++qs == QS) {
+          qs = 0;
+          qph ^= 1u;
+        }
+        if (t < 0) break;
         int mb, nb, ks, bi;
-        decode_tile(t, args, mb, nb, ks, bi);
+        decode_tile<MODE>(t, args, mb, nb, ks, bi);
         const int kb0 = ks * args.kb_per_split;
         const int kb1 = min(kb0 + args.kb_per_split, args.kb_total);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, args.err, ERR_TIMEOUT_MMA)) {
@@ -230,31 +385,132 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
     }
-  } else {
+  } else if (warp < 6) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const float alpha = args.alpha * (args.alpha_ptr ? *args.alpha_ptr : 1.f);
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < args.num_tiles; t += gridDim.x) {
+    int qs = 0;
+    uint32_t qph = 0;
+    while (true) {
+      if (!mbar_wait_warp(&qfull[qs], qph, abort_flag, args.err, ERR_TIMEOUT_EPILOGUE)) break;
+      const int t = qtile[qs];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&qempty[qs]);
+      if (++qs == QS) {
+        qs = 0;
+        qph ^= 1u;
+      }
+      if (t < 0) break;
       int mb, nb, ks, bi;
-      decode_tile(t, args, mb, nb, ks, bi);
+      decode_tile<MODE>(t, args, mb, nb, ks, bi);
       if (!mbar_wait_warp(&tfull[acc], acc_phase, abort_flag, args.err, ERR_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const int row = mb * BM + q * 32 + lane;
-      const bool row_ok = row < args.M;
+      if constexpr (MODE == MODE_RS) {
+        // ---- reduce-scatter epilogue
+        const int mr = args.tp.rows_per_rank >> 7;
+        const int owner = mb / mr;
+        const int lrow = row - owner * args.tp.rows_per_rank;
+        const int tiles_per_rank = mr * args.tiles_n;
+        const int tile_local = (mb - owner * mr) * args.tiles_n + nb;
+        const int rank = args.tp.rank;
+        const long long N = args.N;
+        bool wait_ok = true;
+        if (owner == rank) {
+          for (int s = 0; s < args.tp.world && wait_ok; ++s) {
+            if (s == rank) continue;
+            const uint32_t* f = args.tp.rs_flag[rank] + ((long long)s * tiles_per_rank + tile_local) * 4 + q;
+            wait_ok = wait_epoch<true>(f, args.tp.epoch, abort_flag, args.err, ERR_TIMEOUT_PEER);
+          }
+          wait_ok = __all_sync(0xffffffffu, wait_ok) != 0;
+        }
+        if (!wait_ok) break;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        __syncwarp();
-        tmem_ld_32x32b_x32(tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN + c * 32), r);
-        tmem_ld_wait();
-        const int col0 = nb * BN + c * 32;
-        if (!row_ok || col0 >= args.N) continue;
-        const bool full_cols = col0 + 32 <= args.N;
-        float v[32];
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          __syncwarp();
+          tmem_ld_32x32b_x32(tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN + c * 32), r);
+          tmem_ld_wait();
+          const int col0 = nb * BN + c * 32;
+          if (col0 >= args.N) continue;
+          const bool full_cols = col0 + 32 <= args.N;
+          float v[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * alpha;
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * alpha;
+          if (owner != rank) {
+            float* dst = args.tp.rs_recv[owner] + ((long long)rank * args.tp.rows_per_rank + lrow) * N + col0;
+            if (full_cols) {
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                reinterpret_cast<float4*>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (col0 + i < args.N) dst[i] = v[i];
+            }
+          } else {
+            for (int s = 0; s < args.tp.world; ++s) {
+              if (s == rank) continue;
+              const float* src = args.tp.rs_recv[rank] + ((long long)s * args.tp.rows_per_rank + lrow) * N + col0;
+              if (full_cols) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  const float4 x = __ldcg(reinterpret_cast<const float4*>(src) + i);
+                  v[4 * i] += x.x; v[4 * i + 1] += x.y; v[4 * i + 2] += x.z; v[4 * i + 3] += x.w;
+                }
+              } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                  if (col0 + i < args.N) v[i] += __ldcg(src + i);
+              }
+            }
+            __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.D) + (long long)lrow * args.ldd + col0;
+            if (args.R != nullptr) {
+              const __nv_bfloat16* rr = args.R + (long long)lrow * args.ldr + col0;
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (full_cols || col0 + i < args.N) v[i] += args.rcoef * __bfloat162float(rr[i]);
+            }
+            if (full_cols) {
+              uint4 ov[4];
+              uint32_t* ow = reinterpret_cast<uint32_t*>(ov);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) ow[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) reinterpret_cast<uint4*>(out)[i] = ov[i];
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (col0 + i < args.N) out[i] = __float2bfloat16_rn(v[i]);
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+        if (owner != rank) {
+          // this lane quarter of the tile is in the owner's receive buffer: announce it
+          __threadfence_system();
+          __syncwarp();
+          if (lane == 0)
+            st_release_sys_u32(args.tp.rs_flag[owner] + ((long long)rank * tiles_per_rank + tile_local) * 4 + q,
+                               args.tp.epoch);
+        }
+      } else {
+        const bool row_ok = row < args.M;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          __syncwarp();
+          tmem_ld_32x32b_x32(tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN + c * 32), r);
+          tmem_ld_wait();
+          const int col0 = nb * BN + c * 32;
+          if (!row_ok || col0 >= args.N) continue;
+          const bool full_cols = col0 + 32 <= args.N;
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * alpha;
         if constexpr (EPI == EPI_F32) {
           float* out = reinterpret_cast<float*>(args.D) + bi * args.d_bstride + (long long)row * args.ldd + col0;
           if (full_cols) {
@@ -366,12 +622,79 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       }
-      tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
       }
+    }
+  } else if constexpr (MODE == MODE_AG) {
+    // ------------------------------------------------------------ all-gather copy warps (6, 7)
+    const int ct = threadIdx.x - 192;  // 0..63
+    const TpArgs& tp = args.tp;
+    if (ct < tp.world && ct != tp.rank) {
+      // this rank's rows of this call are in its gather buffer (written by earlier kernels)
+      __threadfence_system();
+      st_release_sys_u32(tp.ag_ready[ct] + tp.rank, tp.epoch);
+    }
+    const int mr = tp.rows_per_rank >> 7;
+    const int jobs = (tp.world - 1) * mr;
+    const int start = (int)((long long)blockIdx.x * jobs / gridDim.x);
+    const int vpr = tp.ag_row_bytes >> 4;  // 16-byte vectors per row
+    const int total = BM * vpr;
+    uint32_t ready_mask = 1u << tp.rank;
+    for (int i = 0; i < jobs; ++i) {
+      const int j = (start + i) % jobs;
+      const int gmb = ((tp.rank + 1) * mr + j) % args.tiles_m;
+      const int owner = gmb / mr;
+      if (ct == 0) {
+        int st = 0;  // 0 skip, 1 copy, 2 abort
+        if (*abort_flag) {
+          st = 2;
+        } else if (atomicMax(tp.ag_claim + j, tp.epoch) != tp.epoch) {
+          st = 1;
+          if (!((ready_mask >> owner) & 1u)) {
+            if (wait_epoch<true>(tp.ag_ready[tp.rank] + owner, tp.epoch, abort_flag, args.err, ERR_TIMEOUT_PEER))
+              ready_mask |= 1u << owner;
+            else
+              st = 2;
+          }
+        }
+        *copy_word = st;
+      }
+      named_bar_sync(2, 64);
+      const int st = *copy_word;
+      named_bar_sync(2, 64);
+      if (st == 2) break;
+      if (st == 0) continue;
+      const uint8_t* src = tp.ag_src[owner] + (long long)gmb * BM * tp.ag_ld_bytes;
+      uint8_t* dst = tp.ag_dst + (long long)gmb * BM * tp.ag_ld_bytes;
+      for (int base = ct; base < total; base += 64 * 8) {
+        uint4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int idx = base + u * 64;
+          if (idx < total) {
+            const int rr = idx / vpr, cc = idx - rr * vpr;
+            v[u] = __ldcg(reinterpret_cast<const uint4*>(src + (long long)rr * tp.ag_ld_bytes) + cc);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int idx = base + u * 64;
+          if (idx < total) {
+            const int rr = idx / vpr, cc = idx - rr * vpr;
+            reinterpret_cast<uint4*>(dst + (long long)rr * tp.ag_ld_bytes)[cc] = v[u];
+          }
+        }
+      }
+      fence_proxy_async_global();
+      __threadfence();
+      named_bar_sync(2, 64);
+      if (ct == 0) st_release_gpu_u32(tp.ag_done + gmb, tp.epoch);
     }
   }
 
@@ -380,6 +703,17 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+  if constexpr (MODE != MODE_PLAIN) {
+    if (threadIdx.x == 0) {
+      // the last CTA to finish rewinds the tile counter for the next launch
+      __threadfence();
+      if (atomicAdd(args.tp.sched + 1, 1u) == gridDim.x - 1) {
+        atomicExch(args.tp.sched, 0u);
+        atomicExch(args.tp.sched + 1, 0u);
+        __threadfence();
+      }
+    }
   }
 }
 
@@ -429,17 +763,17 @@ int num_sms(int dev) {
   return cache[dev];
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <int BN, bool A_MN, bool B_MN, int EPI, int MODE = MODE_PLAIN>
 static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid,
                         cudaStream_t stream) {
   using C = GemmCfg<BN>;
-  auto kern = gemm_bf16_kernel<BN, A_MN, B_MN, EPI>;
+  auto kern = gemm_bf16_kernel<BN, A_MN, B_MN, EPI, MODE>;
   static bool attr_set = false;  // one per instantiation
   if (!attr_set) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
     attr_set = true;
   }
-  kern<<<grid, 192, C::SMEM, stream>>>(ta, tb, a);
+  kern<<<grid, ModeThreads<MODE>::value, C::SMEM, stream>>>(ta, tb, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -460,6 +794,21 @@ static void dispatch(bool a_mn, bool b_mn, int epi, const CUtensorMap& ta, const
   TFB_CASE(true, false, EPI_BF16)
 #undef TFB_CASE
   TORCH_CHECK(false, "unsupported gemm variant a_mn=", a_mn, " b_mn=", b_mn, " epi=", epi);
+}
+
+template <int BN>
+static void dispatch_tp(int mode, bool b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
+                        const GemmArgs& a, int grid, cudaStream_t s) {
+#define TFB_TP(MD, BM_, E) \
+  if (mode == MD && b_mn == BM_ && epi == E) return launch_gemm<BN, false, BM_, E, MD>(ta, tb, a, grid, s);
+  TFB_TP(MODE_AG, false, EPI_BF16)
+  TFB_TP(MODE_AG, false, EPI_RELU2)
+  TFB_TP(MODE_AG, true, EPI_BF16)
+  TFB_TP(MODE_AG, true, EPI_RELU2_BWD)
+  TFB_TP(MODE_RS, false, EPI_BF16)
+  TFB_TP(MODE_RS, true, EPI_BF16)
+#undef TFB_TP
+  TORCH_CHECK(false, "unsupported tensor-parallel gemm variant mode=", mode, " b_mn=", b_mn, " epi=", epi);
 }
 
 // A: if !a_mn a [M, K] view (row stride lda), else a [K, M] view.  B likewise with N.
@@ -533,6 +882,101 @@ void gemm_bf16(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_mn, int64_t M
   cudaStream_t s = at::cuda::getCurrentCUDAStream();
   if (bn == 256) dispatch<256>(a_mn, b_mn, (int)epi, ta, tb, a, grid, s);
   else dispatch<128>(a_mn, b_mn, (int)epi, ta, tb, a, grid, s);
+}
+
+// Tensor-parallel GEMMs with the collective fused in (MODE_AG / MODE_RS), A K-major.
+//   AG: A = this rank's [M, K] gather buffer (rows [rank * Mr, (rank+1) * Mr) already
+//       written); ag_src / ag_ready = every rank's gather-buffer base / ready pad;
+//       claim [(world-1) * Mr / 128] and done [M / 128] are local uint32 words.
+//       D [M, N] (and D2 / R as in the plain epilogues).
+//   RS: D [Mr, N] bf16 = sum over ranks of (A B^T)[rank rows] (+ rcoef R), R [Mr, N];
+//       rs_recv / rs_flag = every rank's receive buffer ([world][Mr][N] fp32) / flag
+//       words ([world][Mr / 128 * tiles_n][4]).
+// sched: local uint32[2], zero before the first launch (the kernel leaves it zeroed).
+// Every flag word holds the epoch of the last call that wrote it; epochs increase by
+// one per call on every rank in the same order, starting above the words' initial 0.
+void gemm_tp(int64_t mode, torch::Tensor A, torch::Tensor B, bool b_mn, int64_t M, int64_t N, int64_t K,
+             torch::Tensor D, int64_t epi, c10::optional<torch::Tensor> R, c10::optional<torch::Tensor> D2,
+             double tau, double rcoef, int64_t rank, int64_t world, int64_t rows_per_rank, int64_t epoch,
+             std::vector<int64_t> ag_src, std::vector<int64_t> ag_ready, c10::optional<torch::Tensor> claim,
+             c10::optional<torch::Tensor> done, std::vector<int64_t> rs_recv, std::vector<int64_t> rs_flag,
+             torch::Tensor sched, int64_t bn, torch::Tensor err) {
+  TORCH_CHECK(mode == MODE_AG || mode == MODE_RS, "mode must be AG (1) or RS (2)");
+  TORCH_CHECK(A.is_cuda() && B.is_cuda() && D.is_cuda() && A.dim() == 2 && B.dim() == 2 && D.dim() == 2, "2-D CUDA operands");
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16 && D.scalar_type() == at::kBFloat16,
+              "bf16 operands");
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && D.stride(1) == 1, "inner dimension must be contiguous");
+  TORCH_CHECK(world >= 1 && world <= kTpMaxRanks && rank >= 0 && rank < world, "rank / world");
+  TORCH_CHECK(rows_per_rank % 128 == 0 && M == world * rows_per_rank, "M must be world x rows_per_rank, rows % 128 == 0");
+  TORCH_CHECK(K % 8 == 0 && N > 0, "K must be a multiple of 8");
+  TORCH_CHECK(A.size(0) >= M && A.size(1) >= K, "A shape");
+  TORCH_CHECK(!b_mn ? (B.size(0) >= N && B.size(1) >= K) : (B.size(0) >= K && B.size(1) >= N), "B shape");
+  TORCH_CHECK(sched.scalar_type() == at::kInt && sched.is_cuda() && sched.numel() >= 2, "sched int32[2]");
+  TORCH_CHECK(bn == 128 || bn == 256, "bn must be 128 or 256");
+  c10::cuda::CUDAGuard guard(A.device());
+  const int BM = 128, BK = 64;
+  CUtensorMap ta = make_tmap_bf16(A.data_ptr(), K, M, A.stride(0), 64, BM, 1, 0);
+  CUtensorMap tb = !b_mn ? make_tmap_bf16(B.data_ptr(), K, N, B.stride(0), 64, (uint32_t)bn, 1, 0)
+                         : make_tmap_bf16(B.data_ptr(), N, K, B.stride(0), 64, 64, 1, 0);
+  GemmArgs a{};
+  a.M = (int)M; a.N = (int)N; a.K = (int)K;
+  a.tiles_m = (int)(M / BM);
+  a.tiles_n = (int)((N + bn - 1) / bn);
+  a.kb_total = (int)((K + BK - 1) / BK);
+  a.kb_per_split = a.kb_total;
+  a.split_k = 1;
+  a.batch = 1;
+  a.num_tiles = a.tiles_m * a.tiles_n;
+  a.alpha = 1.f; a.beta = 0.f; a.tau = (float)tau; a.rcoef = (float)rcoef;
+  a.alpha_ptr = nullptr;
+  a.D = D.data_ptr(); a.ldd = D.stride(0); a.d_bstride = 0;
+  a.D2 = nullptr; a.ldd2 = 0; a.d2_bstride = 0; a.R = nullptr; a.ldr = 0; a.r_bstride = 0;
+  if (epi == EPI_RELU2) {
+    TORCH_CHECK(D2.has_value() && D2->scalar_type() == at::kBFloat16 && D2->stride(-1) == 1, "RELU2 needs D2");
+    a.D2 = D2->data_ptr(); a.ldd2 = D2->stride(0);
+  }
+  if (R.has_value()) {
+    TORCH_CHECK(R->scalar_type() == at::kBFloat16 && R->stride(-1) == 1, "R must be bf16 row-major");
+    a.R = reinterpret_cast<const __nv_bfloat16*>(R->data_ptr()); a.ldr = R->stride(0);
+  }
+  TORCH_CHECK(epi != EPI_RELU2_BWD || a.R != nullptr, "RELU2_BWD needs R = pre-activation");
+  a.err = err.data_ptr<int>();
+  TpArgs& tp = a.tp;
+  tp.rank = (int)rank; tp.world = (int)world; tp.rows_per_rank = (int)rows_per_rank; tp.epoch = (uint32_t)epoch;
+  tp.sched = reinterpret_cast<uint32_t*>(sched.data_ptr<int>());
+  if (mode == MODE_AG) {
+    TORCH_CHECK((int64_t)ag_src.size() == world && (int64_t)ag_ready.size() == world, "one gather buffer / pad per rank");
+    TORCH_CHECK(claim.has_value() && done.has_value() && claim->numel() >= (world - 1) * rows_per_rank / 128 &&
+                    done->numel() >= M / 128, "claim / done words");
+    TORCH_CHECK(D.size(0) >= M && D.size(1) >= N, "D shape");
+    TORCH_CHECK((A.stride(0) * 2) % 16 == 0, "gather rows must be 16-byte aligned");
+    for (int r = 0; r < world; ++r) {
+      TORCH_CHECK((ag_src[r] & 15) == 0, "gather buffers must be 16-byte aligned");
+      tp.ag_src[r] = reinterpret_cast<const uint8_t*>(ag_src[r]);
+      tp.ag_ready[r] = reinterpret_cast<uint32_t*>(ag_ready[r]);
+    }
+    TORCH_CHECK(ag_src[rank] == reinterpret_cast<int64_t>(A.data_ptr()), "A must be this rank's gather buffer");
+    tp.ag_dst = reinterpret_cast<uint8_t*>(A.data_ptr());
+    tp.ag_ld_bytes = A.stride(0) * 2;
+    tp.ag_row_bytes = (int)(K * 2);
+    tp.ag_claim = reinterpret_cast<uint32_t*>(claim->data_ptr<int>());
+    tp.ag_done = reinterpret_cast<uint32_t*>(done->data_ptr<int>());
+  } else {
+    TORCH_CHECK(epi == EPI_BF16, "reduce-scatter epilogue is bf16 (+ residual)");
+    TORCH_CHECK((int64_t)rs_recv.size() == world && (int64_t)rs_flag.size() == world, "one receive buffer / flag array per rank");
+    TORCH_CHECK(N % 4 == 0, "N must be a multiple of 4 (16-byte receive rows)");
+    TORCH_CHECK(D.size(0) >= rows_per_rank && D.size(1) >= N, "D shape");
+    if (a.R) TORCH_CHECK(R->size(0) >= rows_per_rank && R->size(1) >= N, "R shape");
+    for (int r = 0; r < world; ++r) {
+      TORCH_CHECK((rs_recv[r] & 15) == 0 && (rs_flag[r] & 3) == 0, "receive buffers 16-byte, flags 4-byte aligned");
+      tp.rs_recv[r] = reinterpret_cast<float*>(rs_recv[r]);
+      tp.rs_flag[r] = reinterpret_cast<uint32_t*>(rs_flag[r]);
+    }
+  }
+  const int grid = std::min(a.num_tiles, num_sms(A.get_device()));
+  cudaStream_t s = at::cuda::getCurrentCUDAStream();
+  if (bn == 256) dispatch_tp<256>((int)mode, b_mn, (int)epi, ta, tb, a, grid, s);
+  else dispatch_tp<128>((int)mode, b_mn, (int)epi, ta, tb, a, grid, s);
 }
 
 }  // namespace tfb

@@ -393,3 +393,6 @@ class TrainEngine:
         else:
             self.opt.step(update_adamw)
         self.layout.refresh_bf16()
+        tpc = getattr(self.model, "tpc", None)
+        if tpc is not None:
+            tpc.weights_version += 1

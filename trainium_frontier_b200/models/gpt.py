@@ -229,7 +229,16 @@ class Block(nn.Module):
                                            requires_grad=not rc.qk_shift_freeze) if rc.qk_shift else None)
         self.sandwich = rc.mlp_sandwich_norm
 
+    @property
+    def plain(self) -> bool:
+        return (self.x0_gate_s is None and self.local_conv is None and self.qk_shift_beta is None
+                and not self.sandwich and self.attn.plain and self.mlp.plain)
+
     def forward(self, x, x0, ve, cos, sin, attn_mask, ve_bi=None, ve_tri=None):
+        tpc = getattr(self, "_tpc", None)
+        if tpc is not None:
+            from ..parallel.tensor_parallel import block_forward_tp
+            return block_forward_tp(self, x, x0, cos, sin, tpc, self._layer_idx)
         fast = (self.x0_gate_s is None and self.local_conv is None and self.qk_shift_beta is None
                 and not self.sandwich and attn_mask is None and self.attn.plain)
         if fast:
@@ -432,6 +441,26 @@ class GPT(nn.Module):
         return rows
 
     # ------------------------------------------------------------------ forward
+    def enable_tp(self, tpc) -> None:
+        """Run every block tensor-parallel over ``tpc`` (plain blocks only); the batch
+        given to forward is then this rank's sequence shard of the group's micro-batch."""
+        bad = [i for i, b in enumerate(self.transformer.h) if not b.plain]
+        if bad or len(self.value_embeds) or len(self.ngram_embeds) or self.rc.doc_mask \
+                or any(self.layer_is_short) or self.out_pool_lambdas is not None or self.out_bigram is not None:
+            raise ValueError("tensor parallelism supports the plain block family only "
+                             f"(non-plain layers: {bad}, or VE / n-gram / masks / pooling enabled)")
+        self.tpc = tpc
+        for i, b in enumerate(self.transformer.h):
+            b._tpc = tpc
+            b._layer_idx = i
+
+    def disable_tp(self) -> None:
+        """Back to whole-model blocks (every rank holds every weight whole), e.g. for an
+        evaluation whose batches do not have the tensor-parallel row shape."""
+        self.tpc = None
+        for b in self.transformer.h:
+            b._tpc = None
+
     def hidden(self, idx: torch.Tensor) -> torch.Tensor:
         """Final normed hidden states [B, T, C] (compute dtype)."""
         _b, t = idx.shape

@@ -65,6 +65,12 @@ class Trainer:
         if cfg.init_from:
             ckpt.warm_start_from(cfg.init_from, model)
         self.model = model
+        self.tpc = None
+        if cfg.tp > 1:
+            from .parallel.tensor_parallel import TPContext
+            rows = cfg.device_batch_size * cfg.pack_factor * cfg.seq_len
+            self.tpc = TPContext(cfg.tp, self.device, rows, self.gconf.n_embd, 2 * self.gconf.n_layer)
+            model.enable_tp(self.tpc)
         self.opt = setup_optimizer(model, cfg, compute_dtype=self.dtype)
         self.rows_per_micro = cfg.device_batch_size * cfg.pack_factor
         tokens_per_micro = self.rows_per_micro * cfg.seq_len * world_size
@@ -220,6 +226,7 @@ def main(argv: list[str] | None = None) -> None:
     if ddp:
         dist.barrier()
     if cfg.eval_public:
+        tr.model.disable_tp()
         tok = syn.SyntheticTokenizer(cfg.vocab_size)
         causal = causality_check(tr.model, tok, cfg.device_batch_size, cfg.seq_len, device)
         res = evaluate_bpb(tr.model, tok, max(1, cfg.device_batch_size * cfg.pack_factor), cfg.seq_len, device,
