@@ -319,6 +319,21 @@ def run_reference(args) -> dict:
     }
 
 
+def run_infer(args) -> dict:
+    from trainium_frontier_b200.utils import infer_bench
+    if args.impl == "reference" and not os.path.exists(os.path.join(ROOT, "baseline", "_ref", "train.py")):
+        return {"impl": "reference", "unavailable": "baseline/_ref not installed"}
+    rank, world, local, dev = dist_setup(args.gpus)
+    clocks = ClockSampler(local)
+    clocks.start()
+    out = infer_bench.run(args, args.impl, ROOT, rank, world, local, dev)
+    out["clocks"] = clocks.stop()
+    if args.impl == "ours":
+        from trainium_frontier_b200.ops import _ext
+        out["gpu_launches"] = _ext.launch_count()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
@@ -331,13 +346,18 @@ def main():
     ap.add_argument("--grad-sync", default="auto")
     ap.add_argument("--preset", default="d20", choices=sorted(CONFIGS), help="model / batch configuration")
     ap.add_argument("--tp", type=int, default=1, help="tensor-parallel degree (ours; DP = N / tp)")
+    ap.add_argument("--workload", default="train", choices=["train", "infer"],
+                    help="train: the d20 pretraining step (default); infer: held-out eval + KV-cache decode")
     args = ap.parse_args()
     if args.micro_rows <= 0:
         args.micro_rows = 4 if args.preset == "d26" else 32
     if args.warmup < 3:
         args.warmup = 3
     try:
-        out = run_reference(args) if args.impl == "reference" else run_ours(args)
+        if args.workload == "infer":
+            out = run_infer(args)
+        else:
+            out = run_reference(args) if args.impl == "reference" else run_ours(args)
     except Exception as e:  # noqa: BLE001
         if args.impl == "reference":
             out = {"impl": "reference", "unavailable": f"{type(e).__name__}: {str(e)[:200]}"}

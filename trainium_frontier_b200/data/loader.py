@@ -119,6 +119,17 @@ class PackedRowLoader:
         return rows[:, :-1], rows[:, 1:], {"epoch": 1}
 
 
+def _to_dev(bx, by, dev):
+    """Rows -> (x int32, y int64) on `dev`; on CUDA through pinned host memory."""
+    x = torch.tensor(bx, dtype=torch.int32)
+    y = torch.tensor(by, dtype=torch.long)
+    if dev.type == "cuda":
+        x, y = x.pin_memory().to(dev, non_blocking=True), y.pin_memory().to(dev, non_blocking=True)
+    elif dev != x.device:
+        x, y = x.to(dev), y.to(dev)
+    return x, y, {"documents": 0}
+
+
 def make_eval_dataloader(tokenizer, batch_size: int, seq_len: int, split: str,
                          device: torch.device | str, max_stream_tokens: int = 1 << 21,
                          seed: int | None = None, **_unused):
@@ -143,8 +154,7 @@ def make_eval_dataloader(tokenizer, batch_size: int, seq_len: int, split: str,
         by.append(row[1:])
         pos += seq_len
         if len(bx) == batch_size:
-            yield (torch.tensor(bx, dtype=torch.int32, device=dev),
-                   torch.tensor(by, dtype=torch.long, device=dev), {"documents": 0})
+            yield _to_dev(bx, by, dev)
             bx, by = [], []
     tail = stream[pos:]
     if len(tail) > 1:
@@ -156,5 +166,4 @@ def make_eval_dataloader(tokenizer, batch_size: int, seq_len: int, split: str,
         while len(bx) < batch_size:
             bx.append([bos] * seq_len)
             by.append([-1] * seq_len)
-        yield (torch.tensor(bx, dtype=torch.int32, device=dev),
-               torch.tensor(by, dtype=torch.long, device=dev), {"documents": 0})
+        yield _to_dev(bx, by, dev)

@@ -1,7 +1,12 @@
-"""Roofline of the fused data-parallel collectives against NCCL, at the d20 Muon size.
+"""Roofline of the fused collectives against NCCL.
 
     torchrun --nproc-per-node N --master-addr 127.0.0.1 -m trainium_frontier_b200.utils.comm_bench \
-        [--numel 393216000] [--iters 10] [--json out.json]
+        [--what dp|tp] [--numel 393216000] [--rows 4] [--iters 10] [--json out.json]
+
+``--what tp`` times the tensor-parallel GEMMs with the collective fused in (d26 shapes)
+against NCCL all-gather / reduce-scatter plus the plain tcgen05 GEMM; roofline = max(FLOPs
+at the measured sustained bf16 GEMM rate, NVLink bytes into this GPU at 770 GB/s).
+The default (``dp``) is the data-parallel distributed-Muon pair:
 
 Times, with CUDA events on the launching stream and the max over ranks:
 
@@ -56,12 +61,120 @@ def _time(fn, iters: int, warm: int = 3) -> float:
     return float(ms.item())
 
 
+def _gemm_peak() -> float:
+    here = os.path.dirname(os.path.abspath(__file__))
+    try:
+        with open(os.path.join(here, "..", "..", "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d.get("bf16_tflops_sustained", d.get("bf16_tflops", 1400.0)))
+    except (OSError, ValueError):
+        return 1400.0
+
+
+def bench_tp(args) -> None:
+    """Fused TP GEMMs at the d26 shapes (C 1664, 13 heads x 128 split 7/6, MLP 6656 split
+    3328/3328, seq 4096, 4 sequences per rank) against NCCL collective + plain GEMM."""
+    from ..ops import gemm
+    from ..ops._ext import check_errors
+    from ..parallel.tensor_parallel import EPI_RELU2, TPContext, tp_split
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", device_id=dev)
+    C, F, D, H = 1664, 6656, 128, 13
+    Mr = args.rows * 4096
+    tpc = TPContext(world, dev, Mr, C, 2)
+    M = tpc.M
+    _, nq = tp_split(H * D, world, rank, D)
+    _, nf = tp_split(F, world, rank, 128)
+    bf = torch.bfloat16
+    x = torch.randn(Mr, C, device=dev).to(bf)
+    wqkv = (torch.randn(3 * nq, C, device=dev) * 0.02).to(bf)
+    wfc = (torch.randn(nf, C, device=dev) * 0.02).to(bf)
+    wproj = (torch.randn(C, nq, device=dev) * 0.02).to(bf)
+    wmp = (torch.randn(C, nf, device=dev) * 0.02).to(bf)
+    y = torch.randn(M, nq, device=dev).to(bf)
+    u = torch.randn(M, nf, device=dev).to(bf)
+    res = torch.randn(Mr, C, device=dev).to(bf)
+    h = torch.empty(M, nf, device=dev, dtype=bf)
+    full = torch.empty(M, C, device=dev, dtype=bf)
+    peak = _gemm_peak()
+    out = {"world": world, "rows_per_rank": Mr, "gemm_peak_tflops": peak, "link_gbs": LINK_GBS}
+
+    def ag(w, epi=0):
+        def f():
+            tpc.put_rows(0, x)
+            tpc.ag_gemm(0, w, False, epi, D2=h if epi == EPI_RELU2 else None)
+            tpc.put_rows(1, x)
+            tpc.rs_gemm(y, wproj, False, res)   # keeps AG calls separated by an RS (buffer reuse rule)
+        return f
+
+    def nccl_ag(w, epi=0):
+        def f():
+            dist.all_gather_into_tensor(full, x)
+            if epi == EPI_RELU2:
+                gemm.linear_relu2_fwd(full, w)
+            else:
+                gemm.linear_fwd(full, w)
+            z = gemm.linear_fwd(y, wproj)
+            o = torch.empty(Mr, C, device=dev, dtype=bf)
+            dist.reduce_scatter_tensor(o, z)
+            o += res
+        return f
+
+    def rs(a, w):
+        def f():
+            tpc.rs_gemm(a, w, False, res)
+        return f
+
+    def nccl_rs(a, w):
+        def f():
+            z = gemm.linear_fwd(a, w)
+            o = torch.empty(Mr, C, device=dev, dtype=bf)
+            dist.reduce_scatter_tensor(o, z)
+            o += res
+        return f
+
+    t_rs_proj = _time(rs(y, wproj), args.iters)
+    t_rs_mlp = _time(rs(u, wmp), args.iters)
+    n_rs_proj = _time(nccl_rs(y, wproj), args.iters)
+    n_rs_mlp = _time(nccl_rs(u, wmp), args.iters)
+    t_ag_qkv = _time(ag(wqkv), args.iters) - t_rs_proj
+    t_ag_fc = _time(ag(wfc, EPI_RELU2), args.iters) - t_rs_proj
+    n_ag_qkv = _time(nccl_ag(wqkv), args.iters) - n_rs_proj
+    n_ag_fc = _time(nccl_ag(wfc, EPI_RELU2), args.iters) - n_rs_proj
+    check_errors(dev)
+    link_ag = (world - 1) * Mr * C * 2
+    link_rs = (world - 1) * Mr * C * 4
+    rows = {
+        "ag_gemm_qkv": (t_ag_qkv, n_ag_qkv, 2.0 * M * C * 3 * nq, link_ag),
+        "ag_gemm_fc_relu2": (t_ag_fc, n_ag_fc, 2.0 * M * C * nf, link_ag),
+        "gemm_rs_attn_proj": (t_rs_proj, n_rs_proj, 2.0 * M * nq * C, link_rs),
+        "gemm_rs_mlp_proj": (t_rs_mlp, n_rs_mlp, 2.0 * M * nf * C, link_rs),
+    }
+    for k, (t, tn, fl, link) in rows.items():
+        roof = max(fl / (peak * 1e9), link / (LINK_GBS * 1e6))
+        out[k] = {"ms": t, "nccl_plus_gemm_ms": tn, "tflops": fl / t / 1e9, "roofline_ms": roof,
+                  "frac_of_roofline": roof / t, "nvlink_bytes_in": link}
+    if rank == 0:
+        print(json.dumps(out))
+        if args.json:
+            with open(args.json, "w") as f:
+                json.dump(out, f, indent=1)
+    tpc.close()
+    dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
+    ap.add_argument("--what", default="dp", choices=["dp", "tp"])
     ap.add_argument("--numel", type=int, default=20 * (4 * 1280 * 1280 + 2 * 1280 * 5120))
+    ap.add_argument("--rows", type=int, default=4, help="tp: sequences of 4096 tokens per rank")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--json", default="")
     args = ap.parse_args()
+    if args.what == "tp":
+        return bench_tp(args)
     import torch.distributed._symmetric_memory as symm_mem
 
     from ..ops._ext import C, check_errors, err_word
