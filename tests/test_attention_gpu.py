@@ -18,15 +18,22 @@ def _ref(q, k, v, causal, scale):
     return o, lse
 
 
-@pytest.mark.parametrize("B,T,H,D,causal", [(2, 256, 2, 128, True), (1, 512, 3, 64, True),
-                                            (2, 384, 2, 128, False), (1, 1024, 2, 128, True)])
-def test_flash_fwd_bwd(cuda_device, B, T, H, D, causal):
+@pytest.mark.parametrize("B,T,H,D,causal,kgrow", [(2, 256, 2, 128, True, 0.0), (1, 512, 3, 64, True, 0.0),
+                                                  (2, 384, 2, 128, False, 0.0), (1, 1024, 2, 128, True, 0.0),
+                                                  (2, 512, 2, 128, False, 0.0), (1, 2048, 1, 128, True, 0.0),
+                                                  (1, 1024, 2, 128, True, 3.0)])
+def test_flash_fwd_bwd(cuda_device, B, T, H, D, causal, kgrow):
+    """T % 256 == 0 with D = 128 runs the two-query-tile forward; kgrow > 0 scales the keys
+    up along the sequence so the running row max keeps growing (exercises the O rescale)."""
     from trainium_frontier_b200.ops._ext import check_errors
     from trainium_frontier_b200.ops.attention import flash_bwd, flash_fwd
     torch.manual_seed(0)
     scale = D ** -0.5
     q = torch.randn(B, T, H, D, device=cuda_device).to(torch.bfloat16)
-    k = torch.randn(B, T, H, D, device=cuda_device).to(torch.bfloat16)
+    k = torch.randn(B, T, H, D, device=cuda_device)
+    if kgrow:
+        k = k * (1.0 + kgrow * torch.arange(T, device=cuda_device) / T).view(1, T, 1, 1)
+    k = k.to(torch.bfloat16)
     v = torch.randn(B, T, H, D, device=cuda_device).to(torch.bfloat16)
     do = torch.randn(B, T, H, D, device=cuda_device).to(torch.bfloat16)
     M = B * T

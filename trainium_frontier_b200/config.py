@@ -321,6 +321,14 @@ PRESETS: dict[str, dict[str, Any]] = {
     "d12": dict(depth=12, n_embd=768, head_dim=128, seq_len=2048, total_batch_size=524288),
     "d20": dict(depth=20, n_embd=1280, head_dim=128, seq_len=2048, total_batch_size=524288),
     "d26": dict(depth=26, n_embd=1664, head_dim=128, seq_len=4096, total_batch_size=1048576),
+    # the 5-minute single-GPU research loop (depth 6, aspect 96 -> width 576 rounded up to
+    # the 128 head dim; its own learning rates, softcap and rotary base)
+    "autoresearch": dict(depth=6, n_embd=640, head_dim=128, seq_len=2048, device_batch_size=16, pack_factor=1,
+                         total_batch_size=131072, logit_softcap=11.0, rope_base=2_000_000.0, embedding_lr=0.2,
+                         unembedding_lr=0.004, matrix_lr=0.04, scalar_lr=0.3, weight_decay=0.0,
+                         embed_adamw_beta1=0.75, embed_adamw_beta2=0.99, warmdown_ratio=0.0, final_lr_frac=0.02,
+                         max_train_seconds=300, progress_mode="time", ve=False, ngram_ve=False,
+                         local_conv=False, qk_shift=False),
 }
 
 

@@ -315,6 +315,280 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ================================================================================ forward, two Q tiles
+// One CTA per (batch*head, pair of 128-query tiles), heaviest pairs first.  The two tiles
+// share every K/V tile load and ping-pong on the tensor core: while softmax warpgroup 0
+// turns S0 = Q0 K_j^T into P0, the MMA warp runs S1 / P1 V for tile 1, and vice versa.
+//   warp 0      TMA: Q0 + Q1 once, then K_0, V_0, K_1, V_1, ... through a 3-slot ring
+//   warp 1      MMA: S0(j+1), P0 V(j), S1(j+1), P1 V(j) per step j
+//   warps 2-5   softmax of tile 0 (one query row per thread = TMEM lane)
+//   warps 6-9   softmax of tile 1
+// TMEM: S0 | S1 | O0 | O1 (4 x 128 columns).  The row max used as the exponent reference
+// only moves when it grows by more than 8 (log2 units), so O is rarely rescaled; p values
+// stay below 2^8.  exp2 is one FFMA feeding ex2.approx.ftz.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+constexpr size_t kFwd2Smem = 1024 + 2 * 32768 + 3 * 32768 + 2 * 32768 + 24 * 8 + 16;
+
+__global__ void __launch_bounds__(320, 1)
+    fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const FaArgs a) {
+  constexpr int D = 128;
+  constexpr uint32_t TILE = 128u * D * 2u;
+  constexpr uint32_t IDESC_S = umma_idesc_bf16(128, 128, false, false);
+  constexpr uint32_t IDESC_O = umma_idesc_bf16(128, D, false, true);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                 // [2] tiles
+  uint8_t* sKV = sQ + 2 * TILE;       // [3] slots
+  uint8_t* sP = sKV + 3 * TILE;       // [2] tiles
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * TILE);
+  uint64_t* bar_q = bars + 0;
+  uint64_t* kv_full = bars + 1;    // [3]
+  uint64_t* kv_empty = bars + 4;   // [3]
+  uint64_t* s_full = bars + 7;     // [2]
+  uint64_t* s_free = bars + 9;     // [2]
+  uint64_t* p_full = bars + 11;    // [2]
+  uint64_t* pv_done = bars + 13;   // [2]
+  uint64_t* drain = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int BH = a.B * a.H;
+  const int n_pairs = a.n_tiles >> 1;
+  const int pc = n_pairs - 1 - (int)(blockIdx.x / BH);
+  const int bh = (int)(blockIdx.x % BH);
+  const int b = bh / a.H, h = bh % a.H;
+  const int qt0 = 2 * pc;
+  const int row0 = b * a.T + qt0 * 128;
+  const int n0 = a.causal ? qt0 + 1 : a.n_tiles;   // K/V tiles of tile 0
+  const int n1 = a.causal ? qt0 + 2 : a.n_tiles;   // ... of tile 1 (>= n0)
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_q, 1);
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&s_free[t], 128);
+      mbar_init(&p_full[t], 128);
+      mbar_init(&pv_done[t], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      bool ok = true;
+      uint32_t out_valid = 0, out_parity = 0;
+      mbar_arrive_expect_tx(bar_q, 2 * TILE);
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int p = 0; p < 2; ++p)
+          tma_load_3d(sQ + t * TILE + p * kPanel, &tmQ, bar_q, h * D + p * 64, row0 + t * 128, 0);
+      const int items = 2 * n1;
+      for (int i = 0; i < items && ok; ++i) {
+        const int slot = i % 3;
+        if (i >= 3 && !mbar_wait(&kv_empty[slot], ((i / 3) + 1) & 1, abort_flag, a.err, ERR_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&kv_full[slot], TILE);
+        out_valid |= 1u << slot;
+        out_parity = (out_parity & ~(1u << slot)) | ((uint32_t)((i / 3) & 1) << slot);
+        const int krow = b * a.T + (i >> 1) * 128;
+        const CUtensorMap* map = (i & 1) ? &tmV : &tmK;
+#pragma unroll
+        for (int p = 0; p < 2; ++p) tma_load_3d(sKV + slot * TILE + p * kPanel, map, &kv_full[slot], h * D + p * 64, krow, 0);
+      }
+      if (!ok) {
+        for (int s = 0; s < 3; ++s) {
+          if (!((out_valid >> s) & 1u)) continue;
+          const unsigned long long t0 = globaltimer_ns();
+          while (!mbar_try_wait(&kv_full[s], (out_parity >> s) & 1u))
+            if (globaltimer_ns() - t0 > 100000000ull) break;
+        }
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(bar_q, 0))
+          if (globaltimer_ns() - t0 > 100000000ull) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(bar_q, 0, abort_flag, a.err, ERR_TIMEOUT_MMA);
+      const uint32_t q_addr[2] = {smem_u32(sQ), smem_u32(sQ + TILE)};
+      const uint32_t p_addr[2] = {smem_u32(sP), smem_u32(sP + TILE)};
+      auto kv_wait = [&](int item) -> bool {
+        return mbar_wait(&kv_full[item % 3], (item / 3) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA);
+      };
+      auto issue_s = [&](int t, int j) -> bool {
+        if (!kv_wait(2 * j)) return false;
+        if (j >= 1 && !mbar_wait(&s_free[t], (j - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sKV + ((2 * j) % 3) * TILE);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_bf16(tmem + t * 128, desc_kmajor(q_addr[t], kk), desc_kmajor(k_addr, kk), IDESC_S, kk > 0 ? 1u : 0u);
+        umma_commit(&s_full[t]);
+        return true;
+      };
+      auto issue_pv = [&](int t, int j) -> bool {
+        if (!kv_wait(2 * j + 1)) return false;
+        if (!mbar_wait(&p_full[t], j & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sKV + ((2 * j + 1) % 3) * TILE);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16(tmem + 256 + t * 128, desc_kmajor(p_addr[t], kk), desc_mnmajor(v_addr, kk), IDESC_O,
+                    (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&pv_done[t]);
+        return true;
+      };
+      if (ok) ok = issue_s(0, 0) && issue_s(1, 0);
+      if (ok) umma_commit(&kv_empty[0]);  // K_0 read by both tiles
+      for (int j = 0; j < n1 && ok; ++j) {
+        if (j + 1 < n0 && !issue_s(0, j + 1)) { ok = false; break; }
+        if (j < n0 && !issue_pv(0, j)) { ok = false; break; }
+        if (j + 1 < n1) {
+          if (!issue_s(1, j + 1)) { ok = false; break; }
+          umma_commit(&kv_empty[(2 * (j + 1)) % 3]);  // K_{j+1} done
+        }
+        if (!issue_pv(1, j)) { ok = false; break; }
+        umma_commit(&kv_empty[(2 * j + 1) % 3]);      // V_j done
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        umma_commit(drain);
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(drain, 0))
+          if (globaltimer_ns() - t0 > 100000000ull) break;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax (tile t)
+    const int t = (warp - 2) >> 2;
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const uint32_t tS = tmem + t * 128, tO = tmem + 256 + t * 128;
+    uint8_t* myP = sP + t * TILE;
+    const int n_t = t == 0 ? n0 : n1;
+    const int qt = qt0 + t;
+    const float c = a.scale_log2;
+    float m_run = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_t; ++j) {
+      if (!mbar_wait_warp(&s_full[t], j & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      tc_fence_after();
+      float x[128];
+      {
+        uint32_t* xr = reinterpret_cast<uint32_t*>(x);
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          __syncwarp();
+          tmem_ld_32x32b_x32(tS + lane_off + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(xr + 32 * cc));
+        }
+        tmem_ld_wait();
+      }
+      tc_fence_before();
+      mbar_arrive(&s_free[t]);
+      const bool diag = a.causal && (j == qt);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 128; ++i) {
+        if (diag && i > r) x[i] = -INFINITY;
+        mx = fmaxf(mx, x[i]);
+      }
+      const float mxs = mx * c;
+      float alpha = 1.f;
+      const bool grow = mxs > m_run + 8.f;
+      if (grow) {
+        alpha = ex2_approx(m_run - mxs);
+        m_run = mxs;
+      }
+      float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 128; i += 2) {
+        const float p0 = ex2_approx(fmaf(x[i], c, -m_run));
+        const float p1 = ex2_approx(fmaf(x[i + 1], c, -m_run));
+        x[i] = p0;
+        x[i + 1] = p1;
+        sum0 += p0;
+        sum1 += p1;
+      }
+      l = l * alpha + (sum0 + sum1);
+      if (j >= 1) {
+        if (!mbar_wait_warp(&pv_done[t], (j - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll 1
+          for (int cc = 0; cc < D / 32; ++cc) {
+            uint32_t o[32];
+            __syncwarp();
+            tmem_ld_32x32b_x32(tO + lane_off + cc * 32, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st_32x32b_x32(tO + lane_off + cc * 32, o);
+          }
+          tmem_st_wait();
+        }
+      }
+      store_row_bf16_sw128(myP, r, x);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[t]);
+    }
+    if (ok && mbar_wait_warp(&pv_done[t], (n_t - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) {
+      tc_fence_after();
+      const float inv_l = 1.f / l;
+      __nv_bfloat16* dst = a.O + (long long)(row0 + t * 128 + r) * a.ldo + h * D;
+#pragma unroll 1
+      for (int cc = 0; cc < D / 32; ++cc) {
+        uint32_t o[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(tO + lane_off + cc * 32, o);
+        tmem_ld_wait();
+        float f[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(o[i]) * inv_l;
+        store_row_bf16_global(dst + cc * 32, f, 32);
+      }
+      a.lse[(long long)bh * a.T + qt * 128 + r] = (m_run + log2f(l)) * kLn2;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // ================================================================================ backward
 template <int D>
 __global__ void __launch_bounds__(192, 1)
@@ -661,7 +935,12 @@ void fa_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, int64_t B, int64_
   a.err = err.data_ptr<int>();
   const unsigned grid = (unsigned)(B * H * (T / 128));
   auto s = at::cuda::getCurrentCUDAStream();
-  if (D == 128) {
+  static const bool one_tile = getenv("TFB_FA_FWD_ONE_TILE") != nullptr;
+  if (D == 128 && T % 256 == 0 && !one_tile) {
+    static bool init = false;
+    if (!init) { set_smem(fa_fwd2_kernel, kFwd2Smem); init = true; }
+    fa_fwd2_kernel<<<grid / 2, 320, kFwd2Smem, s>>>(tq, tk, tv, a);
+  } else if (D == 128) {
     static bool init = false;
     if (!init) { set_smem(fa_fwd_kernel<128>, FaCfg<128>::FWD_SMEM); init = true; }
     fa_fwd_kernel<128><<<grid, 192, FaCfg<128>::FWD_SMEM, s>>>(tq, tk, tv, a);

@@ -33,8 +33,9 @@
 //                 reads this GPU's own memory.
 //   MODE_RS       GEMM -> reduce-scatter.  D = sum over ranks of the partial products,
 //                 scattered by row owner.  Tiles of the peers' rows come first: their
-//                 fp32 partials are stored straight into the owner's receive buffer
-//                 (P2P stores) and announced per tile and TMEM lane quarter with a
+//                 partials (bf16, staged through shared memory so they leave as whole
+//                 128-byte row segments) are stored straight into the owner's receive
+//                 buffer (P2P stores) and announced per tile and TMEM lane quarter with a
 //                 release flag; tiles of this rank's rows come last and add the peers'
 //                 partials (acquire-waited, bounded) and the residual in the epilogue.
 // In the TP modes tiles are handed out dynamically (an atomic counter read by the
@@ -67,7 +68,7 @@ struct TpArgs {
   uint32_t* ag_claim;                  // local claim word per remote m-block job
   uint32_t* ag_done;                   // local "copied" word per m-block
   // reduce-scatter side
-  float* rs_recv[kTpMaxRanks];         // every rank's receive buffer [world][rows_per_rank][N] fp32
+  __nv_bfloat16* rs_recv[kTpMaxRanks];  // every rank's receive buffer [world][rows_per_rank][N] bf16
   uint32_t* rs_flag[kTpMaxRanks];      // every rank's flags [world][tiles per rank][4]
   uint32_t* sched;                     // local [2]: tile counter, finished-CTA counter
 };
@@ -96,6 +97,7 @@ struct GemmCfg {
   static constexpr uint32_t TMEM_COLS = 2 * BN;
   static constexpr int QSLOTS = 4;  // tile-id ring
   static constexpr size_t SMEM = 1024 + STAGES * (A_BYTES + B_BYTES) + (2 * STAGES + 5 + 2 * QSLOTS) * 8 + 64;
+  static constexpr size_t SMEM_RS = SMEM + 128 + 4 * 4096;  // + epilogue staging tiles
 };
 
 template <int MODE>
@@ -196,6 +198,8 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(qtile + QS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* copy_word = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  // MODE_RS: per-epilogue-warp staging tile [32 rows][64 cols] bf16 (4 KB each)
+  uint8_t* staging = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tmem_slot + 4) + 127) & ~uintptr_t(127));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -427,6 +431,42 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
           wait_ok = __all_sync(0xffffffffu, wait_ok) != 0;
         }
         if (!wait_ok) break;
+        if (owner != rank) {
+          // Peer rows: bf16 partials to the owner's receive buffer.  Each 64-column slab is
+          // staged in this warp's swizzled smem tile (thread = row), then written out as
+          // whole 128-byte row segments, four rows per instruction.
+          uint8_t* stg = staging + q * 4096;
+          __nv_bfloat16* dst_base = args.tp.rs_recv[owner] + (long long)rank * args.tp.rows_per_rank * N;
+#pragma unroll 1
+          for (int c2 = 0; c2 < BN / 64; ++c2) {
+            uint32_t r0[32], r1[32];
+            __syncwarp();
+            tmem_ld_32x32b_x32(tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN + c2 * 64), r0);
+            tmem_ld_32x32b_x32(tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN + c2 * 64 + 32), r1);
+            tmem_ld_wait();
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) {
+              const uint32_t* src = cc < 4 ? r0 + cc * 8 : r1 + (cc - 4) * 8;
+              uint4 u;
+              u.x = pack_bf16x2(__uint_as_float(src[0]) * alpha, __uint_as_float(src[1]) * alpha);
+              u.y = pack_bf16x2(__uint_as_float(src[2]) * alpha, __uint_as_float(src[3]) * alpha);
+              u.z = pack_bf16x2(__uint_as_float(src[4]) * alpha, __uint_as_float(src[5]) * alpha);
+              u.w = pack_bf16x2(__uint_as_float(src[6]) * alpha, __uint_as_float(src[7]) * alpha);
+              *reinterpret_cast<uint4*>(stg + lane * 128 + ((cc ^ (lane & 7)) << 4)) = u;
+            }
+            __syncwarp();
+            const int col0 = nb * BN + c2 * 64;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int rr = i * 4 + (lane >> 3), cc = lane & 7;
+              const int gcol = col0 + cc * 8;
+              const int lr = mb * BM + q * 32 + rr - owner * args.tp.rows_per_rank;
+              if (gcol < args.N)
+                *reinterpret_cast<uint4*>(dst_base + (long long)lr * N + gcol) =
+                    *reinterpret_cast<const uint4*>(stg + rr * 128 + ((cc ^ (rr & 7)) << 4));
+            }
+          }
+        } else {
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t r[32];
@@ -439,31 +479,21 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
           float v[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * alpha;
-          if (owner != rank) {
-            float* dst = args.tp.rs_recv[owner] + ((long long)rank * args.tp.rows_per_rank + lrow) * N + col0;
-            if (full_cols) {
-#pragma unroll
-              for (int i = 0; i < 8; ++i)
-                reinterpret_cast<float4*>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-            } else {
-#pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (col0 + i < args.N) dst[i] = v[i];
-            }
-          } else {
             for (int s = 0; s < args.tp.world; ++s) {
               if (s == rank) continue;
-              const float* src = args.tp.rs_recv[rank] + ((long long)s * args.tp.rows_per_rank + lrow) * N + col0;
-              if (full_cols) {
+              const __nv_bfloat16* src = args.tp.rs_recv[rank] + ((long long)s * args.tp.rows_per_rank + lrow) * N + col0;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                  const float4 x = __ldcg(reinterpret_cast<const float4*>(src) + i);
-                  v[4 * i] += x.x; v[4 * i + 1] += x.y; v[4 * i + 2] += x.z; v[4 * i + 3] += x.w;
+              for (int i = 0; i < 4; ++i) {
+                if (col0 + 8 * i < args.N) {   // N % 8 == 0: whole 8-column groups
+                  const uint4 x = __ldcg(reinterpret_cast<const uint4*>(src) + i);
+                  const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&x);
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) {
+                    const float2 f = __bfloat1622float2(x2[j]);
+                    v[8 * i + 2 * j] += f.x;
+                    v[8 * i + 2 * j + 1] += f.y;
+                  }
                 }
-              } else {
-#pragma unroll
-                for (int i = 0; i < 32; ++i)
-                  if (col0 + i < args.N) v[i] += __ldcg(src + i);
               }
             }
             __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.D) + (long long)lrow * args.ldd + col0;
@@ -768,12 +798,13 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
                         cudaStream_t stream) {
   using C = GemmCfg<BN>;
   auto kern = gemm_bf16_kernel<BN, A_MN, B_MN, EPI, MODE>;
+  constexpr size_t smem = MODE == MODE_RS ? C::SMEM_RS : C::SMEM;
   static bool attr_set = false;  // one per instantiation
   if (!attr_set) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr_set = true;
   }
-  kern<<<grid, ModeThreads<MODE>::value, C::SMEM, stream>>>(ta, tb, a);
+  kern<<<grid, ModeThreads<MODE>::value, smem, stream>>>(ta, tb, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -890,7 +921,7 @@ void gemm_bf16(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_mn, int64_t M
 //       claim [(world-1) * Mr / 128] and done [M / 128] are local uint32 words.
 //       D [M, N] (and D2 / R as in the plain epilogues).
 //   RS: D [Mr, N] bf16 = sum over ranks of (A B^T)[rank rows] (+ rcoef R), R [Mr, N];
-//       rs_recv / rs_flag = every rank's receive buffer ([world][Mr][N] fp32) / flag
+//       rs_recv / rs_flag = every rank's receive buffer ([world][Mr][N] bf16) / flag
 //       words ([world][Mr / 128 * tiles_n][4]).
 // sched: local uint32[2], zero before the first launch (the kernel leaves it zeroed).
 // Every flag word holds the epoch of the last call that wrote it; epochs increase by
@@ -964,12 +995,12 @@ void gemm_tp(int64_t mode, torch::Tensor A, torch::Tensor B, bool b_mn, int64_t 
   } else {
     TORCH_CHECK(epi == EPI_BF16, "reduce-scatter epilogue is bf16 (+ residual)");
     TORCH_CHECK((int64_t)rs_recv.size() == world && (int64_t)rs_flag.size() == world, "one receive buffer / flag array per rank");
-    TORCH_CHECK(N % 4 == 0, "N must be a multiple of 4 (16-byte receive rows)");
+    TORCH_CHECK(N % 8 == 0, "N must be a multiple of 8 (16-byte receive rows)");
     TORCH_CHECK(D.size(0) >= rows_per_rank && D.size(1) >= N, "D shape");
     if (a.R) TORCH_CHECK(R->size(0) >= rows_per_rank && R->size(1) >= N, "R shape");
     for (int r = 0; r < world; ++r) {
       TORCH_CHECK((rs_recv[r] & 15) == 0 && (rs_flag[r] & 3) == 0, "receive buffers 16-byte, flags 4-byte aligned");
-      tp.rs_recv[r] = reinterpret_cast<float*>(rs_recv[r]);
+      tp.rs_recv[r] = reinterpret_cast<__nv_bfloat16*>(rs_recv[r]);
       tp.rs_flag[r] = reinterpret_cast<uint32_t*>(rs_flag[r]);
     }
   }

@@ -113,11 +113,11 @@ class TPContext:
         self.ready_peers = fpeers
         self.rsflag_peers = [[p + 4 * (tp + par * tp * self.rs_tiles * 4) for p in fpeers] for par in range(2)]
         recv_elems = tp * self.Mr * self.C
-        self.recv = symm_mem.empty(2 * recv_elems, dtype=torch.float32, device=dev)
+        self.recv = symm_mem.empty(2 * recv_elems, dtype=BF16, device=dev)
         rh = symm_mem.rendezvous(self.recv, self.pg)
         self._h.append(rh)
         roff = self.recv.data_ptr() - int(rh.buffer_ptrs[self.tp_rank])
-        self.recv_peers = [[int(p) + roff + 4 * par * recv_elems for p in rh.buffer_ptrs] for par in range(2)]
+        self.recv_peers = [[int(p) + roff + 2 * par * recv_elems for p in rh.buffer_ptrs] for par in range(2)]
         self.sched = torch.zeros(4, dtype=torch.int32, device=dev)
         self.claim = torch.zeros(max(1, (tp - 1) * self.Mr // 128), dtype=torch.int32, device=dev)
         self.done = torch.zeros(self.M // 128, dtype=torch.int32, device=dev)

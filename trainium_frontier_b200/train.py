@@ -146,7 +146,11 @@ class Trainer:
 
 
 def main(argv: list[str] | None = None) -> None:
-    cfg = parse_args(argv)
+    run(parse_args(argv))
+
+
+def run(cfg: RunConfig) -> dict:
+    """The training loop of ``main`` for an already-built config; returns the summary."""
     device_type = detect_device_type(cfg.device_type)
     ddp, rank, local_rank, world_size, device = init_runtime(device_type, cfg.seed)
     print0(f"config: {json.dumps(cfg.model_config().__dict__)}")
@@ -239,7 +243,11 @@ def main(argv: list[str] | None = None) -> None:
     print0(f"steps: {step}")
     print0(f"total_train_tokens: {total_tokens}")
     print0(f"num_params: {nparams}")
+    summary = {"steps": step, "total_train_tokens": total_tokens, "num_params": nparams}
+    if cfg.eval_public:
+        summary.update(val_bpb=res["val_bpb"], causality_passed=causal["passed"])
     cleanup_runtime()
+    return summary
 
 
 if __name__ == "__main__":

@@ -145,7 +145,7 @@ def bench_tp(args) -> None:
     n_ag_fc = _time(nccl_ag(wfc, EPI_RELU2), args.iters) - n_rs_proj
     check_errors(dev)
     link_ag = (world - 1) * Mr * C * 2
-    link_rs = (world - 1) * Mr * C * 4
+    link_rs = (world - 1) * Mr * C * 2
     rows = {
         "ag_gemm_qkv": (t_ag_qkv, n_ag_qkv, 2.0 * M * C * 3 * nq, link_ag),
         "ag_gemm_fc_relu2": (t_ag_fc, n_ag_fc, 2.0 * M * C * nf, link_ag),
