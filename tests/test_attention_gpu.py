@@ -26,7 +26,7 @@ def test_flash_fwd_bwd(cuda_device, B, T, H, D, causal, kgrow):
     """T % 256 == 0 with D = 128 runs the two-query-tile forward; kgrow > 0 scales the keys
     up along the sequence so the running row max keeps growing (exercises the O rescale)."""
     from trainium_frontier_b200.ops._ext import check_errors
-    from trainium_frontier_b200.ops.attention import flash_bwd, flash_fwd
+    from trainium_frontier_b200.ops.flash_attention import flash_bwd, flash_fwd
     torch.manual_seed(0)
     scale = D ** -0.5
     q = torch.randn(B, T, H, D, device=cuda_device).to(torch.bfloat16)
@@ -57,7 +57,7 @@ def test_flash_fwd_bwd(cuda_device, B, T, H, D, causal, kgrow):
 
 def test_flash_strided_qkv_views(cuda_device):
     """q / k / v as column slices of one [M, 3C] buffer (the fused projection layout)."""
-    from trainium_frontier_b200.ops.attention import flash_fwd
+    from trainium_frontier_b200.ops.flash_attention import flash_fwd
     torch.manual_seed(1)
     B, T, H, D = 2, 256, 3, 128
     Cd = H * D

@@ -192,6 +192,17 @@ class RunConfig:
     engram_table_mult: int = 32
     engram_mem_dim: int = 128
     engram_conv_kernel: int = 4
+    engram_site: str = "2"             # block index after which Y joins the residual (negatives from the end)
+    engram_orders: str = "2,3"
+    engram_heads: int = 1
+    engram_key_dim: int = 0            # 0 -> n_embd (no W_Q)
+    engram_share_ngram_tables: bool = False
+    engram_bf16: bool = True
+    parallel_block_coalesce: str = "none"
+    block_nudge: bool = False
+    block_nudge_site: str = "qk"       # "qk" or "resid"
+    selective_gate: bool = False
+    selective_gate_channels: int = 32
     # ---- schedules / extras --------------------------------------------------------
     batch_ramp: bool = False
     batch_ramp_grad_accum: str = "2,4,8"
@@ -242,7 +253,9 @@ SHAPE_CRITICAL_TOGGLES = (
     "ngram_ve_dim", "ngram_ve_bf16", "local_conv", "local_conv_kernel", "qk_shift",
     "head_gate", "out_pool", "out_pool_layers", "x0_gate", "gated_mlp", "coalesced_swiglu",
     "parallel_block", "out_bigram", "engram", "engram_table_mult", "engram_mem_dim",
-    "engram_conv_kernel",
+    "engram_conv_kernel", "engram_site", "engram_orders", "engram_heads", "engram_key_dim",
+    "engram_share_ngram_tables", "engram_bf16", "parallel_block_coalesce", "block_nudge", "block_nudge_site",
+    "selective_gate", "selective_gate_channels",
 )
 ARCH_TOGGLE_NAMES = SHAPE_CRITICAL_TOGGLES + (
     "rope_base", "logit_softcap", "ve_gate_channels", "qk_shift_beta", "qk_shift_freeze",
@@ -302,6 +315,15 @@ def validate(cfg: RunConfig) -> None:
         raise ValueError("--adam-every-n must be >= 1")
     if cfg.tp < 1:
         raise ValueError("--tp must be >= 1")
+    if cfg.parallel_block_coalesce != "none":
+        raise ValueError("--parallel-block-coalesce: only 'none' is built (the fused QKV GEMM already reads "
+                         "the three attention inputs as one weight); 'vfc' / 'all' change the state_dict layout")
+    if cfg.block_nudge_site not in ("qk", "resid"):
+        raise ValueError("--block-nudge-site must be 'qk' or 'resid'")
+    if cfg.engram:
+        orders = [int(o) for o in cfg.engram_orders.split(",") if o.strip()]
+        if not orders or any(o not in (2, 3) for o in orders):
+            raise ValueError("--engram-orders supports 2 and 3")
     if cfg.ve_gate_channels * 3 > max(cfg.model_config().n_embd, 1) and cfg.ngram_ve:
         raise ValueError("n_embd too small for three value-embedding gate slices")
 

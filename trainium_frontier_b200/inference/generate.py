@@ -22,7 +22,7 @@ import torch
 
 from ..ops import gemm
 from ..ops._ext import C, err_word
-from ..ops.attention import flash_fwd, supported
+from ..ops.flash_attention import flash_fwd, supported
 from ..ops.fused import w16
 
 
@@ -30,7 +30,8 @@ def _is_plain(model) -> bool:
     rc = model.rc
     return not (rc.ve or rc.ngram_ve or rc.local_conv or rc.qk_shift or rc.head_gate or rc.out_pool or
                 rc.x0_gate or rc.mlp_sandwich_norm or rc.gated_mlp or rc.coalesced_swiglu or rc.doc_mask or
-                rc.out_bigram or "S" in rc.window_pattern or (model.config.n_kv_heads not in (0, model.config.n_head)))
+                rc.out_bigram or rc.engram or rc.parallel_block or rc.block_nudge or rc.selective_gate or
+                "S" in rc.window_pattern or (model.config.n_kv_heads not in (0, model.config.n_head)))
 
 
 @torch.no_grad()

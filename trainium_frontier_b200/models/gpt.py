@@ -216,6 +216,75 @@ class MLP(nn.Module):
         return ops.linear(a, self.c_proj.weight, residual)
 
 
+ENGRAM_HASH_PRIMES = tuple(_next_prime(20011 + 7919 * k) for k in range(24))
+
+
+def engram_primes(head_idx: int, order: int) -> tuple[int, ...]:
+    """Multipliers of one Engram hash head (oldest token first); orders use disjoint
+    12-prime regions so heads of order 2 and 3 never share one (train.py:1182-1206)."""
+    base = (order - 2) * 12 + head_idx * order
+    if base + order > len(ENGRAM_HASH_PRIMES):
+        raise ValueError("too many Engram hash heads for the prime table")
+    return tuple(ENGRAM_HASH_PRIMES[base + j] for j in range(order))
+
+
+def _rng_neutral(build):
+    """Build a module without moving the CPU generator (its weights are overwritten by
+    init_weights, so construction must not shift any later tensor's initial values)."""
+    state = torch.random.get_rng_state()
+    try:
+        return build()
+    finally:
+        torch.random.set_rng_state(state)
+
+
+class EngramLite(nn.Module):
+    """Hashed n-gram memory read through a hidden-state gate (train.py:2767-2840):
+    Y = SiLU(conv(norm(a v))) + a v with a = sigmoid(<norm q, norm k> / sqrt(d)),
+    k = W_K e, v = W_V e, q = W_Q h (or h), e = the gathered table rows of the current
+    token's 2-/3-gram hashes.  Zero tables and a zero conv make it an exact no-op at
+    step 0 while W_K / W_V stay nonzero so the tables receive gradient."""
+
+    def __init__(self, config: GPTConfig, rc: RunConfig, padded_vocab: int, share_e_dim: int | None = None):
+        super().__init__()
+        self.orders = tuple(int(o) for o in rc.engram_orders.split(",") if o.strip())
+        self.heads = rc.engram_heads
+        self.share = share_e_dim is not None
+        self.mem_dim = rc.engram_mem_dim
+        self.rows = rc.engram_table_mult * padded_vocab
+        self.mod = _largest_prime_below(self.rows)
+        dt = torch.bfloat16 if rc.engram_bf16 else torch.float32
+        self.table_keys = tuple(f"e{h}o{o}" for o in self.orders for h in range(self.heads))
+        if self.share:
+            self.tables = nn.ModuleDict()
+            self.e_dim = share_e_dim
+        else:
+            self.tables = nn.ModuleDict({k: nn.Embedding(self.rows, self.mem_dim,
+                                                         _weight=torch.zeros(self.rows, self.mem_dim, dtype=dt))
+                                         for k in self.table_keys})
+            self.e_dim = self.mem_dim * len(self.table_keys)
+        self.key_dim = rc.engram_key_dim if rc.engram_key_dim > 0 else config.n_embd
+        self.w_k = _rng_neutral(lambda: Linear(self.e_dim, self.key_dim))
+        self.w_v = _rng_neutral(lambda: Linear(self.e_dim, config.n_embd))
+        self.w_q = _rng_neutral(lambda: Linear(config.n_embd, self.key_dim)) if self.key_dim != config.n_embd else None
+        self.conv = CausalConv(config.n_embd, rc.engram_conv_kernel) if rc.engram_conv_kernel > 0 else None
+        self.scale = self.key_dim ** -0.5
+
+    def gather(self, idx: dict[str, torch.Tensor], dtype: torch.dtype) -> torch.Tensor:
+        parts = [self.tables[k].weight[idx[k]].to(dtype) for k in self.table_keys]
+        return parts[0] if len(parts) == 1 else torch.cat(parts, dim=-1)
+
+    def forward(self, h: torch.Tensor, e: torch.Tensor) -> torch.Tensor:
+        k = ops.linear(e, self.w_k.weight)
+        v = ops.linear(e, self.w_v.weight)
+        q = ops.linear(h, self.w_q.weight) if self.w_q is not None else h
+        a = torch.sigmoid((ops.norm(q) * ops.norm(k)).sum(dim=-1, keepdim=True) * self.scale)
+        vt = a * v
+        if self.conv is None:
+            return vt
+        return F.silu(self.conv(ops.norm(vt))) + vt
+
+
 class Block(nn.Module):
     def __init__(self, config: GPTConfig, rc: RunConfig, layer_idx: int):
         super().__init__()
@@ -228,11 +297,24 @@ class Block(nn.Module):
         self.qk_shift_beta = (nn.Parameter(torch.full((config.n_embd,), float(rc.qk_shift_beta)),
                                            requires_grad=not rc.qk_shift_freeze) if rc.qk_shift else None)
         self.sandwich = rc.mlp_sandwich_norm
+        # parallel block: attention and MLP read the same normed residual (train.py:2708-2746)
+        if rc.parallel_block:
+            self.par_lambda_a = nn.Parameter(torch.ones(1))
+            self.par_lambda_m = nn.Parameter(torch.ones(1))
+        else:
+            self.par_lambda_a = self.par_lambda_m = None
+        # frozen zero nudge: an exact identity kept out of every optimizer group
+        self.block_nudge = nn.Parameter(torch.zeros(1), requires_grad=False) if rc.block_nudge else None
+        self.nudge_site = rc.block_nudge_site
+        # data-dependent resid / x0 mix from the first channels (zero-init => static lambdas)
+        self.gate_channels = rc.selective_gate_channels
+        self.scalar_gate = Linear(rc.selective_gate_channels, 2) if rc.selective_gate else None
 
     @property
     def plain(self) -> bool:
         return (self.x0_gate_s is None and self.local_conv is None and self.qk_shift_beta is None
-                and not self.sandwich and self.attn.plain and self.mlp.plain)
+                and not self.sandwich and self.attn.plain and self.mlp.plain and self.par_lambda_a is None
+                and self.block_nudge is None and self.scalar_gate is None)
 
     def forward(self, x, x0, ve, cos, sin, attn_mask, ve_bi=None, ve_tri=None):
         tpc = getattr(self, "_tpc", None)
@@ -240,19 +322,27 @@ class Block(nn.Module):
             from ..parallel.tensor_parallel import block_forward_tp
             return block_forward_tp(self, x, x0, cos, sin, tpc, self._layer_idx)
         fast = (self.x0_gate_s is None and self.local_conv is None and self.qk_shift_beta is None
-                and not self.sandwich and attn_mask is None and self.attn.plain)
+                and not self.sandwich and attn_mask is None and self.attn.plain and self.par_lambda_a is None
+                and self.block_nudge is None and self.scalar_gate is None)
         if fast:
             xm, h = ops.mix_norm(x, x0, self.resid_lambda, self.x0_lambda)
             y = self.attn(h, h, h, None, cos, sin, None)
             x = ops.linear(y, self.attn.c_proj.weight, residual=xm)
             return self.mlp(ops.norm(x), residual=x)
-        if self.x0_gate_s is not None:
+        if self.scalar_gate is not None:
+            g = ops.linear(x[..., :self.gate_channels], self.scalar_gate.weight)
+            x = (self.resid_lambda * (1.0 + g[..., 0:1])) * x + (self.x0_lambda * (1.0 + g[..., 1:2])) * x0
+        elif self.x0_gate_s is not None:
             gate0 = 2.0 * torch.sigmoid(self.x0_gate_s * x.mean(dim=-1, keepdim=True))
             x = self.resid_lambda * x + self.x0_lambda * (gate0 * x0)
         else:
             x = self.resid_lambda * x + self.x0_lambda * x0
         x = x.to(x0.dtype)
+        if self.block_nudge is not None and self.nudge_site == "resid":
+            x = x + self.block_nudge.to(x.dtype) * x
         q_in = k_in = v_in = x
+        if self.block_nudge is not None and self.nudge_site == "qk":
+            q_in = k_in = x + self.block_nudge.to(x.dtype) * x
         if self.qk_shift_beta is not None:
             q_in = k_in = x + self.qk_shift_beta.to(x.dtype) * causal_shift_1(x)
         if self.local_conv is not None:
@@ -260,6 +350,11 @@ class Block(nn.Module):
             v_in = x if self.qk_shift_beta is None else v_in
             if self.qk_shift_beta is None:
                 q_in = k_in = x
+        if self.par_lambda_a is not None:
+            h = ops.norm(x)
+            attn_out = self.attn(h, h, h, ve, cos, sin, attn_mask, ve_bi, ve_tri)
+            y = ops.linear(attn_out, self.attn.c_proj.weight)
+            return x + self.par_lambda_a.to(x.dtype) * y + self.par_lambda_m.to(x.dtype) * self.mlp(h)
         hq = ops.norm(q_in)
         hk = hq if k_in is q_in else ops.norm(k_in)
         hv = hq if v_in is q_in else ops.norm(v_in)
@@ -327,6 +422,19 @@ class GPT(nn.Module):
             self.out_bigram = None
         self.out_pool_lambdas = (nn.Parameter(torch.zeros(min(rc.out_pool_layers, config.n_layer)))
                                  if rc.out_pool else None)
+        # Engram-lite, built last among the table owners so it cannot shift their RNG draws
+        self.engram_site = int(rc.engram_site) % config.n_layer if rc.engram else -1
+        self.engram_share_keys: tuple[str, ...] = ()
+        if rc.engram:
+            share_dim = None
+            if rc.engram_share_ngram_tables:
+                self.engram_share_keys = tuple(k for k in self.ngram_embeds if int(k[1:]) <= self.engram_site)
+                if not self.engram_share_keys:
+                    raise ValueError("--engram-share-ngram-tables needs an n-gram table at or before the Engram site")
+                share_dim = self.ngram_dim * len(self.engram_share_keys)
+            self.engram = EngramLite(config, rc, V, share_dim)
+        else:
+            self.engram = None
         cos, sin = self._precompute_rotary_embeddings(config.sequence_len, config.head_dim)
         self.register_buffer("cos", cos, persistent=False)
         self.register_buffer("sin", sin, persistent=False)
@@ -381,6 +489,11 @@ class GPT(nn.Module):
             torch.nn.init.zeros_(block.mlp.c_proj.weight)
             block.resid_lambda.fill_(1.0)
             block.x0_lambda.fill_(0.05)
+            if block.par_lambda_a is not None:
+                block.par_lambda_a.fill_(1.0)
+                block.par_lambda_m.fill_(1.0)
+            if block.scalar_gate is not None:
+                torch.nn.init.zeros_(block.scalar_gate.weight)
             for g in (block.attn.ve_gate, block.attn.ve_gate_bi, block.attn.ve_gate_tri):
                 if g is not None:
                     torch.nn.init.zeros_(g.weight)
@@ -390,6 +503,14 @@ class GPT(nn.Module):
             torch.nn.init.zeros_(tbl.weight)
         for proj in self.ngram_proj.values():
             torch.nn.init.uniform_(proj.weight, -s, s)
+        if self.engram is not None:
+            for tbl in self.engram.tables.values():
+                torch.nn.init.zeros_(tbl.weight)
+            for lin in (self.engram.w_k, self.engram.w_v, self.engram.w_q):
+                if lin is not None:
+                    torch.nn.init.uniform_(lin.weight, -s, s)
+            if self.engram.conv is not None:
+                torch.nn.init.zeros_(self.engram.conv.weight)
         if self.out_bigram is not None:
             torch.nn.init.zeros_(self.out_bigram.weight)
             torch.nn.init.zeros_(self.out_bigram_gate.weight)
@@ -411,6 +532,8 @@ class GPT(nn.Module):
         nparams = sum(p.numel() for p in self.parameters())
         non_matmul = self.transformer.wte.weight.numel() + 2 * self.config.n_layer
         non_matmul += sum(p.numel() for p in self.ngram_embeds.parameters())
+        if self.engram is not None:
+            non_matmul += sum(p.numel() for p in self.engram.tables.parameters())
         if self.out_bigram is not None:
             non_matmul += self.out_bigram.weight.numel()
         h, d, t = self.config.n_head, self.config.head_dim, self.config.sequence_len
@@ -424,6 +547,12 @@ class GPT(nn.Module):
         cur = idx.long()
         prev = F.pad(cur[:, :-1], (1, 0), value=pad)
         prev2 = F.pad(cur[:, :-2], (2, 0), value=pad)
+        if self.engram is not None:
+            for key in self.engram.tables:
+                head, order = int(key[1:key.index("o")]), int(key[key.index("o") + 1:])
+                pr = engram_primes(head, order)
+                hsh = (prev * pr[0]) ^ (cur * pr[1]) if order == 2 else (prev2 * pr[0]) ^ (prev * pr[1]) ^ (cur * pr[2])
+                out[key] = hsh % self.engram.mod
         for key in self.ngram_embeds:
             layer = int(key[1:])
             p1, p2, p3 = _ngram_primes(layer)
@@ -434,8 +563,10 @@ class GPT(nn.Module):
             out[key] = (hsh % self.ngram_mod)
         return out
 
-    def _ngram_lookup(self, key: str, ids: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    def _ngram_lookup(self, key: str, ids: torch.Tensor, dtype: torch.dtype, raw: dict | None = None) -> torch.Tensor:
         rows = self.ngram_embeds[key].weight[ids].to(dtype)
+        if raw is not None:
+            raw[key] = rows   # pre-projection rows, what a shared Engram memory reads
         if key in self.ngram_proj:
             rows = ops.linear(rows, self.ngram_proj[key].weight)
         return rows
@@ -446,7 +577,7 @@ class GPT(nn.Module):
         given to forward is then this rank's sequence shard of the group's micro-batch."""
         bad = [i for i, b in enumerate(self.transformer.h) if not b.plain]
         if bad or len(self.value_embeds) or len(self.ngram_embeds) or self.rc.doc_mask \
-                or any(self.layer_is_short) or self.out_pool_lambdas is not None or self.out_bigram is not None:
+                or any(self.layer_is_short) or self.out_pool_lambdas is not None or self.out_bigram is not None or self.engram is not None:
             raise ValueError("tensor parallelism supports the plain block family only "
                              f"(non-plain layers: {bad}, or VE / n-gram / masks / pooling enabled)")
         self.tpc = tpc
@@ -470,7 +601,8 @@ class GPT(nn.Module):
         x = ops.embed_norm(idx, self.transformer.wte.weight, dt)
         x0 = x
         doc_mask = doc_boundary_mask(idx) if self.rc.doc_mask else None
-        ngram_idx = self._ngram_hash_indices(idx) if len(self.ngram_embeds) else None
+        ngram_idx = self._ngram_hash_indices(idx) if (len(self.ngram_embeds) or self.engram is not None) else None
+        engram_raw = {} if (self.engram is not None and self.engram.share) else None
         pool_from = self.config.n_layer - self.out_pool_lambdas.numel() if self.out_pool_lambdas is not None else 1 << 30
         pool_buf = []
         for i, block in enumerate(self.transformer.h):
@@ -478,15 +610,22 @@ class GPT(nn.Module):
             ve_bi = ve_tri = None
             if ngram_idx is not None:
                 if f"b{i}" in self.ngram_embeds:
-                    ve_bi = self._ngram_lookup(f"b{i}", ngram_idx[f"b{i}"], dt)
+                    ve_bi = self._ngram_lookup(f"b{i}", ngram_idx[f"b{i}"], dt, engram_raw)
                 if f"t{i}" in self.ngram_embeds:
-                    ve_tri = self._ngram_lookup(f"t{i}", ngram_idx[f"t{i}"], dt)
+                    ve_tri = self._ngram_lookup(f"t{i}", ngram_idx[f"t{i}"], dt, engram_raw)
             if doc_mask is None and not self.layer_is_short[i]:
                 attn_mask = None
             else:
                 static = self.mask_short[:t, :t] if self.layer_is_short[i] else torch.zeros(t, t, device=idx.device)
                 attn_mask = static.to(idx.device) + (doc_mask if doc_mask is not None else 0)
             x = block(x, x0, ve, cos, sin, attn_mask, ve_bi, ve_tri)
+            if i == self.engram_site:
+                if engram_raw is not None:
+                    parts = [engram_raw[k] for k in self.engram_share_keys]
+                    e_t = parts[0] if len(parts) == 1 else torch.cat(parts, dim=-1)
+                else:
+                    e_t = self.engram.gather(ngram_idx, dt)
+                x = x + self.engram(x, e_t).to(x.dtype)
             if i >= pool_from:
                 pool_buf.append(x)
         if self.out_pool_lambdas is not None:

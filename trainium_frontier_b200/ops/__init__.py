@@ -80,7 +80,7 @@ def attention(q, k, v, causal: bool = True, scale: float | None = None, attn_mas
     full, T % 128 == 0, head_dim 64 / 128); additive masks (document / sliding-window
     variants of the family) use the reference composition."""
     if _cuda(q) and q.dtype == torch.bfloat16 and attn_mask is None:
-        from .attention import FlashAttnFn, supported
+        from .flash_attention import FlashAttnFn, supported
         B, T, H, D = q.shape
         if supported(T, D):
             return FlashAttnFn.apply(q, k, v, causal, scale if scale is not None else D ** -0.5)
@@ -91,7 +91,7 @@ def attention_qkv(qkv: torch.Tensor, cos, sin, n_head: int, head_dim: int, scale
     """Plain-block attention core from the fused projection [B, T, 3C]:
     RoPE + QK-norm on q, k, then causal attention.  Returns [B, T, C]."""
     B, T, C3 = qkv.shape
-    from .attention import supported
+    from .flash_attention import supported
     if _cuda(qkv) and qkv.dtype == torch.bfloat16 and supported(T, head_dim):
         from .fused import AttnQKVFn
         c2 = cos.reshape(-1, cos.shape[-1])[:T].contiguous()

@@ -305,7 +305,7 @@ class AttnQKVFn(Function):
 
     @staticmethod
     def forward(ctx, qkv, cos, sin, B, T, H, D, scale):
-        from .attention import flash_fwd
+        from .flash_attention import flash_fwd
         Cd = H * D
         qkv2 = qkv.view(B * T, 3 * Cd)
         qkn = torch.empty((B * T, 2 * Cd), dtype=BF16, device=qkv.device)
@@ -318,7 +318,7 @@ class AttnQKVFn(Function):
 
     @staticmethod
     def backward(ctx, dy):
-        from .attention import flash_bwd
+        from .flash_attention import flash_bwd
         qkv2, qkn, rstd, cos, sin, o, lse = ctx.saved_tensors
         B, T, H, D, scale = ctx.meta
         Cd = H * D

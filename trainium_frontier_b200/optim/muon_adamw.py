@@ -324,6 +324,10 @@ def setup_optimizer(model, cfg: RunConfig, compute_dtype: torch.dtype | None = N
         scalar_params.extend([block.resid_lambda, block.x0_lambda])
         if block.x0_gate_s is not None:
             scalar_params.append(block.x0_gate_s)
+        if block.par_lambda_a is not None:
+            scalar_params.extend([block.par_lambda_a, block.par_lambda_m])
+        if block.scalar_gate is not None:
+            matrix_params.append(block.scalar_gate.weight)
         if block.qk_shift_beta is not None and block.qk_shift_beta.requires_grad:
             gate_params.append(block.qk_shift_beta)
         if block.attn.head_gate is not None:
@@ -331,6 +335,11 @@ def setup_optimizer(model, cfg: RunConfig, compute_dtype: torch.dtype | None = N
         matrix_params.extend(p for name, p in block.attn.named_parameters() if name != "head_gate_bias")
         matrix_params.extend(block.mlp.parameters())
     matrix_params.extend(p.weight for p in model.ngram_proj.values())
+    engram_conv = []
+    if getattr(model, "engram", None) is not None:
+        matrix_params.extend(l.weight for l in (model.engram.w_k, model.engram.w_v, model.engram.w_q) if l is not None)
+        if model.engram.conv is not None:
+            engram_conv.append(model.engram.conv.weight)
     if model.out_pool_lambdas is not None:
         scalar_params.append(model.out_pool_lambdas)
     if model.out_bigram is not None:
@@ -355,6 +364,11 @@ def setup_optimizer(model, cfg: RunConfig, compute_dtype: torch.dtype | None = N
         groups.append(dict(kind="adamw", params=ve_params, lr=cfg.embedding_lr * dscale,
                            betas=(cfg.embed_adamw_beta1, cfg.embed_adamw_beta2), eps=1e-10, weight_decay=cfg.ve_wd))
     ngram_params = list(model.ngram_embeds.parameters())
+    if getattr(model, "engram", None) is not None:
+        ngram_params.extend(model.engram.tables.parameters())
+    if engram_conv:
+        groups.append(dict(kind="adamw", params=engram_conv, lr=cfg.matrix_lr, betas=(0.9, 0.95), eps=1e-10,
+                           weight_decay=0.0))
     if ngram_params:
         lr = (cfg.ngram_ve_lr if cfg.ngram_ve_lr > 0 else cfg.embedding_lr) * dscale
         rms = cfg.ngram_ve_opt == "rmsprop"

@@ -23,6 +23,8 @@ def split_clip_params(model, exclude_ngram: bool = True):
         ids = {id(p) for p in model.ngram_embeds.parameters()}
         if getattr(model, "out_bigram", None) is not None:
             ids.add(id(model.out_bigram.weight))
+        if getattr(model, "engram", None) is not None:
+            ids |= {id(p) for p in model.engram.tables.parameters()}
     if not ids:
         return list(model.parameters()), []
     main, ng = [], []

@@ -94,7 +94,7 @@ def bench_gemm(dev, peaks, shapes=None):
 
 def bench_attention(dev, peaks, B=16, T=2048, H=10, D=128):
     """Causal flash attention fwd / bwd at the d20 shape (FLOPs counted causally)."""
-    from ..ops.attention import flash_bwd, flash_fwd
+    from ..ops.flash_attention import flash_bwd, flash_fwd
     t = Timer(dev)
     M = B * T
     q, k, v, do = (torch.randn(M, H * D, device=dev, dtype=torch.bfloat16) for _ in range(4))
@@ -114,7 +114,7 @@ def bench_attention(dev, peaks, B=16, T=2048, H=10, D=128):
 def one_kernel(case: str, dev):
     """A single small launch after three warm-ups (for ncu captures of one kernel)."""
     from ..ops import gemm
-    from ..ops.attention import flash_bwd, flash_fwd
+    from ..ops.flash_attention import flash_bwd, flash_fwd
     if case == "gemm":
         x = torch.randn(16384, 1280, device=dev, dtype=torch.bfloat16)
         w = torch.randn(5120, 1280, device=dev, dtype=torch.bfloat16)
