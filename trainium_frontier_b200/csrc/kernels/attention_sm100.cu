@@ -16,6 +16,10 @@
 //     P^T = exp(S^T * scale - LSE_i), dS^T = P^T (dP^T - Dvec_i)   (registers -> smem)
 //     dV += P^T dO_i, dK += dS^T Q_i                       (TMEM accumulators)
 //     dQ_i = dS K  -> fp32 vector atomics into a dQ accumulator
+// Faster forms for head_dim 128 (below): a two-query-tile forward that ping-pongs two
+// softmax warpgroups on the tensor core, and a pipelined backward (double-buffered Q / dO,
+// dQ drained by dedicated warps).  TFB_FA_FWD_ONE_TILE / TFB_FA_BWD_SERIAL select the
+// simple forms above (kept as the reference the fast forms are tested against).
 // Every wait is bounded (see sm100_common.cuh); every TMA load is a plain per-CTA load.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -516,13 +520,21 @@ __global__ void __launch_bounds__(320, 1)
       }
       tc_fence_before();
       mbar_arrive(&s_free[t]);
-      const bool diag = a.causal && (j == qt);
-      float mx = -INFINITY;
+      if (a.causal && j == qt) {  // diagonal tile: keys after this query row are masked
 #pragma unroll
-      for (int i = 0; i < 128; ++i) {
-        if (diag && i > r) x[i] = -INFINITY;
-        mx = fmaxf(mx, x[i]);
+        for (int i = 0; i < 128; ++i)
+          if (i > r) x[i] = -INFINITY;
       }
+      // eight independent max / sum chains (a single 128-long chain is latency-bound)
+      float mx8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mx8[k] = x[k];
+#pragma unroll
+      for (int i = 8; i < 128; i += 8)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(mx8[k], x[i + k]);
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float mxs = mx * c;
       float alpha = 1.f;
       const bool grow = mxs > m_run + 8.f;
@@ -530,17 +542,16 @@ __global__ void __launch_bounds__(320, 1)
         alpha = ex2_approx(m_run - mxs);
         m_run = mxs;
       }
-      float sum0 = 0.f, sum1 = 0.f;
+      float sm8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < 128; i += 2) {
-        const float p0 = ex2_approx(fmaf(x[i], c, -m_run));
-        const float p1 = ex2_approx(fmaf(x[i + 1], c, -m_run));
-        x[i] = p0;
-        x[i + 1] = p1;
-        sum0 += p0;
-        sum1 += p1;
-      }
-      l = l * alpha + (sum0 + sum1);
+      for (int i = 0; i < 128; i += 8)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float p = ex2_approx(fmaf(x[i + k], c, -m_run));
+          x[i + k] = p;
+          sm8[k] += p;
+        }
+      l = l * alpha + (((sm8[0] + sm8[1]) + (sm8[2] + sm8[3])) + ((sm8[4] + sm8[5]) + (sm8[6] + sm8[7])));
       if (j >= 1) {
         if (!mbar_wait_warp(&pv_done[t], (j - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
         tc_fence_after();
@@ -859,6 +870,331 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ================================================================================ backward, pipelined
+// D = 128.  One CTA per (batch*head, 128-key tile), transposed frame as above, but:
+//   * Q_i / dO_i / LSE_i / Dvec_i are double-buffered, so tile i+1 loads during tile i;
+//   * P^T and dS^T share one shared-memory tile (dS is written once the dV MMA has read P);
+//   * TMEM: R0 = S^T, R1 = dP^T then dQ, dV, dK.  S^T(i+1) is issued as soon as the softmax
+//     warps have read S^T(i); dQ(i) lands in R1 once dP^T(i) has been read, and four
+//     dedicated warps drain it (fp32 vector atomics into the dQ accumulator) while the
+//     softmax warps already work on tile i+1.
+//   warp 0 TMA, warp 1 MMA, warps 2-5 softmax / dS / epilogue, warps 6-9 dQ drain.
+constexpr size_t kBwd2Need = 2 * 32768 + 4 * 32768 + 32768 + 4 * 512 + 24 * 8 + 32;
+constexpr size_t kBwd2Smem = 232448;
+
+__global__ void __launch_bounds__(320, 1)
+    fa_bwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO, const FaArgs a) {
+  constexpr int D = 128;
+  constexpr uint32_t TILE = 128u * D * 2u;
+  constexpr uint32_t IDESC_SS = umma_idesc_bf16(128, 128, false, false);  // S^T, dP^T
+  constexpr uint32_t IDESC_KV = umma_idesc_bf16(128, D, false, true);     // dV, dK
+  constexpr uint32_t IDESC_Q = umma_idesc_bf16(128, D, true, true);       // dQ
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  if (pad + kBwd2Need > kBwd2Smem) {  // dynamic shared memory base too poorly aligned
+    if (threadIdx.x == 0) atomicOr(a.err, ERR_BAD_ARG);
+    return;
+  }
+  uint8_t* smem = smem_raw + pad;
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + TILE;
+  uint8_t* sQ = sV + TILE;          // [2]
+  uint8_t* sDO = sQ + 2 * TILE;     // [2]
+  uint8_t* sPD = sDO + 2 * TILE;    // P^T, then dS^T
+  float* sLse = reinterpret_cast<float*>(sPD + TILE);  // [2][128]
+  float* sDv = sLse + 256;                             // [2][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDv + 256);
+  uint64_t* bar_kv = bars + 0;
+  uint64_t* qdo_full = bars + 1;   // [2]
+  uint64_t* qdo_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* s_free = bars + 6;
+  uint64_t* dp_full = bars + 7;
+  uint64_t* p_full = bars + 8;
+  uint64_t* dv_done = bars + 9;
+  uint64_t* ds_full = bars + 10;
+  uint64_t* dq_full = bars + 11;
+  uint64_t* dq_free = bars + 12;
+  uint64_t* pds_free = bars + 13;
+  uint64_t* kv_done = bars + 14;
+  uint64_t* drain = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int BH = a.B * a.H;
+  const int kt = (int)(blockIdx.x / BH);
+  const int bh = (int)(blockIdx.x % BH);
+  const int b = bh / a.H, h = bh % a.H;
+  const int krow0 = b * a.T + kt * 128;
+  const int i0 = a.causal ? kt : 0;
+  const int n_it = a.n_tiles - i0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_kv, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qdo_full[i], 1);
+      mbar_init(&qdo_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 128);
+    mbar_init(dp_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(dv_done, 1);
+    mbar_init(ds_full, 128);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 128);
+    mbar_init(pds_free, 1);
+    mbar_init(kv_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmDO);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tR0 = tmem, tR1 = tmem + 128, tDV = tmem + 256, tDK = tmem + 384;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      bool ok = true;
+      uint32_t out_valid = 0, out_parity = 0;
+      mbar_arrive_expect_tx(bar_kv, 2 * TILE);
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        tma_load_3d(sK + p * kPanel, &tmK, bar_kv, h * D + p * 64, krow0, 0);
+        tma_load_3d(sV + p * kPanel, &tmV, bar_kv, h * D + p * 64, krow0, 0);
+      }
+      for (int it = 0; it < n_it && ok; ++it) {
+        const int bf = it & 1;
+        if (it >= 2 && !mbar_wait(&qdo_empty[bf], ((it - 2) >> 1) & 1, abort_flag, a.err, ERR_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&qdo_full[bf], 2 * TILE + 2 * 512);
+        out_valid |= 1u << bf;
+        out_parity = (out_parity & ~(1u << bf)) | ((uint32_t)((it >> 1) & 1) << bf);
+        const int qi = i0 + it;
+        const int qrow = b * a.T + qi * 128;
+        bulk_load(sLse + bf * 128, a.lse + (long long)bh * a.T + qi * 128, 512, &qdo_full[bf]);
+        bulk_load(sDv + bf * 128, a.dvec + (long long)bh * a.T + qi * 128, 512, &qdo_full[bf]);
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          tma_load_3d(sQ + bf * TILE + p * kPanel, &tmQ, &qdo_full[bf], h * D + p * 64, qrow, 0);
+          tma_load_3d(sDO + bf * TILE + p * kPanel, &tmDO, &qdo_full[bf], h * D + p * 64, qrow, 0);
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        for (int s = 0; s < 2; ++s) {
+          if (!((out_valid >> s) & 1u)) continue;
+          const unsigned long long t0 = globaltimer_ns();
+          while (!mbar_try_wait(&qdo_full[s], (out_parity >> s) & 1u))
+            if (globaltimer_ns() - t0 > 100000000ull) break;
+        }
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(bar_kv, 0))
+          if (globaltimer_ns() - t0 > 100000000ull) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(bar_kv, 0, abort_flag, a.err, ERR_TIMEOUT_MMA);
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), pd_addr = smem_u32(sPD);
+      for (int it = 0; it < n_it && ok; ++it) {
+        const int bf = it & 1;
+        const uint32_t q_addr = smem_u32(sQ + bf * TILE), do_addr = smem_u32(sDO + bf * TILE);
+        if (!mbar_wait(&qdo_full[bf], (it >> 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
+        if (it >= 1 && !mbar_wait(s_free, (it - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)  // S^T = K Q^T
+          umma_bf16(tR0, desc_kmajor(k_addr, kk), desc_kmajor(q_addr, kk), IDESC_SS, kk > 0 ? 1u : 0u);
+        umma_commit(s_full);
+        if (it >= 1 && !mbar_wait(dq_free, (it - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)  // dP^T = V dO^T
+          umma_bf16(tR1, desc_kmajor(v_addr, kk), desc_kmajor(do_addr, kk), IDESC_SS, kk > 0 ? 1u : 0u);
+        umma_commit(dp_full);
+        if (!mbar_wait(p_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // dV += P^T dO
+          umma_bf16(tDV, desc_kmajor(pd_addr, kk), desc_mnmajor(do_addr, kk), IDESC_KV, (it > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(dv_done);
+        if (!mbar_wait(ds_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // dK += dS^T Q
+          umma_bf16(tDK, desc_kmajor(pd_addr, kk), desc_mnmajor(q_addr, kk), IDESC_KV, (it > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // dQ = dS K  (into R1: dP^T has been read)
+          umma_bf16(tR1, desc_mnmajor(pd_addr, kk), desc_mnmajor(k_addr, kk), IDESC_Q, kk > 0 ? 1u : 0u);
+        umma_commit(dq_full);
+        umma_commit(pds_free);
+        umma_commit(&qdo_empty[bf]);
+      }
+      if (ok) {
+        umma_commit(kv_done);
+      } else {
+        *abort_flag = 1;
+        umma_commit(drain);
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(drain, 0))
+          if (globaltimer_ns() - t0 > 100000000ull) break;
+      }
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------------------------ P, dS, epilogue
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const float c = a.scale_log2;
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int bf = it & 1;
+      const int i = i0 + it;
+      const float* lse = sLse + bf * 128;
+      const float* dvec = sDv + bf * 128;
+      if (!mbar_wait_warp(&qdo_full[bf], (it >> 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      if (!mbar_wait_warp(s_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      tc_fence_after();
+      const bool diag = a.causal && (i == kt);
+      uint32_t pk[64];  // P^T row as packed bf16 pairs (kept for dS)
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t sv[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(tR0 + lane_off + c4 * 32, sv);
+        tmem_ld_wait();
+        if (diag) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const int cc = c4 * 32 + e;
+            float p0 = ex2_approx(fmaf(__uint_as_float(sv[e]), c, -lse[cc] * kLog2e));
+            float p1 = ex2_approx(fmaf(__uint_as_float(sv[e + 1]), c, -lse[cc + 1] * kLog2e));
+            if (cc < r) p0 = 0.f;  // query cc precedes key r: no attention
+            if (cc + 1 < r) p1 = 0.f;
+            pk[cc >> 1] = pack_bf16x2(p0, p1);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const int cc = c4 * 32 + e;
+            pk[cc >> 1] = pack_bf16x2(ex2_approx(fmaf(__uint_as_float(sv[e]), c, -lse[cc] * kLog2e)),
+                                      ex2_approx(fmaf(__uint_as_float(sv[e + 1]), c, -lse[cc + 1] * kLog2e)));
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(s_free);
+      if (it >= 1 && !mbar_wait_warp(pds_free, (it - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+#pragma unroll
+      for (int cc = 0; cc < 16; ++cc) {
+        const uint4 u = make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
+        *reinterpret_cast<uint4*>(sPD + (cc >> 3) * kPanel + sw128_chunk_offset(r, cc & 7)) = u;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+      if (!mbar_wait_warp(dp_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      if (!mbar_wait_warp(dv_done, it & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      tc_fence_after();
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t dv[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(tR1 + lane_off + c4 * 32, dv);
+        tmem_ld_wait();
+        uint32_t dsk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const int cc = c4 * 32 + e;
+          const float2 pf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&pk[cc >> 1]));
+          dsk[e >> 1] = pack_bf16x2(pf.x * (__uint_as_float(dv[e]) - dvec[cc]),
+                                    pf.y * (__uint_as_float(dv[e + 1]) - dvec[cc + 1]));
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int ch = c4 * 4 + q;
+          *reinterpret_cast<uint4*>(sPD + (ch >> 3) * kPanel + sw128_chunk_offset(r, ch & 7)) =
+              make_uint4(dsk[4 * q], dsk[4 * q + 1], dsk[4 * q + 2], dsk[4 * q + 3]);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(ds_full);
+    }
+    if (ok && mbar_wait_warp(kv_done, 0, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) {
+      tc_fence_after();
+      __nv_bfloat16* dvp = a.dV + (long long)(krow0 + r) * a.lddv + h * D;
+      __nv_bfloat16* dkp = a.dK + (long long)(krow0 + r) * a.lddk + h * D;
+#pragma unroll 1
+      for (int cc = 0; cc < D / 32; ++cc) {
+        uint32_t o[32];
+        float f[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(tDV + lane_off + cc * 32, o);
+        tmem_ld_wait();
+#pragma unroll
+        for (int v = 0; v < 32; ++v) f[v] = __uint_as_float(o[v]);
+        store_row_bf16_global(dvp + cc * 32, f, 32);
+        __syncwarp();
+        tmem_ld_32x32b_x32(tDK + lane_off + cc * 32, o);
+        tmem_ld_wait();
+#pragma unroll
+        for (int v = 0; v < 32; ++v) f[v] = __uint_as_float(o[v]) * a.scale;
+        store_row_bf16_global(dkp + cc * 32, f, 32);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ dQ drain
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    for (int it = 0; it < n_it; ++it) {
+      const int i = i0 + it;
+      if (!mbar_wait_warp(dq_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) break;
+      tc_fence_after();
+      float* dq = a.dq_acc + (long long)(b * a.T + i * 128 + r) * a.lddq + h * D;
+#pragma unroll 1
+      for (int cc = 0; cc < D / 32; ++cc) {
+        uint32_t o[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(tR1 + lane_off + cc * 32, o);
+        tmem_ld_wait();
+#pragma unroll
+        for (int v = 0; v < 8; ++v)
+          atomicAdd(reinterpret_cast<float4*>(dq + cc * 32) + v,
+                    make_float4(__uint_as_float(o[4 * v]) * a.scale, __uint_as_float(o[4 * v + 1]) * a.scale,
+                                __uint_as_float(o[4 * v + 2]) * a.scale, __uint_as_float(o[4 * v + 3]) * a.scale));
+      }
+      tc_fence_before();
+      mbar_arrive(dq_free);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // Dvec[bh, t] = sum_d dO[t, h*D + d] * O[t, h*D + d]; one warp per (row, head).
 __global__ void fa_bwd_dot_kernel(const __nv_bfloat16* __restrict__ dO, long long lddo,
                                   const __nv_bfloat16* __restrict__ O, long long ldo, float* __restrict__ dvec,
@@ -996,7 +1332,12 @@ void fa_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, 
   a.dV = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr()); a.lddv = dv.stride(0);
   a.err = err.data_ptr<int>();
   const unsigned grid = (unsigned)(B * H * (T / 128));
-  if (D == 128) {
+  static const bool serial_bwd = getenv("TFB_FA_BWD_SERIAL") != nullptr;
+  if (D == 128 && !serial_bwd) {
+    static bool init = false;
+    if (!init) { set_smem(fa_bwd2_kernel, kBwd2Smem); init = true; }
+    fa_bwd2_kernel<<<grid, 320, kBwd2Smem, s>>>(tq, tk, tv, tdo, a);
+  } else if (D == 128) {
     static bool init = false;
     if (!init) { set_smem(fa_bwd_kernel<128>, FaCfg<128>::BWD_SMEM); init = true; }
     fa_bwd_kernel<128><<<grid, 192, FaCfg<128>::BWD_SMEM, s>>>(tq, tk, tv, tdo, a);

@@ -9,10 +9,12 @@
 // double-buffered: the epilogue drains tile i while the MMAs of tile i+1 run) and
 // read back with tcgen05.ld for a fused epilogue.
 //
-// CTA = 6 warps, one CTA per SM, grid = min(#tiles, #SMs), tiles strided over CTAs:
+// CTA = 10 warps (12 with the all-gather copy warps), one CTA per SM, grid = min(#tiles, #SMs):
 //   warp 0      TMA producer            (full[s] <- TMA bytes, waits empty[s])
 //   warp 1      TMEM owner + MMA issuer (waits full[s], commits empty[s] / tfull[a])
-//   warps 2..5  epilogue, one TMEM lane quarter each (waits tfull[a], arrives tempty[a])
+//   warps 2..9  epilogue: warp w drains TMEM lane quarter (w & 3), column half (w - 2) >> 2
+//               (waits tfull[a], arrives tempty[a]); two warps per quarter halve the
+//               drain time, which short-K tiles would otherwise wait on
 // Tile 128 x BN x 64 (BN = 256 or 128), 4 or 6 pipeline stages.
 //
 // Epilogues (the fused ops the model needs):
@@ -69,7 +71,7 @@ struct TpArgs {
   uint32_t* ag_done;                   // local "copied" word per m-block
   // reduce-scatter side
   __nv_bfloat16* rs_recv[kTpMaxRanks];  // every rank's receive buffer [world][rows_per_rank][N] bf16
-  uint32_t* rs_flag[kTpMaxRanks];      // every rank's flags [world][tiles per rank][4]
+  uint32_t* rs_flag[kTpMaxRanks];      // every rank's flags [world][tiles per rank][8]
   uint32_t* sched;                     // local [2]: tile counter, finished-CTA counter
 };
 
@@ -97,7 +99,7 @@ struct GemmCfg {
   static constexpr uint32_t TMEM_COLS = 2 * BN;
   static constexpr int QSLOTS = 4;  // tile-id ring
   static constexpr size_t SMEM = 1024 + STAGES * (A_BYTES + B_BYTES) + (2 * STAGES + 5 + 2 * QSLOTS) * 8 + 64;
-  static constexpr size_t SMEM_RS = SMEM + 128 + 4 * 4096;  // + epilogue staging tiles
+  static constexpr size_t SMEM_RS = SMEM + 128 + 8 * 4096;  // + epilogue staging tiles
 };
 
 template <int MODE>
@@ -172,7 +174,7 @@ __device__ __forceinline__ bool wait_epoch(const uint32_t* flag, uint32_t epoch,
 
 template <int MODE>
 struct ModeThreads {
-  static constexpr int value = MODE == MODE_AG ? 256 : 192;
+  static constexpr int value = MODE == MODE_AG ? 384 : 320;
 };
 
 template <int BN, bool A_MN, bool B_MN, int EPI, int MODE>
@@ -198,7 +200,7 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(qtile + QS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* copy_word = reinterpret_cast<volatile int*>(tmem_slot + 2);
-  // MODE_RS: per-epilogue-warp staging tile [32 rows][64 cols] bf16 (4 KB each)
+  // MODE_RS: per-epilogue-warp staging tile [32 rows][64 cols] bf16 (4 KB each, 8 warps)
   uint8_t* staging = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tmem_slot + 4) + 127) & ~uintptr_t(127));
 
   const int warp = threadIdx.x >> 5;
@@ -211,11 +213,11 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 128);
+      mbar_init(&tempty[i], 256);
     }
     for (int i = 0; i < QS; ++i) {
       mbar_init(&qfull[i], 1);
-      mbar_init(&qempty[i], 5);  // MMA thread + one lane of each epilogue warp
+      mbar_init(&qempty[i], 9);  // MMA thread + one lane of each epilogue warp
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -389,9 +391,10 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
         }
       }
     }
-  } else if (warp < 6) {
+  } else if (warp < 10) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int hf = (warp - 2) >> 2;  // column half of the tile this warp drains
     const float alpha = args.alpha * (args.alpha_ptr ? *args.alpha_ptr : 1.f);
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -425,7 +428,7 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
         if (owner == rank) {
           for (int s = 0; s < args.tp.world && wait_ok; ++s) {
             if (s == rank) continue;
-            const uint32_t* f = args.tp.rs_flag[rank] + ((long long)s * tiles_per_rank + tile_local) * 4 + q;
+            const uint32_t* f = args.tp.rs_flag[rank] + ((long long)s * tiles_per_rank + tile_local) * 8 + hf * 4 + q;
             wait_ok = wait_epoch<true>(f, args.tp.epoch, abort_flag, args.err, ERR_TIMEOUT_PEER);
           }
           wait_ok = __all_sync(0xffffffffu, wait_ok) != 0;
@@ -435,10 +438,10 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
           // Peer rows: bf16 partials to the owner's receive buffer.  Each 64-column slab is
           // staged in this warp's swizzled smem tile (thread = row), then written out as
           // whole 128-byte row segments, four rows per instruction.
-          uint8_t* stg = staging + q * 4096;
+          uint8_t* stg = staging + (warp - 2) * 4096;
           __nv_bfloat16* dst_base = args.tp.rs_recv[owner] + (long long)rank * args.tp.rows_per_rank * N;
 #pragma unroll 1
-          for (int c2 = 0; c2 < BN / 64; ++c2) {
+          for (int c2 = hf * (BN / 128); c2 < (hf + 1) * (BN / 128); ++c2) {
             uint32_t r0[32], r1[32];
             __syncwarp();
             tmem_ld_32x32b_x32(tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN + c2 * 64), r0);
@@ -468,7 +471,7 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
           }
         } else {
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = hf * (BN / 64); c < (hf + 1) * (BN / 64); ++c) {
           uint32_t r[32];
           __syncwarp();
           tmem_ld_32x32b_x32(tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN + c * 32), r);
@@ -520,17 +523,18 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
         tc_fence_before();
         mbar_arrive(&tempty[acc]);
         if (owner != rank) {
-          // this lane quarter of the tile is in the owner's receive buffer: announce it
-          __threadfence_system();
+          // This lane quarter of the tile is in the owner's receive buffer: announce it.  The
+          // warp barrier orders every lane's stores before lane 0's system-scope release
+          // (cumulative), so one release per warp replaces a fence per thread.
           __syncwarp();
           if (lane == 0)
-            st_release_sys_u32(args.tp.rs_flag[owner] + ((long long)rank * tiles_per_rank + tile_local) * 4 + q,
+            st_release_sys_u32(args.tp.rs_flag[owner] + ((long long)rank * tiles_per_rank + tile_local) * 8 + hf * 4 + q,
                                args.tp.epoch);
         }
       } else {
         const bool row_ok = row < args.M;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = hf * (BN / 64); c < (hf + 1) * (BN / 64); ++c) {
           uint32_t r[32];
           __syncwarp();
           tmem_ld_32x32b_x32(tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN + c * 32), r);
@@ -663,7 +667,7 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
     }
   } else if constexpr (MODE == MODE_AG) {
     // ------------------------------------------------------------ all-gather copy warps (6, 7)
-    const int ct = threadIdx.x - 192;  // 0..63
+    const int ct = threadIdx.x - 320;  // 0..63
     const TpArgs& tp = args.tp;
     if (ct < tp.world && ct != tp.rank) {
       // this rank's rows of this call are in its gather buffer (written by earlier kernels)
@@ -922,7 +926,7 @@ void gemm_bf16(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_mn, int64_t M
 //       D [M, N] (and D2 / R as in the plain epilogues).
 //   RS: D [Mr, N] bf16 = sum over ranks of (A B^T)[rank rows] (+ rcoef R), R [Mr, N];
 //       rs_recv / rs_flag = every rank's receive buffer ([world][Mr][N] bf16) / flag
-//       words ([world][Mr / 128 * tiles_n][4]).
+//       words ([world][Mr / 128 * tiles_n][8]: lane quarter x column half).
 // sched: local uint32[2], zero before the first launch (the kernel leaves it zeroed).
 // Every flag word holds the epoch of the last call that wrote it; epochs increase by
 // one per call on every rank in the same order, starting above the words' initial 0.

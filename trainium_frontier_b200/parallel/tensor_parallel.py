@@ -100,10 +100,11 @@ class TPContext:
         self.slot_bytes = slot_elems * 2
         self.slots = [self.gpool[i * slot_elems:(i + 1) * slot_elems].view(self.M, self.C)
                       for i in range(self.n_slots + 2)]
-        # ready pads [tp] + RS flags 2 x [tp][tiles][4] in one symmetric int32 buffer
+        # ready pads [tp] + RS flags 2 x [tp][tiles][8] (lane quarter x column half) in one
+        # symmetric int32 buffer
         tiles_n = (self.C + 127) // 128
         self.rs_tiles = (self.Mr // 128) * tiles_n
-        flag_words = tp + 2 * tp * self.rs_tiles * 4
+        flag_words = tp + 2 * tp * self.rs_tiles * 8
         self.flags = symm_mem.empty(flag_words, dtype=torch.int32, device=dev)
         self.flags.zero_()
         fh = symm_mem.rendezvous(self.flags, self.pg)
@@ -111,7 +112,7 @@ class TPContext:
         foff = self.flags.data_ptr() - int(fh.buffer_ptrs[self.tp_rank])
         fpeers = [int(p) + foff for p in fh.buffer_ptrs]
         self.ready_peers = fpeers
-        self.rsflag_peers = [[p + 4 * (tp + par * tp * self.rs_tiles * 4) for p in fpeers] for par in range(2)]
+        self.rsflag_peers = [[p + 4 * (tp + par * tp * self.rs_tiles * 8) for p in fpeers] for par in range(2)]
         recv_elems = tp * self.Mr * self.C
         self.recv = symm_mem.empty(2 * recv_elems, dtype=BF16, device=dev)
         rh = symm_mem.rendezvous(self.recv, self.pg)
