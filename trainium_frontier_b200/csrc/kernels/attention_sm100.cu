@@ -31,6 +31,8 @@ namespace tfb {
 
 CUtensorMap make_tmap_bf16(const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
                            uint32_t box_inner, uint32_t box_outer, uint64_t batch, uint64_t batch_stride_elems);
+CUtensorMap make_tmap_f32(const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                          uint32_t box_inner, uint32_t box_outer);
 
 struct FaArgs {
   int B, T, H, n_tiles, causal;
@@ -872,21 +874,25 @@ __global__ void __launch_bounds__(192, 1)
 
 // ================================================================================ backward, pipelined
 // D = 128.  One CTA per (batch*head, 128-key tile), transposed frame as above, but:
-//   * Q_i / dO_i / LSE_i / Dvec_i are double-buffered, so tile i+1 loads during tile i;
+//   * Q_i / LSE_i / Dvec_i are double-buffered (tile i+1 loads during tile i); dO_i is
+//     single-buffered and reloaded as soon as the dV MMA of tile i has read it;
 //   * P^T and dS^T share one shared-memory tile (dS is written once the dV MMA has read P);
 //   * TMEM: R0 = S^T, R1 = dP^T then dQ, dV, dK.  S^T(i+1) is issued as soon as the softmax
-//     warps have read S^T(i); dQ(i) lands in R1 once dP^T(i) has been read, and four
-//     dedicated warps drain it (fp32 vector atomics into the dQ accumulator) while the
-//     softmax warps already work on tile i+1.
+//     warps have read S^T(i); dQ(i) lands in R1 once dP^T(i) has been read;
+//   * four dedicated warps drain dQ: 32-column slices are staged (scaled, 128-byte swizzle)
+//     in a double-buffered shared tile and added into the fp32 dQ accumulator by TMA bulk
+//     reduce-adds, so no per-thread global atomics remain.
 //   warp 0 TMA, warp 1 MMA, warps 2-5 softmax / dS / epilogue, warps 6-9 dQ drain.
-constexpr size_t kBwd2Need = 2 * 32768 + 4 * 32768 + 32768 + 4 * 512 + 24 * 8 + 32;
+constexpr size_t kBwd2Need = 2 * 32768 + 2 * 32768 + 32768 + 32768 + 2 * 16384 + 4 * 512 + 32 * 8 + 32;
 constexpr size_t kBwd2Smem = 232448;
 
 __global__ void __launch_bounds__(320, 1)
     fa_bwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO, const FaArgs a) {
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                   const __grid_constant__ CUtensorMap tmDQ, const FaArgs a) {
   constexpr int D = 128;
   constexpr uint32_t TILE = 128u * D * 2u;
+  constexpr uint32_t STG = 128u * 32u * 4u;  // one 32-column fp32 dQ slice
   constexpr uint32_t IDESC_SS = umma_idesc_bf16(128, 128, false, false);  // S^T, dP^T
   constexpr uint32_t IDESC_KV = umma_idesc_bf16(128, D, false, true);     // dV, dK
   constexpr uint32_t IDESC_Q = umma_idesc_bf16(128, D, true, true);       // dQ
@@ -901,26 +907,31 @@ __global__ void __launch_bounds__(320, 1)
   uint8_t* sK = smem;
   uint8_t* sV = sK + TILE;
   uint8_t* sQ = sV + TILE;          // [2]
-  uint8_t* sDO = sQ + 2 * TILE;     // [2]
-  uint8_t* sPD = sDO + 2 * TILE;    // P^T, then dS^T
-  float* sLse = reinterpret_cast<float*>(sPD + TILE);  // [2][128]
-  float* sDv = sLse + 256;                             // [2][128]
+  uint8_t* sDO = sQ + 2 * TILE;     // [1]
+  uint8_t* sPD = sDO + TILE;        // P^T, then dS^T
+  uint8_t* sDQ = sPD + TILE;        // [2] dQ staging slices
+  float* sLse = reinterpret_cast<float*>(sDQ + 2 * STG);  // [2][128]
+  float* sDv = sLse + 256;                                // [2][128]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sDv + 256);
   uint64_t* bar_kv = bars + 0;
-  uint64_t* qdo_full = bars + 1;   // [2]
-  uint64_t* qdo_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;
-  uint64_t* s_free = bars + 6;
-  uint64_t* dp_full = bars + 7;
-  uint64_t* p_full = bars + 8;
-  uint64_t* dv_done = bars + 9;
-  uint64_t* ds_full = bars + 10;
-  uint64_t* dq_full = bars + 11;
-  uint64_t* dq_free = bars + 12;
-  uint64_t* pds_free = bars + 13;
-  uint64_t* kv_done = bars + 14;
-  uint64_t* drain = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* q_full = bars + 1;     // [2]
+  uint64_t* q_empty = bars + 3;    // [2]
+  uint64_t* do_full = bars + 5;
+  uint64_t* do_empty = bars + 6;
+  uint64_t* s_full = bars + 7;
+  uint64_t* s_free = bars + 8;
+  uint64_t* dp_full = bars + 9;
+  uint64_t* p_full = bars + 10;
+  uint64_t* dv_done = bars + 11;
+  uint64_t* ds_full = bars + 12;
+  uint64_t* dq_full = bars + 13;
+  uint64_t* dq_free = bars + 14;
+  uint64_t* pds_free = bars + 15;
+  uint64_t* kv_done = bars + 16;
+  uint64_t* drain = bars + 17;
+  uint64_t* stg_full = bars + 18;  // [2]
+  uint64_t* stg_free = bars + 20;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -935,9 +946,13 @@ __global__ void __launch_bounds__(320, 1)
   if (threadIdx.x == 0) {
     mbar_init(bar_kv, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&qdo_full[i], 1);
-      mbar_init(&qdo_empty[i], 1);
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&stg_full[i], 128);
+      mbar_init(&stg_free[i], 1);
     }
+    mbar_init(do_full, 1);
+    mbar_init(do_empty, 1);
     mbar_init(s_full, 1);
     mbar_init(s_free, 128);
     mbar_init(dp_full, 1);
@@ -955,6 +970,7 @@ __global__ void __launch_bounds__(320, 1)
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
     tma_prefetch_desc(&tmDO);
+    tma_prefetch_desc(&tmDQ);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -970,7 +986,9 @@ __global__ void __launch_bounds__(320, 1)
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       bool ok = true;
-      uint32_t out_valid = 0, out_parity = 0;
+      uint32_t q_valid = 0, q_par = 0;
+      bool do_pending = false;
+      uint32_t do_par = 0;
       mbar_arrive_expect_tx(bar_kv, 2 * TILE);
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
@@ -979,51 +997,59 @@ __global__ void __launch_bounds__(320, 1)
       }
       for (int it = 0; it < n_it && ok; ++it) {
         const int bf = it & 1;
-        if (it >= 2 && !mbar_wait(&qdo_empty[bf], ((it - 2) >> 1) & 1, abort_flag, a.err, ERR_TIMEOUT_PRODUCER)) {
+        const int qi = i0 + it;
+        const int qrow = b * a.T + qi * 128;
+        if (it >= 2 && !mbar_wait(&q_empty[bf], ((it - 2) >> 1) & 1, abort_flag, a.err, ERR_TIMEOUT_PRODUCER)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&qdo_full[bf], 2 * TILE + 2 * 512);
-        out_valid |= 1u << bf;
-        out_parity = (out_parity & ~(1u << bf)) | ((uint32_t)((it >> 1) & 1) << bf);
-        const int qi = i0 + it;
-        const int qrow = b * a.T + qi * 128;
-        bulk_load(sLse + bf * 128, a.lse + (long long)bh * a.T + qi * 128, 512, &qdo_full[bf]);
-        bulk_load(sDv + bf * 128, a.dvec + (long long)bh * a.T + qi * 128, 512, &qdo_full[bf]);
+        mbar_arrive_expect_tx(&q_full[bf], TILE + 2 * 512);
+        q_valid |= 1u << bf;
+        q_par = (q_par & ~(1u << bf)) | ((uint32_t)((it >> 1) & 1) << bf);
+        bulk_load(sLse + bf * 128, a.lse + (long long)bh * a.T + qi * 128, 512, &q_full[bf]);
+        bulk_load(sDv + bf * 128, a.dvec + (long long)bh * a.T + qi * 128, 512, &q_full[bf]);
 #pragma unroll
-        for (int p = 0; p < 2; ++p) {
-          tma_load_3d(sQ + bf * TILE + p * kPanel, &tmQ, &qdo_full[bf], h * D + p * 64, qrow, 0);
-          tma_load_3d(sDO + bf * TILE + p * kPanel, &tmDO, &qdo_full[bf], h * D + p * 64, qrow, 0);
+        for (int p = 0; p < 2; ++p) tma_load_3d(sQ + bf * TILE + p * kPanel, &tmQ, &q_full[bf], h * D + p * 64, qrow, 0);
+        if (it >= 1 && !mbar_wait(do_empty, (it - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
         }
+        mbar_arrive_expect_tx(do_full, TILE);
+        do_pending = true;
+        do_par = it & 1;
+#pragma unroll
+        for (int p = 0; p < 2; ++p) tma_load_3d(sDO + p * kPanel, &tmDO, do_full, h * D + p * 64, qrow, 0);
       }
       if (!ok) {
         *abort_flag = 1;
+        const unsigned long long t0 = globaltimer_ns();
         for (int s = 0; s < 2; ++s) {
-          if (!((out_valid >> s) & 1u)) continue;
-          const unsigned long long t0 = globaltimer_ns();
-          while (!mbar_try_wait(&qdo_full[s], (out_parity >> s) & 1u))
+          if (!((q_valid >> s) & 1u)) continue;
+          while (!mbar_try_wait(&q_full[s], (q_par >> s) & 1u))
             if (globaltimer_ns() - t0 > 100000000ull) break;
         }
-        const unsigned long long t0 = globaltimer_ns();
+        while (do_pending && !mbar_try_wait(do_full, do_par))
+          if (globaltimer_ns() - t0 > 200000000ull) break;
         while (!mbar_try_wait(bar_kv, 0))
-          if (globaltimer_ns() - t0 > 100000000ull) break;
+          if (globaltimer_ns() - t0 > 300000000ull) break;
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       bool ok = mbar_wait(bar_kv, 0, abort_flag, a.err, ERR_TIMEOUT_MMA);
-      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), pd_addr = smem_u32(sPD);
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), pd_addr = smem_u32(sPD), do_addr = smem_u32(sDO);
       for (int it = 0; it < n_it && ok; ++it) {
         const int bf = it & 1;
-        const uint32_t q_addr = smem_u32(sQ + bf * TILE), do_addr = smem_u32(sDO + bf * TILE);
-        if (!mbar_wait(&qdo_full[bf], (it >> 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
+        const uint32_t q_addr = smem_u32(sQ + bf * TILE);
+        if (!mbar_wait(&q_full[bf], (it >> 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
         if (it >= 1 && !mbar_wait(s_free, (it - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)  // S^T = K Q^T
           umma_bf16(tR0, desc_kmajor(k_addr, kk), desc_kmajor(q_addr, kk), IDESC_SS, kk > 0 ? 1u : 0u);
         umma_commit(s_full);
+        if (!mbar_wait(do_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
         if (it >= 1 && !mbar_wait(dq_free, (it - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
@@ -1036,6 +1062,7 @@ __global__ void __launch_bounds__(320, 1)
         for (int kk = 0; kk < 8; ++kk)  // dV += P^T dO
           umma_bf16(tDV, desc_kmajor(pd_addr, kk), desc_mnmajor(do_addr, kk), IDESC_KV, (it > 0 || kk > 0) ? 1u : 0u);
         umma_commit(dv_done);
+        umma_commit(do_empty);  // dO read by dP^T and dV
         if (!mbar_wait(ds_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
@@ -1046,7 +1073,7 @@ __global__ void __launch_bounds__(320, 1)
           umma_bf16(tR1, desc_mnmajor(pd_addr, kk), desc_mnmajor(k_addr, kk), IDESC_Q, kk > 0 ? 1u : 0u);
         umma_commit(dq_full);
         umma_commit(pds_free);
-        umma_commit(&qdo_empty[bf]);
+        umma_commit(&q_empty[bf]);
       }
       if (ok) {
         umma_commit(kv_done);
@@ -1070,7 +1097,7 @@ __global__ void __launch_bounds__(320, 1)
       const int i = i0 + it;
       const float* lse = sLse + bf * 128;
       const float* dvec = sDv + bf * 128;
-      if (!mbar_wait_warp(&qdo_full[bf], (it >> 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      if (!mbar_wait_warp(&q_full[bf], (it >> 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
       if (!mbar_wait_warp(s_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
       tc_fence_after();
       const bool diag = a.causal && (i == kt);
@@ -1162,30 +1189,59 @@ __global__ void __launch_bounds__(320, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------------ dQ drain
+    // ------------------------------------------------------------------ dQ drain (TMA reduce-add)
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-    for (int it = 0; it < n_it; ++it) {
+    const bool issuer = (warp == 6 && lane == 0);
+    int g = 0;          // staging slices issued so far (this CTA)
+    bool ok = true;
+    for (int it = 0; it < n_it && ok; ++it) {
       const int i = i0 + it;
-      if (!mbar_wait_warp(dq_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) break;
+      if (!mbar_wait_warp(dq_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
       tc_fence_after();
-      float* dq = a.dq_acc + (long long)(b * a.T + i * 128 + r) * a.lddq + h * D;
-#pragma unroll 1
-      for (int cc = 0; cc < D / 32; ++cc) {
-        uint32_t o[32];
-        __syncwarp();
-        tmem_ld_32x32b_x32(tR1 + lane_off + cc * 32, o);
-        tmem_ld_wait();
+      uint32_t o[4][32];
 #pragma unroll
-        for (int v = 0; v < 8; ++v)
-          atomicAdd(reinterpret_cast<float4*>(dq + cc * 32) + v,
-                    make_float4(__uint_as_float(o[4 * v]) * a.scale, __uint_as_float(o[4 * v + 1]) * a.scale,
-                                __uint_as_float(o[4 * v + 2]) * a.scale, __uint_as_float(o[4 * v + 3]) * a.scale));
+      for (int cc = 0; cc < 4; ++cc) {
+        __syncwarp();
+        tmem_ld_32x32b_x32(tR1 + lane_off + cc * 32, o[cc]);
       }
+      tmem_ld_wait();
       tc_fence_before();
-      mbar_arrive(dq_free);
+      mbar_arrive(dq_free);  // R1 may take dP^T of the next tile
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc, ++g) {
+        const int sb = g & 1;
+        if (g >= 2 && !mbar_wait_warp(&stg_free[sb], ((g - 2) >> 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = sDQ + sb * STG;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {  // row r: 32 fp32 = 8 x 16 B chunks, 128-byte swizzle
+          const float4 v = make_float4(__uint_as_float(o[cc][4 * q]) * a.scale, __uint_as_float(o[cc][4 * q + 1]) * a.scale,
+                                       __uint_as_float(o[cc][4 * q + 2]) * a.scale, __uint_as_float(o[cc][4 * q + 3]) * a.scale);
+          *reinterpret_cast<float4*>(st + r * 128 + ((q ^ (r & 7)) << 4)) = v;
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&stg_full[sb]);
+        if (issuer) {
+          if (!mbar_wait(&stg_full[sb], (g >> 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) {
+            ok = false;
+          } else {
+            tma_reduce_add_3d(&tmDQ, st, h * D + cc * 32, b * a.T + i * 128, 0);
+            bulk_commit_group();
+            if (g >= 1) {
+              bulk_wait_group_read<1>();            // slice g-1 has been read from shared memory
+              mbar_arrive(&stg_free[(g - 1) & 1]);
+            }
+          }
+        }
+        ok = __all_sync(0xffffffffu, ok) != 0;
+        if (!ok) break;
+      }
     }
+    if (issuer) bulk_wait_group<0>();  // every reduce-add has completed before the CTA exits
   }
   tc_fence_before();
   __syncthreads();
@@ -1336,7 +1392,8 @@ void fa_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, 
   if (D == 128 && !serial_bwd) {
     static bool init = false;
     if (!init) { set_smem(fa_bwd2_kernel, kBwd2Smem); init = true; }
-    fa_bwd2_kernel<<<grid, 320, kBwd2Smem, s>>>(tq, tk, tv, tdo, a);
+    CUtensorMap tdq = make_tmap_f32(dq_acc.data_ptr(), cols, rows, dq_acc.stride(0), 32, 128);
+    fa_bwd2_kernel<<<grid, 320, kBwd2Smem, s>>>(tq, tk, tv, tdo, tdq, a);
   } else if (D == 128) {
     static bool init = false;
     if (!init) { set_smem(fa_bwd_kernel<128>, FaCfg<128>::BWD_SMEM); init = true; }

@@ -787,6 +787,24 @@ CUtensorMap make_tmap_bf16(const void* ptr, uint64_t inner, uint64_t outer, uint
   return m;
 }
 
+// fp32 variant (e.g. the destination of TMA bulk reduce-adds), 128-byte swizzle.
+CUtensorMap make_tmap_f32(const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                          uint32_t box_inner, uint32_t box_outer) {
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "TMA base address must be 16-byte aligned");
+  TORCH_CHECK((row_stride_elems * 4) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  TORCH_CHECK(box_inner * 4 <= 128, "128-byte swizzle: inner box of at most 32 fp32");
+  CUtensorMap m;
+  cuuint64_t dims[3] = {inner, outer, 1};
+  cuuint64_t strides[2] = {row_stride_elems * 4, row_stride_elems * outer * 4};
+  cuuint32_t box[3] = {box_inner, box_outer, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(ptr), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (fp32) failed with code ", int(r));
+  return m;
+}
+
 int num_sms(int dev) {
   static int cache[64] = {0};
   if (!cache[dev]) {
