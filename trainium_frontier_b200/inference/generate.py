@@ -90,7 +90,7 @@ class Generator:
         h = torch.empty_like(x)
         rstd = torch.empty(M, dtype=torch.float32, device=self.dev)
         C().mix_norm_fwd(x, x0, self.lam[i][0], self.lam[i][1], xm, h, rstd)
-        qkv = gemm.linear_fwd(h, self.wqkv[i])
+        qkv = gemm.linear_fwd(h, self.wqkv[i]) if prefill else gemm.linear_small_m(h, self.wqkv[i]).to(torch.bfloat16)
         qkn = torch.empty((M, 2 * Cd), dtype=torch.bfloat16, device=self.dev)
         C().rope_norm_fwd(qkv, 0, 2 * H, D, self.cos, self.sin, T, 0, None, qkn, pos_t)
         if prefill:
@@ -102,15 +102,25 @@ class Generator:
             C().kv_append(qkn[:, Cd:], qkv[:, 2 * Cd:], self.kc[i], self.vc[i], self.counters[0:1])
             y = torch.empty((M, Cd), dtype=torch.bfloat16, device=self.dev)
             C().decode_attn(qkn[:, :Cd], self.kc[i], self.vc[i], self.counters[1:2], H, D, self.scale, y)
-        x = gemm.linear_fwd(y, self.wo[i], residual=xm)
+        if prefill:
+            x = gemm.linear_fwd(y, self.wo[i], residual=xm)
+            h2 = torch.empty_like(x)
+            C().rmsnorm_fwd(x, h2, None)
+            act, _ = gemm.linear_relu2_fwd(h2, self.wfc[i], tau=self.tau)
+            return gemm.linear_fwd(act, self.wp[i], residual=x)
+        # decode: a few rows per step -> split-K GEMMs over every SM, fp32 partial sums
+        x = (gemm.linear_small_m(y, self.wo[i]) + xm.float()).to(torch.bfloat16)
         h2 = torch.empty_like(x)
         C().rmsnorm_fwd(x, h2, None)
-        act, _ = gemm.linear_relu2_fwd(h2, self.wfc[i], tau=self.tau)
-        return gemm.linear_fwd(act, self.wp[i], residual=x)
+        hf = gemm.linear_small_m(h2, self.wfc[i]).to(torch.bfloat16).float() - self.tau
+        act = torch.relu(hf).square().to(torch.bfloat16)
+        return (gemm.linear_small_m(act, self.wp[i]) + x.float()).to(torch.bfloat16)
 
     def _head(self, x):
         xf = torch.empty_like(x)
         C().rmsnorm_fwd(x, xf, None)
+        if x.shape[0] <= 64:
+            return gemm.linear_small_m(xf, self.wlm).to(torch.bfloat16)
         return gemm.linear_fwd(xf, self.wlm)
 
     def _embed(self, idx):

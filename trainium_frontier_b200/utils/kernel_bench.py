@@ -119,6 +119,10 @@ def one_kernel(case: str, dev):
         x = torch.randn(16384, 1280, device=dev, dtype=torch.bfloat16)
         w = torch.randn(5120, 1280, device=dev, dtype=torch.bfloat16)
         fn = lambda: gemm.linear_fwd(x, w)
+    elif case == "gemm_relu2":
+        x = torch.randn(16384, 1280, device=dev, dtype=torch.bfloat16)
+        w = torch.randn(5120, 1280, device=dev, dtype=torch.bfloat16)
+        fn = lambda: gemm.linear_relu2_fwd(x, w)
     elif case == "gemm_dw":
         dy = torch.randn(16384, 5120, device=dev, dtype=torch.bfloat16)
         x = torch.randn(16384, 1280, device=dev, dtype=torch.bfloat16)
@@ -139,7 +143,7 @@ def one_kernel(case: str, dev):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("what", nargs="?", default="gemm")
-    ap.add_argument("--one", default="", help="run one small case: gemm | gemm_dw | fa_fwd | fa_bwd")
+    ap.add_argument("--one", default="", help="run one small case: gemm | gemm_relu2 | gemm_dw | fa_fwd | fa_bwd")
     ap.add_argument("--json", default="")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
