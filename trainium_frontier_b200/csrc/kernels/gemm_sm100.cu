@@ -87,6 +87,7 @@ struct GemmArgs {
   const __nv_bfloat16* R;
   long long ldr, r_bstride;
   int* err;
+  int tma_store;  // bf16 outputs leave through TMA stores of staged 32 x 64 slabs
   TpArgs tp;
 };
 
@@ -99,7 +100,7 @@ struct GemmCfg {
   static constexpr uint32_t TMEM_COLS = 2 * BN;
   static constexpr int QSLOTS = 4;  // tile-id ring
   static constexpr size_t SMEM = 1024 + STAGES * (A_BYTES + B_BYTES) + (2 * STAGES + 5 + 2 * QSLOTS) * 8 + 64;
-  static constexpr size_t SMEM_RS = SMEM + 128 + 8 * 4096;  // + epilogue staging tiles
+  static constexpr size_t SMEM_ALL = SMEM + 1024 + 8 * 4096;  // + epilogue staging tiles
 };
 
 template <int MODE>
@@ -180,6 +181,7 @@ struct ModeThreads {
 template <int BN, bool A_MN, bool B_MN, int EPI, int MODE>
 __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmD2,
                      const __grid_constant__ GemmArgs args) {
   using C = GemmCfg<BN>;
   constexpr int BM = C::BM, BK = C::BK, STAGES = C::STAGES, QS = C::QSLOTS;
@@ -200,8 +202,9 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(qtile + QS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* copy_word = reinterpret_cast<volatile int*>(tmem_slot + 2);
-  // MODE_RS: per-epilogue-warp staging tile [32 rows][64 cols] bf16 (4 KB each, 8 warps)
-  uint8_t* staging = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tmem_slot + 4) + 127) & ~uintptr_t(127));
+  // per-epilogue-warp staging tile [32 rows][64 cols] bf16 (4 KB each, 8 warps), 1 KB
+  // aligned: the 128-byte-swizzled layout TMA stores read
+  uint8_t* staging = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tmem_slot + 4) + 1023) & ~uintptr_t(1023));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -531,6 +534,110 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
             st_release_sys_u32(args.tp.rs_flag[owner] + ((long long)rank * tiles_per_rank + tile_local) * 8 + hf * 4 + q,
                                args.tp.epoch);
         }
+      } else if (EPI != EPI_F32 && args.tma_store) {
+        // ---- bf16 outputs through TMA stores: each warp stages its 32 rows x 64 columns
+        // (128-byte swizzle) and one lane stores the slab, so global writes are whole lines
+        // instead of 32 rows touched per store instruction.
+        uint8_t* stg = staging + (warp - 2) * 4096;
+        const int row0 = mb * BM + q * 32;
+        const bool row_ok = row < args.M;
+        auto stage = [&](const float* v) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint4 u;
+            u.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+            u.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+            u.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+            u.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+            *reinterpret_cast<uint4*>(stg + lane * 128 + ((j ^ (lane & 7)) << 4)) = u;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+        };
+        auto store = [&](const CUtensorMap* map, int col0) {
+          if (lane == 0 && row0 < args.M) {  // rows past M are clipped by TMA; skip all-outside slabs
+            tma_store_3d(map, stg, col0, row0, bi);
+            bulk_commit_group();
+            bulk_wait_group_read<0>();  // the slab may be overwritten after this
+          }
+          __syncwarp();
+        };
+#pragma unroll 1
+        for (int s2 = hf * (BN / 128); s2 < (hf + 1) * (BN / 128); ++s2) {
+          uint32_t r0[32], r1[32];
+          __syncwarp();
+          tmem_ld_32x32b_x32(tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN + s2 * 64), r0);
+          tmem_ld_32x32b_x32(tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN + s2 * 64 + 32), r1);
+          tmem_ld_wait();
+          const int col0 = nb * BN + s2 * 64;
+          if (col0 >= args.N) continue;
+          float v[64];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            v[i] = __uint_as_float(r0[i]) * alpha;
+            v[32 + i] = __uint_as_float(r1[i]) * alpha;
+          }
+          if constexpr (EPI == EPI_BF16) {
+            if (args.R != nullptr && row_ok) {
+              const __nv_bfloat16* rr = args.R + bi * args.r_bstride + (long long)row * args.ldr + col0;
+              const float rc = args.rcoef;
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                if (col0 + 8 * i < args.N) {  // N % 8 == 0 on this path
+                  const uint4 u = reinterpret_cast<const uint4*>(rr)[i];
+                  const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) {
+                    const float2 f = __bfloat1622float2(h2[j]);
+                    v[8 * i + 2 * j] += rc * f.x;
+                    v[8 * i + 2 * j + 1] += rc * f.y;
+                  }
+                }
+              }
+            }
+          } else if constexpr (EPI == EPI_RELU2) {
+            stage(v);                      // pre-activation h
+            store(&tmD2, col0);
+#pragma unroll
+            for (int i = 0; i < 64; ++i) {
+              const float h = __bfloat162float(__float2bfloat16_rn(v[i])) - args.tau;
+              const float rl = h > 0.f ? h : 0.f;
+              v[i] = rl * rl;
+            }
+          } else if constexpr (EPI == EPI_RELU2_BWD) {
+            float hf8[64];
+            if (row_ok) {
+              const __nv_bfloat16* hh = args.R + bi * args.r_bstride + (long long)row * args.ldr + col0;
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                uint4 u = make_uint4(0u, 0u, 0u, 0u);
+                if (col0 + 8 * i < args.N) u = reinterpret_cast<const uint4*>(hh)[i];
+                const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const float2 f = __bfloat1622float2(h2[j]);
+                  hf8[8 * i + 2 * j] = f.x;
+                  hf8[8 * i + 2 * j + 1] = f.y;
+                }
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 64; ++i) hf8[i] = 0.f;
+            }
+#pragma unroll
+            for (int i = 0; i < 64; ++i) {
+              const float g = __bfloat162float(__float2bfloat16_rn(v[i]));
+              const float h = hf8[i] - args.tau;
+              v[i] = h > 0.f ? g * (2.f * h) : 0.f;
+            }
+          }
+          stage(v);
+          store(&tmD, col0);
+        }
+        if (lane == 0) bulk_wait_group<0>();
+        __syncwarp();
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
       } else {
         const bool row_ok = row < args.M;
 #pragma unroll 1
@@ -816,25 +923,25 @@ int num_sms(int dev) {
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI, int MODE = MODE_PLAIN>
-static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid,
-                        cudaStream_t stream) {
+static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const CUtensorMap& td2,
+                        const GemmArgs& a, int grid, cudaStream_t stream) {
   using C = GemmCfg<BN>;
   auto kern = gemm_bf16_kernel<BN, A_MN, B_MN, EPI, MODE>;
-  constexpr size_t smem = MODE == MODE_RS ? C::SMEM_RS : C::SMEM;
+  constexpr size_t smem = C::SMEM_ALL;
   static bool attr_set = false;  // one per instantiation
   if (!attr_set) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr_set = true;
   }
-  kern<<<grid, ModeThreads<MODE>::value, smem, stream>>>(ta, tb, a);
+  kern<<<grid, ModeThreads<MODE>::value, smem, stream>>>(ta, tb, td, td2, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 template <int BN>
 static void dispatch(bool a_mn, bool b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
-                     const GemmArgs& a, int grid, cudaStream_t s) {
+                     const CUtensorMap& td, const CUtensorMap& td2, const GemmArgs& a, int grid, cudaStream_t s) {
 #define TFB_CASE(AM, BM_, E) \
-  if (a_mn == AM && b_mn == BM_ && epi == E) return launch_gemm<BN, AM, BM_, E>(ta, tb, a, grid, s);
+  if (a_mn == AM && b_mn == BM_ && epi == E) return launch_gemm<BN, AM, BM_, E>(ta, tb, td, td2, a, grid, s);
   TFB_CASE(false, false, EPI_BF16)
   TFB_CASE(false, false, EPI_RELU2)
   TFB_CASE(false, false, EPI_F32)
@@ -851,9 +958,9 @@ static void dispatch(bool a_mn, bool b_mn, int epi, const CUtensorMap& ta, const
 
 template <int BN>
 static void dispatch_tp(int mode, bool b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
-                        const GemmArgs& a, int grid, cudaStream_t s) {
+                        const CUtensorMap& td, const CUtensorMap& td2, const GemmArgs& a, int grid, cudaStream_t s) {
 #define TFB_TP(MD, BM_, E) \
-  if (mode == MD && b_mn == BM_ && epi == E) return launch_gemm<BN, false, BM_, E, MD>(ta, tb, a, grid, s);
+  if (mode == MD && b_mn == BM_ && epi == E) return launch_gemm<BN, false, BM_, E, MD>(ta, tb, td, td2, a, grid, s);
   TFB_TP(MODE_AG, false, EPI_BF16)
   TFB_TP(MODE_AG, false, EPI_RELU2)
   TFB_TP(MODE_AG, true, EPI_BF16)
@@ -862,6 +969,19 @@ static void dispatch_tp(int mode, bool b_mn, int epi, const CUtensorMap& ta, con
   TFB_TP(MODE_RS, true, EPI_BF16)
 #undef TFB_TP
   TORCH_CHECK(false, "unsupported tensor-parallel gemm variant mode=", mode, " b_mn=", b_mn, " epi=", epi);
+}
+
+// The TMA-store epilogue needs 16-byte aligned rows and whole 8-column groups.
+static bool tma_store_ok(int64_t epi, int64_t N, const void* d, long long ldd, long long dbs, const void* d2,
+                         long long ldd2, long long d2bs) {
+  static const bool off = getenv("TFB_GEMM_NO_TMA_STORE") != nullptr;
+  if (off || epi == EPI_F32 || N % 8 != 0) return false;
+  auto ok = [](const void* p, long long ld, long long bs) {
+    return p != nullptr && (reinterpret_cast<uintptr_t>(p) & 15) == 0 && (ld * 2) % 16 == 0 && (bs * 2) % 16 == 0;
+  };
+  if (!ok(d, ldd, dbs)) return false;
+  if (epi == EPI_RELU2 && !ok(d2, ldd2, d2bs)) return false;
+  return true;
 }
 
 // A: if !a_mn a [M, K] view (row stride lda), else a [K, M] view.  B likewise with N.
@@ -931,10 +1051,16 @@ void gemm_bf16(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_mn, int64_t M
   }
   TORCH_CHECK(epi != EPI_RELU2_BWD || a.R != nullptr, "RELU2_BWD needs R = pre-activation");
   a.err = err.data_ptr<int>();
+  CUtensorMap td = ta, td2 = ta;
+  a.tma_store = tma_store_ok(epi, N, D.data_ptr(), a.ldd, d_bs, epi == EPI_RELU2 ? a.D2 : nullptr, a.ldd2, a.d2_bstride);
+  if (a.tma_store) {
+    td = make_tmap_bf16(a.D, N, M, a.ldd, 64, 32, nb, d_bs);
+    if (epi == EPI_RELU2) td2 = make_tmap_bf16(a.D2, N, M, a.ldd2, 64, 32, nb, a.d2_bstride);
+  }
   const int grid = std::min(a.num_tiles, num_sms(A.get_device()));
   cudaStream_t s = at::cuda::getCurrentCUDAStream();
-  if (bn == 256) dispatch<256>(a_mn, b_mn, (int)epi, ta, tb, a, grid, s);
-  else dispatch<128>(a_mn, b_mn, (int)epi, ta, tb, a, grid, s);
+  if (bn == 256) dispatch<256>(a_mn, b_mn, (int)epi, ta, tb, td, td2, a, grid, s);
+  else dispatch<128>(a_mn, b_mn, (int)epi, ta, tb, td, td2, a, grid, s);
 }
 
 // Tensor-parallel GEMMs with the collective fused in (MODE_AG / MODE_RS), A K-major.
@@ -1026,10 +1152,17 @@ void gemm_tp(int64_t mode, torch::Tensor A, torch::Tensor B, bool b_mn, int64_t 
       tp.rs_flag[r] = reinterpret_cast<uint32_t*>(rs_flag[r]);
     }
   }
+  CUtensorMap td = ta, td2 = ta;
+  a.tma_store = 0;
+  if (mode == MODE_AG && tma_store_ok(epi, N, a.D, a.ldd, 0, epi == EPI_RELU2 ? a.D2 : nullptr, a.ldd2, 0)) {
+    a.tma_store = 1;
+    td = make_tmap_bf16(a.D, N, M, a.ldd, 64, 32, 1, 0);
+    if (epi == EPI_RELU2) td2 = make_tmap_bf16(a.D2, N, M, a.ldd2, 64, 32, 1, 0);
+  }
   const int grid = std::min(a.num_tiles, num_sms(A.get_device()));
   cudaStream_t s = at::cuda::getCurrentCUDAStream();
-  if (bn == 256) dispatch_tp<256>((int)mode, b_mn, (int)epi, ta, tb, a, grid, s);
-  else dispatch_tp<128>((int)mode, b_mn, (int)epi, ta, tb, a, grid, s);
+  if (bn == 256) dispatch_tp<256>((int)mode, b_mn, (int)epi, ta, tb, td, td2, a, grid, s);
+  else dispatch_tp<128>((int)mode, b_mn, (int)epi, ta, tb, td, td2, a, grid, s);
 }
 
 }  // namespace tfb

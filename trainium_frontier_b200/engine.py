@@ -273,7 +273,8 @@ class TrainEngine:
         self.grad_accum = grad_accum
         self.rank, self.world = world()
         if grad_sync == "auto":
-            grad_sync = "dist_muon" if self.world > 1 else "none"
+            # the NVLink kernels over symmetric memory on GPUs, NCCL collectives elsewhere
+            grad_sync = ("fused" if device.type == "cuda" else "dist_muon") if self.world > 1 else "none"
         if grad_sync == "fused" and (device.type != "cuda" or self.world < 2):
             grad_sync = "dist_muon" if self.world > 1 else "none"
         if self.world == 1:
