@@ -93,7 +93,8 @@ class RunConfig:
     device_type: str = ""
     seed: int = 42
     init_from: str = ""
-    resume_from: str = ""
+    resume_from: str = ""           # a resume file, or a directory of resume_rank{r}.pt files
+    save_every: int = 0             # write <out_dir>/resume/resume_rank{r}.pt every N steps (0 = never)
     compile_only: bool = False
     log_every: int = 10
     # ---- optimizer -----------------------------------------------------------------

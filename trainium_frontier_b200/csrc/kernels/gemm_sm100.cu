@@ -88,6 +88,12 @@ struct GemmArgs {
   long long ldr, r_bstride;
   int* err;
   int tma_store;  // bf16 outputs leave through TMA stores of staged 32 x 64 slabs
+  // split-K finish (EPI_F32 with split_k > 1): the last split to add into a warp's region
+  // of the fp32 workspace D writes bf16(D (+ rcoef R) | relu2(D)) to fin_out and re-zeroes D
+  __nv_bfloat16* fin_out;
+  long long ld_fin;
+  int* fin_cnt;
+  int fin_relu2;
   TpArgs tp;
 };
 
@@ -171,6 +177,44 @@ __device__ __forceinline__ bool wait_epoch(const uint32_t* flag, uint32_t epoch,
       }
     }
   }
+}
+
+// Split-K finish of one warp's region (32 rows x half the tile's columns): counts the
+// splits that have added into it; the last one converts the fp32 sums to the bf16 output
+// (optionally + residual or relu^2) and zeroes the workspace and the counter, so the next
+// launch starts clean without a memset (CUDA-graph friendly decode GEMMs).
+template <int BN>
+__device__ __noinline__ void split_finish(const GemmArgs& a, int mb, int nb, int bi, int q, int hf, int warp, int lane) {
+  __threadfence();  // this lane's partial-sum atomics are visible before the count moves
+  __syncwarp();
+  int last = 0;
+  const long long slot = (((long long)bi * a.tiles_m + mb) * a.tiles_n + nb) * 8 + (warp - 2);
+  if (lane == 0) last = atomicAdd(a.fin_cnt + slot, 1) == a.split_k - 1;
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return;
+  __threadfence();
+  const int row = mb * 128 + q * 32 + lane;
+  if (row < a.M) {
+    float* ws = reinterpret_cast<float*>(a.D) + bi * a.d_bstride + (long long)row * a.ldd;
+    __nv_bfloat16* out = a.fin_out + (long long)row * a.ld_fin;
+    for (int c = hf * (BN / 64); c < (hf + 1) * (BN / 64); ++c) {
+      const int col0 = nb * BN + c * 32;
+      if (col0 >= a.N) break;
+      const int n = min(32, a.N - col0);
+      for (int i = 0; i < n; ++i) {
+        float v = __ldcg(ws + col0 + i);
+        ws[col0 + i] = 0.f;
+        if (a.R != nullptr) v += a.rcoef * __bfloat162float(a.R[(long long)row * a.ldr + col0 + i]);
+        if (a.fin_relu2) {
+          const float h = __bfloat162float(__float2bfloat16_rn(v)) - a.tau;
+          v = h > 0.f ? h * h : 0.f;
+        }
+        out[col0 + i] = __float2bfloat16_rn(v);
+      }
+    }
+  }
+  __syncwarp();
+  if (lane == 0) a.fin_cnt[slot] = 0;
 }
 
 template <int MODE>
@@ -766,6 +810,9 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
 
         tc_fence_before();
         mbar_arrive(&tempty[acc]);
+        if constexpr (EPI == EPI_F32) {
+          if (args.fin_out != nullptr) split_finish<BN>(args, mb, nb, bi, q, hf, warp, lane);
+        }
       }
       if (++acc == 2) {
         acc = 0;
@@ -1061,6 +1108,52 @@ void gemm_bf16(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_mn, int64_t M
   cudaStream_t s = at::cuda::getCurrentCUDAStream();
   if (bn == 256) dispatch<256>(a_mn, b_mn, (int)epi, ta, tb, td, td2, a, grid, s);
   else dispatch<128>(a_mn, b_mn, (int)epi, ta, tb, td, td2, a, grid, s);
+}
+
+// Few-row GEMM (decode): out[M, N] bf16 = x[M, K] W[N, K]^T (+ R | relu^2), K split over the
+// SMs, partial sums added (vector atomics) into the zero-initialised fp32 workspace ws
+// [M, N]; the last split of each region finishes it and re-zeroes ws / cnt (int32, >=
+// tiles * 8 words, zero-initialised once).
+void gemm_splitk_fin(torch::Tensor A, torch::Tensor B, torch::Tensor ws, torch::Tensor cnt, torch::Tensor out,
+                     c10::optional<torch::Tensor> R, bool relu2, double tau, int64_t split, torch::Tensor err) {
+  TORCH_CHECK(A.is_cuda() && A.dim() == 2 && B.dim() == 2 && A.stride(1) == 1 && B.stride(1) == 1, "2-D operands");
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "bf16 inputs");
+  const int64_t M = A.size(0), K = A.size(1), N = B.size(0);
+  TORCH_CHECK(B.size(1) == K, "K mismatch");
+  TORCH_CHECK(ws.scalar_type() == at::kFloat && ws.is_contiguous() && ws.size(0) >= M && ws.size(1) == N, "ws fp32 [M, N]");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.stride(1) == 1 && out.size(0) >= M && out.size(1) >= N, "out bf16 [M, N]");
+  const int BM = 128, BK = 64, bn = 128;
+  c10::cuda::CUDAGuard guard(A.device());
+  CUtensorMap ta = make_tmap_bf16(A.data_ptr(), K, M, A.stride(0), 64, BM, 1, 0);
+  CUtensorMap tb = make_tmap_bf16(B.data_ptr(), K, N, B.stride(0), 64, bn, 1, 0);
+  GemmArgs a{};
+  a.M = (int)M; a.N = (int)N; a.K = (int)K;
+  a.tiles_m = (int)((M + BM - 1) / BM);
+  a.tiles_n = (int)((N + bn - 1) / bn);
+  a.kb_total = (int)((K + BK - 1) / BK);
+  int sk = (int)std::max<int64_t>(1, std::min<int64_t>(split, a.kb_total));
+  a.kb_per_split = (a.kb_total + sk - 1) / sk;
+  sk = (a.kb_total + a.kb_per_split - 1) / a.kb_per_split;
+  TORCH_CHECK(sk > 1, "split-K finish needs at least two splits");
+  a.split_k = sk;
+  a.batch = 1;
+  a.num_tiles = a.tiles_m * a.tiles_n * sk;
+  TORCH_CHECK(cnt.scalar_type() == at::kInt && cnt.numel() >= (int64_t)a.tiles_m * a.tiles_n * 8, "cnt int32 [tiles * 8]");
+  a.alpha = 1.f; a.beta = 1.f; a.tau = (float)tau; a.rcoef = 1.f;
+  a.alpha_ptr = nullptr;
+  a.D = ws.data_ptr(); a.ldd = ws.stride(0); a.d_bstride = 0;
+  a.D2 = nullptr; a.ldd2 = 0; a.d2_bstride = 0; a.R = nullptr; a.ldr = 0; a.r_bstride = 0;
+  if (R.has_value()) {
+    TORCH_CHECK(R->scalar_type() == at::kBFloat16 && R->stride(-1) == 1, "R must be bf16 row-major");
+    a.R = reinterpret_cast<const __nv_bfloat16*>(R->data_ptr()); a.ldr = R->stride(0);
+  }
+  a.err = err.data_ptr<int>();
+  a.tma_store = 0;
+  a.fin_out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr()); a.ld_fin = out.stride(0);
+  a.fin_cnt = cnt.data_ptr<int>();
+  a.fin_relu2 = relu2 ? 1 : 0;
+  const int grid = std::min(a.num_tiles, num_sms(A.get_device()));
+  dispatch<128>(false, false, EPI_F32, ta, tb, ta, ta, a, grid, at::cuda::getCurrentCUDAStream());
 }
 
 // Tensor-parallel GEMMs with the collective fused in (MODE_AG / MODE_RS), A K-major.

@@ -69,6 +69,7 @@ class Generator:
         self.idx = torch.zeros(self.B, 1, dtype=torch.int32, device=dev)
         self.graph = None
         self.tokens = None
+        self.ws: dict = {}   # decode GEMM workspaces (zeroed fp32 sums + counters) per shape
         blocks = list(model.transformer.h)
         self.wqkv = [torch.cat([w16(b.attn.c_q.weight), w16(b.attn.c_k.weight), w16(b.attn.c_v.weight)], 0).contiguous()
                      for b in blocks]
@@ -90,7 +91,7 @@ class Generator:
         h = torch.empty_like(x)
         rstd = torch.empty(M, dtype=torch.float32, device=self.dev)
         C().mix_norm_fwd(x, x0, self.lam[i][0], self.lam[i][1], xm, h, rstd)
-        qkv = gemm.linear_fwd(h, self.wqkv[i]) if prefill else gemm.linear_small_m(h, self.wqkv[i]).to(torch.bfloat16)
+        qkv = gemm.linear_fwd(h, self.wqkv[i]) if prefill else gemm.linear_decode(h, self.wqkv[i], self.ws)
         qkn = torch.empty((M, 2 * Cd), dtype=torch.bfloat16, device=self.dev)
         C().rope_norm_fwd(qkv, 0, 2 * H, D, self.cos, self.sin, T, 0, None, qkn, pos_t)
         if prefill:
@@ -108,19 +109,18 @@ class Generator:
             C().rmsnorm_fwd(x, h2, None)
             act, _ = gemm.linear_relu2_fwd(h2, self.wfc[i], tau=self.tau)
             return gemm.linear_fwd(act, self.wp[i], residual=x)
-        # decode: a few rows per step -> split-K GEMMs over every SM, fp32 partial sums
-        x = (gemm.linear_small_m(y, self.wo[i]) + xm.float()).to(torch.bfloat16)
+        # decode: a few rows per step -> one split-K GEMM launch each (epilogue fused)
+        x = gemm.linear_decode(y, self.wo[i], self.ws, residual=xm)
         h2 = torch.empty_like(x)
         C().rmsnorm_fwd(x, h2, None)
-        hf = gemm.linear_small_m(h2, self.wfc[i]).to(torch.bfloat16).float() - self.tau
-        act = torch.relu(hf).square().to(torch.bfloat16)
-        return (gemm.linear_small_m(act, self.wp[i]) + x.float()).to(torch.bfloat16)
+        act = gemm.linear_decode(h2, self.wfc[i], self.ws, relu2=True, tau=self.tau)
+        return gemm.linear_decode(act, self.wp[i], self.ws, residual=x)
 
     def _head(self, x):
         xf = torch.empty_like(x)
         C().rmsnorm_fwd(x, xf, None)
         if x.shape[0] <= 64:
-            return gemm.linear_small_m(xf, self.wlm).to(torch.bfloat16)
+            return gemm.linear_decode(xf, self.wlm, self.ws)
         return gemm.linear_fwd(xf, self.wlm)
 
     def _embed(self, idx):

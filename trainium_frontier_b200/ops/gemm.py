@@ -117,6 +117,28 @@ def linear_small_m(x: torch.Tensor, w: torch.Tensor, ws: torch.Tensor | None = N
     return _gemm(x2, False, w2, False, M, N, K, ws, EPI_F32, beta=0.0, split_k=split, bn=bn)
 
 
+def linear_decode(x: torch.Tensor, w: torch.Tensor, cache: dict, residual: torch.Tensor | None = None,
+                  relu2: bool = False, tau: float = 0.0) -> torch.Tensor:
+    """bf16 x @ W^T (+ residual | relu(. - tau)^2) for a few rows in ONE launch: split-K over
+    the SMs into an fp32 workspace that the last split of each region converts and
+    re-zeroes (``cache`` keeps one zeroed workspace + counter set per shape; safe inside
+    CUDA graphs since nothing is allocated or memset per call)."""
+    x2, w2 = _c2(x), _c2(w)
+    M, K = x2.shape
+    N = w2.shape[0]
+    key = (M, N, K, x.device)
+    if key not in cache:
+        tiles = math.ceil(M / 128) * math.ceil(N / 128)
+        cache[key] = (torch.zeros((M, N), dtype=torch.float32, device=x.device),
+                      torch.zeros(tiles * 8, dtype=torch.int32, device=x.device),
+                      max(2, min(math.ceil(K / 64), num_sms(x.device) // max(1, tiles))))
+    ws, cnt, split = cache[key]
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    C().gemm_splitk_fin(x2, w2, ws, cnt, out, None if residual is None else _c2(residual), bool(relu2),
+                        float(tau), int(split), err_word(x.device))
+    return out
+
+
 def linear_dw(dy: torch.Tensor, x: torch.Tensor, out: torch.Tensor, accumulate: bool = True,
               alpha: float = 1.0, split_k: int | None = None, alpha_t=None) -> torch.Tensor:
     """out[N,K] (fp32) (+)= alpha * dy^T x."""

@@ -92,6 +92,63 @@ class Trainer:
         else:
             self.byte_w = None
 
+    # ------------------------------------------------------------------ resume
+    def resume_state(self) -> dict:
+        """Everything an exact continuation needs: weights, optimizer state (including the
+        distributed-Muon owner shards of this rank), counters, RNG and the loader cursor."""
+        params = list(self.model.parameters())
+        index = {id(p): i for i, p in enumerate(params)}
+
+        def cpu(v):
+            return v.detach().cpu().clone() if torch.is_tensor(v) else v
+
+        opt_state = {index[id(p)]: {k: cpu(v) for k, v in st.items()} for p, st in self.opt.state.items()
+                     if id(p) in index}
+        dm = self.engine.dist_muon
+        dm_state = {index[k]: {kk: cpu(vv) for kk, vv in st.items()} for k, st in dm.state.items()} \
+            if dm is not None else {}
+        return {"model_state": {k: v.detach().cpu().clone() for k, v in self.model.state_dict().items()},
+                "optimizer": opt_state, "dist_muon": dm_state, "step": self.step_idx,
+                "loss_scale": self.loss_scale, "loss_scale_clean": self.loss_scale_clean,
+                "loader_batches": self.loader.i if self.loader is not None else 0,
+                "rng_cpu": torch.get_rng_state(),
+                "rng_cuda": torch.cuda.get_rng_state(self.device) if self.device.type == "cuda" else None,
+                "world": self.world, "rank": self.rank}
+
+    def save_resume(self, path) -> None:
+        path = Path(path)
+        path.parent.mkdir(parents=True, exist_ok=True)
+        tmp = path.with_suffix(path.suffix + ".tmp")
+        torch.save(self.resume_state(), tmp)
+        os.replace(tmp, path)
+
+    def load_resume(self, path) -> None:
+        st = torch.load(path, map_location="cpu", weights_only=False)
+        if st["world"] != self.world:
+            raise ValueError(f"resume file was written by a world of {st['world']} ranks, not {self.world}")
+        with torch.no_grad():
+            self.model.load_state_dict(st["model_state"], strict=True)   # copies into the flat buffers
+        params = list(self.model.parameters())
+        for i, d in st["optimizer"].items():
+            tgt = self.opt.state[params[i]]
+            for k, v in d.items():
+                tgt[k] = v.to(self.device) if torch.is_tensor(v) else v
+        dm = self.engine.dist_muon
+        if dm is not None:
+            for i, d in st["dist_muon"].items():
+                dm.state[id(params[i])] = {k: v.to(self.device) for k, v in d.items()}
+        self.engine.layout.refresh_bf16()
+        if self.tpc is not None:
+            self.tpc.weights_version += 1
+        self.step_idx = st["step"]
+        self.loss_scale, self.loss_scale_clean = st["loss_scale"], st["loss_scale_clean"]
+        if self.loader is not None:
+            for _ in range(st["loader_batches"] - self.loader.i):   # the stream is deterministic
+                self.loader.next()
+        torch.set_rng_state(st["rng_cpu"])
+        if st.get("rng_cuda") is not None and self.device.type == "cuda":
+            torch.cuda.set_rng_state(st["rng_cuda"], self.device)
+
     @property
     def h2d_bytes_per_step(self) -> int:
         return self.grad_accum * self.rows_per_micro * (self.cfg.seq_len + 1) * 4
@@ -155,6 +212,10 @@ def run(cfg: RunConfig) -> dict:
     ddp, rank, local_rank, world_size, device = init_runtime(device_type, cfg.seed)
     print0(f"config: {json.dumps(cfg.model_config().__dict__)}")
     tr = Trainer(cfg, device, rank, world_size)
+    if cfg.resume_from:
+        tr.load_resume(Path(cfg.resume_from) / f"resume_rank{rank}.pt" if Path(cfg.resume_from).is_dir()
+                       else cfg.resume_from)
+        print0(f"resumed at step {tr.step_idx}")
     nparams = sum(p.numel() for p in tr.model.parameters())
     flops_per_token = tr.model.estimate_flops()
     print0(f"num_params={nparams:,} flops_per_token={flops_per_token:e} grad_accum={tr.grad_accum} "
@@ -172,8 +233,8 @@ def run(cfg: RunConfig) -> dict:
     budget_started = loop_started
     recent: list[float] = []
     smooth = 0.0
-    total_tokens = 0
-    step = 0
+    total_tokens = tr.step_idx * tr.tokens_per_step
+    step = tr.step_idx
     gc.collect()
     while step < cfg.num_steps:
         elapsed = time.monotonic() - budget_started
@@ -213,6 +274,8 @@ def run(cfg: RunConfig) -> dict:
             print0(f"step {step:05d} | loss {deb:.4f} | dt {dt:.3f}s | tok/s {tr.tokens_per_step / max(dt, 1e-9):,.0f} "
                    f"| mfu {flops_per_token * tr.tokens_per_step / max(dt, 1e-9) / 1e12:.0f} TF/s", flush=True)
         step += 1
+        if cfg.save_every > 0 and step % cfg.save_every == 0:
+            tr.save_resume(Path(cfg.out_dir) / "resume" / f"resume_rank{rank}.pt")
         if int(control[1].item()):
             break
     out = Path(cfg.out_dir) / "final.pt"
