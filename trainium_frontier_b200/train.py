@@ -296,13 +296,32 @@ def run(cfg: RunConfig) -> dict:
         tr.model.disable_tp()
         tok = syn.SyntheticTokenizer(cfg.vocab_size)
         causal = causality_check(tr.model, tok, cfg.device_batch_size, cfg.seq_len, device)
-        res = evaluate_bpb(tr.model, tok, max(1, cfg.device_batch_size * cfg.pack_factor), cfg.seq_len, device,
-                           max_tokens=cfg.eval_tokens)
+        rows = max(1, cfg.device_batch_size * cfg.pack_factor)
+        res = evaluate_bpb(tr.model, tok, rows, cfg.seq_len, device, max_tokens=cfg.eval_tokens)
+        extra = {}
+        if cfg.eval_seq_len > 0 and cfg.eval_seq_len != cfg.seq_len:
+            alt = evaluate_bpb(tr.model, tok, rows, cfg.eval_seq_len, device, max_tokens=cfg.eval_tokens)
+            extra.update(eval_alt_seq_len=cfg.eval_seq_len, val_bpb_alt=alt["val_bpb"], eval_alt_seconds=alt["eval_seconds"])
+        if ema_shadows is not None:
+            live = [p.detach().clone() for p in tr.model.parameters()]
+            with torch.no_grad():
+                for p, e in zip(tr.model.parameters(), ema_shadows[0]):
+                    p.copy_(e)
+            tr.engine.layout.refresh_bf16()
+            ema = evaluate_bpb(tr.model, tok, rows, cfg.seq_len, device, max_tokens=cfg.eval_tokens)
+            extra.update(val_bpb_ema=ema["val_bpb"], weight_ema_updates=ema_updates)
+            with torch.no_grad():
+                for p, v in zip(tr.model.parameters(), live):
+                    p.copy_(v)
+            tr.engine.layout.refresh_bf16()
         print0("---")
         print0(f"val_bpb: {res['val_bpb']:.6f}")
         print0(f"causality_passed: {causal['passed']}")
         print0(f"causality_max_abs: {causal['max_abs_diff']:.3e}")
         print0(f"eval_tokens: {res['num_tokens']}")
+        print0(f"eval_seconds: {res['eval_seconds']:.2f}")
+        for k, v in extra.items():
+            print0(f"{k}: {v:.6f}" if isinstance(v, float) else f"{k}: {v}")
     print0(f"steps: {step}")
     print0(f"total_train_tokens: {total_tokens}")
     print0(f"num_params: {nparams}")
