@@ -268,6 +268,9 @@ def run(cfg: RunConfig) -> dict:
         if int(control[0].item()):
             raise RuntimeError(f"bad loss detected: {loss}")
         total_tokens += tr.tokens_per_step
+        if step == 0:
+            gc.collect()
+            gc.freeze()   # long-lived objects out of the collector's way after the first step
         smooth = 0.9 * smooth + 0.1 * loss
         deb = smooth / (1 - 0.9 ** (step + 1))
         if step < 5 or step % cfg.log_every == 0:
