@@ -200,16 +200,60 @@ __device__ __noinline__ void split_finish(const GemmArgs& a, int mb, int nb, int
     for (int c = hf * (BN / 64); c < (hf + 1) * (BN / 64); ++c) {
       const int col0 = nb * BN + c * 32;
       if (col0 >= a.N) break;
-      const int n = min(32, a.N - col0);
-      for (int i = 0; i < n; ++i) {
-        float v = __ldcg(ws + col0 + i);
-        ws[col0 + i] = 0.f;
-        if (a.R != nullptr) v += a.rcoef * __bfloat162float(a.R[(long long)row * a.ldr + col0 + i]);
-        if (a.fin_relu2) {
-          const float h = __bfloat162float(__float2bfloat16_rn(v)) - a.tau;
-          v = h > 0.f ? h * h : 0.f;
+      float v[32];
+      if (col0 + 32 <= a.N) {
+        // whole chunk: every load is issued before any store (one memory round trip)
+        float4 w4[8];
+        uint4 r4[4];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w4[i] = __ldcg(reinterpret_cast<const float4*>(ws + col0) + i);
+        if (a.R != nullptr) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) r4[i] = *reinterpret_cast<const uint4*>(a.R + (long long)row * a.ldr + col0 + 8 * i);
         }
-        out[col0 + i] = __float2bfloat16_rn(v);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          v[4 * i] = w4[i].x; v[4 * i + 1] = w4[i].y; v[4 * i + 2] = w4[i].z; v[4 * i + 3] = w4[i].w;
+        }
+        if (a.R != nullptr) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&r4[i]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f = __bfloat1622float2(h2[j]);
+              v[8 * i + 2 * j] += a.rcoef * f.x;
+              v[8 * i + 2 * j + 1] += a.rcoef * f.y;
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (a.fin_relu2) {
+            const float h = __bfloat162float(__float2bfloat16_rn(v[i])) - a.tau;
+            v[i] = h > 0.f ? h * h : 0.f;
+          }
+        }
+        uint4 ov[4];
+        uint32_t* ow = reinterpret_cast<uint32_t*>(ov);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) ow[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) reinterpret_cast<uint4*>(out + col0)[i] = ov[i];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) reinterpret_cast<float4*>(ws + col0)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      } else {
+        const int n = a.N - col0;
+        for (int i = 0; i < n; ++i) {
+          float x = __ldcg(ws + col0 + i);
+          if (a.R != nullptr) x += a.rcoef * __bfloat162float(a.R[(long long)row * a.ldr + col0 + i]);
+          if (a.fin_relu2) {
+            const float h = __bfloat162float(__float2bfloat16_rn(x)) - a.tau;
+            x = h > 0.f ? h * h : 0.f;
+          }
+          out[col0 + i] = __float2bfloat16_rn(x);
+          ws[col0 + i] = 0.f;
+        }
       }
     }
   }
@@ -578,6 +622,40 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
             st_release_sys_u32(args.tp.rs_flag[owner] + ((long long)rank * tiles_per_rank + tile_local) * 8 + hf * 4 + q,
                                args.tp.epoch);
         }
+      } else if (EPI == EPI_F32 && args.tma_store) {
+        // ---- fp32 output through TMA: 32 rows x 32 columns staged per warp (128-byte
+        // swizzle); accumulation (beta = 1 or split-K) is a bulk reduce-add in L2, a plain
+        // result a bulk store -- no per-thread read-modify-write or atomics.
+        uint8_t* stg = staging + (warp - 2) * 4096;
+        const int row0 = mb * BM + q * 32;
+        const bool reduce = args.split_k > 1 || args.beta != 0.f;
+#pragma unroll 1
+        for (int c = hf * (BN / 64); c < (hf + 1) * (BN / 64); ++c) {
+          uint32_t r[32];
+          __syncwarp();
+          tmem_ld_32x32b_x32(tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN + c * 32), r);
+          tmem_ld_wait();
+          const int col0 = nb * BN + c * 32;
+          if (col0 >= args.N) continue;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<float4*>(stg + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                make_float4(__uint_as_float(r[4 * j]) * alpha, __uint_as_float(r[4 * j + 1]) * alpha,
+                            __uint_as_float(r[4 * j + 2]) * alpha, __uint_as_float(r[4 * j + 3]) * alpha);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && row0 < args.M) {
+            if (reduce) tma_reduce_add_3d(&tmD, stg, col0, row0, bi);
+            else tma_store_3d(&tmD, stg, col0, row0, bi);
+            bulk_commit_group();
+            bulk_wait_group_read<0>();
+          }
+          __syncwarp();
+        }
+        if (lane == 0) bulk_wait_group<0>();
+        __syncwarp();
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
       } else if (EPI != EPI_F32 && args.tma_store) {
         // ---- bf16 outputs through TMA stores: each warp stages its 32 rows x 64 columns
         // (128-byte swizzle) and one lane stores the slab, so global writes are whole lines
@@ -974,6 +1052,8 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
                         const GemmArgs& a, int grid, cudaStream_t stream) {
   using C = GemmCfg<BN>;
   auto kern = gemm_bf16_kernel<BN, A_MN, B_MN, EPI, MODE>;
+  // every epilogue stages through the same per-warp tiles (TMA stores / reduce-adds, the
+  // TP reduce-scatter)
   constexpr size_t smem = C::SMEM_ALL;
   static bool attr_set = false;  // one per instantiation
   if (!attr_set) {
@@ -1022,7 +1102,9 @@ static void dispatch_tp(int mode, bool b_mn, int epi, const CUtensorMap& ta, con
 static bool tma_store_ok(int64_t epi, int64_t N, const void* d, long long ldd, long long dbs, const void* d2,
                          long long ldd2, long long d2bs) {
   static const bool off = getenv("TFB_GEMM_NO_TMA_STORE") != nullptr;
-  if (off || epi == EPI_F32 || N % 8 != 0) return false;
+  if (off || N % 8 != 0) return false;
+  if (epi == EPI_F32)  // fp32: 16-byte rows, one batch (the tensor map is 2-D)
+    return dbs == 0 && d != nullptr && (reinterpret_cast<uintptr_t>(d) & 15) == 0 && (ldd * 4) % 16 == 0;
   auto ok = [](const void* p, long long ld, long long bs) {
     return p != nullptr && (reinterpret_cast<uintptr_t>(p) & 15) == 0 && (ld * 2) % 16 == 0 && (bs * 2) % 16 == 0;
   };
@@ -1100,7 +1182,10 @@ void gemm_bf16(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_mn, int64_t M
   a.err = err.data_ptr<int>();
   CUtensorMap td = ta, td2 = ta;
   a.tma_store = tma_store_ok(epi, N, D.data_ptr(), a.ldd, d_bs, epi == EPI_RELU2 ? a.D2 : nullptr, a.ldd2, a.d2_bstride);
-  if (a.tma_store) {
+  if (a.tma_store && epi == EPI_F32) {
+    if (nb != 1) a.tma_store = 0;
+    else td = make_tmap_f32(a.D, N, M, a.ldd, 32, 32);
+  } else if (a.tma_store) {
     td = make_tmap_bf16(a.D, N, M, a.ldd, 64, 32, nb, d_bs);
     if (epi == EPI_RELU2) td2 = make_tmap_bf16(a.D2, N, M, a.ldd2, 64, 32, nb, a.d2_bstride);
   }
@@ -1122,6 +1207,12 @@ void gemm_splitk_fin(torch::Tensor A, torch::Tensor B, torch::Tensor ws, torch::
   TORCH_CHECK(B.size(1) == K, "K mismatch");
   TORCH_CHECK(ws.scalar_type() == at::kFloat && ws.is_contiguous() && ws.size(0) >= M && ws.size(1) == N, "ws fp32 [M, N]");
   TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.stride(1) == 1 && out.size(0) >= M && out.size(1) >= N, "out bf16 [M, N]");
+  TORCH_CHECK((out.stride(0) * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0 &&
+                  (ws.stride(0) * 4) % 16 == 0 && (reinterpret_cast<uintptr_t>(ws.data_ptr()) & 15) == 0,
+              "16-byte aligned rows");
+  if (R.has_value())
+    TORCH_CHECK((R->stride(0) * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(R->data_ptr()) & 15) == 0,
+                "residual rows must be 16-byte aligned");
   const int BM = 128, BK = 64, bn = 128;
   c10::cuda::CUDAGuard guard(A.device());
   CUtensorMap ta = make_tmap_bf16(A.data_ptr(), K, M, A.stride(0), 64, BM, 1, 0);
