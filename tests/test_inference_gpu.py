@@ -53,3 +53,26 @@ def test_decode_attention_kernel(cuda_device):
     vf = vc[:, :L].float().view(B, L, H, D).transpose(1, 2)
     ref = torch.softmax(qf @ kf.transpose(-1, -2) * D ** -0.5, -1) @ vf
     assert (out.float().view(B, H, D) - ref.squeeze(2)).abs().max().item() < 2e-2
+
+
+def test_split_decode_attention_kernel(cuda_device):
+    """Cache length split over CTAs per (batch, head), partials combined by the last CTA;
+    repeated calls check that the arrival counters are left zeroed."""
+    from trainium_frontier_b200.ops._ext import C
+    torch.manual_seed(1)
+    B, Tm, H, D, splits = 3, 640, 4, 128, 5
+    q = torch.randn(B, H * D, device=cuda_device).to(torch.bfloat16)
+    kc = torch.randn(B, Tm, H * D, device=cuda_device).to(torch.bfloat16)
+    vc = torch.randn(B, Tm, H * D, device=cuda_device).to(torch.bfloat16)
+    ws = torch.zeros(B * H * splits * (D + 4), device=cuda_device)
+    cnt = torch.zeros(B * H, dtype=torch.int32, device=cuda_device)
+    for L in (1, 77, 513, 640):
+        ln = torch.tensor([L], dtype=torch.int32, device=cuda_device)
+        out = torch.empty(B, H * D, dtype=torch.bfloat16, device=cuda_device)
+        C().decode_attn_split(q, kc, vc, ln, H, D, D ** -0.5, out, ws, cnt, splits)
+        qf = q.float().view(B, H, 1, D)
+        kf = kc[:, :L].float().view(B, L, H, D).transpose(1, 2)
+        vf = vc[:, :L].float().view(B, L, H, D).transpose(1, 2)
+        ref = torch.softmax(qf @ kf.transpose(-1, -2) * D ** -0.5, -1) @ vf
+        assert (out.float().view(B, H, D) - ref.squeeze(2)).abs().max().item() < 2e-2, L
+        assert int(cnt.abs().sum()) == 0

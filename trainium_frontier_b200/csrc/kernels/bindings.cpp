@@ -30,6 +30,8 @@ void rope_norm_fwd(torch::Tensor buf, int64_t head0, int64_t nheads, int64_t D, 
                    c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> pos_t);
 void decode_attn(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache, torch::Tensor len, int64_t H,
                  int64_t D, double scale, torch::Tensor out);
+void decode_attn_split(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache, torch::Tensor len, int64_t H,
+                       int64_t D, double scale, torch::Tensor out, torch::Tensor ws, torch::Tensor cnt, int64_t splits);
 void kv_append(torch::Tensor k, torch::Tensor v, torch::Tensor kcache, torch::Tensor vcache, torch::Tensor pos);
 void step_advance(torch::Tensor counters);
 void argmax_rows(torch::Tensor logits, int64_t V, torch::Tensor idx_out, c10::optional<torch::Tensor> tokens,
@@ -74,6 +76,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("cos"), py::arg("sin"), py::arg("T"), py::arg("pos_offset"), py::arg("rstd"), py::arg("out"),
         py::arg("pos_t") = py::none());
   m.def("decode_attn", &tfb::decode_attn);
+  m.def("decode_attn_split", &tfb::decode_attn_split);
   m.def("kv_append", &tfb::kv_append);
   m.def("step_advance", &tfb::step_advance);
   m.def("argmax_rows", &tfb::argmax_rows);

@@ -82,6 +82,115 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
   }
 }
 
+// decode_attn_split: the same attention with the cache length split over `splits` CTAs per
+// (batch, head) so the KV stream is read by many SMs at once.  Each CTA scores a chunk of
+// keys (one key per warp at a time, lanes over the head dimension, 256-byte rows),
+// keeps an unnormalised partial output plus (max, sum) in a workspace, and the last CTA
+// of its (batch, head) -- an arrival counter -- combines the partials, writes the row and
+// re-zeroes the counter (no memset between graph replays).
+template <int D>
+__global__ void __launch_bounds__(kDecThreads) decode_attn_split_kernel(
+    const __nv_bfloat16* __restrict__ q, long long ldq, const __nv_bfloat16* __restrict__ kc,
+    const __nv_bfloat16* __restrict__ vc, long long cache_ld, long long cache_bstride, const int* __restrict__ len_ptr,
+    int len_max, __nv_bfloat16* __restrict__ out, long long ldo, int H, float scale, int splits,
+    float* __restrict__ ws, int* __restrict__ cnt) {
+  static_assert(D == 128, "lanes cover 4 dims each");
+  // partial record = D outputs + (max, sum), padded to a multiple of 4 floats so every
+  // record starts on a 16-byte boundary (float4 stores / loads)
+  constexpr int kPartStride = D + 4;
+  constexpr int NW = kDecThreads / 32;
+  __shared__ float s_m[NW], s_l[NW];
+  __shared__ __align__(16) float s_o[NW][D];
+  __shared__ int s_last;
+  const int bh = blockIdx.x / splits, sp = blockIdx.x % splits;
+  const int b = bh / H, h = bh % H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int L = *len_ptr;
+  L = L < 1 ? 1 : (L > len_max ? len_max : L);
+  const int chunk = (L + splits - 1) / splits;
+  const int k0 = sp * chunk, k1 = min(L, k0 + chunk);
+  // q slice of this lane (dims 4*lane .. 4*lane+3), pre-scaled
+  const uint2 qu = *reinterpret_cast<const uint2*>(q + (long long)b * ldq + h * D + 4 * lane);
+  const float2 q01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qu.x));
+  const float2 q23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qu.y));
+  const float qs[4] = {q01.x * scale, q01.y * scale, q23.x * scale, q23.y * scale};
+  const __nv_bfloat16* kb = kc + (long long)b * cache_bstride + h * D + 4 * lane;
+  const __nv_bfloat16* vb = vc + (long long)b * cache_bstride + h * D + 4 * lane;
+  float m = -INFINITY, l = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int k = k0 + warp; k < k1; k += NW) {
+    const uint2 ku = *reinterpret_cast<const uint2*>(kb + (long long)k * cache_ld);
+    const uint2 vu = *reinterpret_cast<const uint2*>(vb + (long long)k * cache_ld);
+    const float2 k01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ku.x));
+    const float2 k23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ku.y));
+    float sdot = qs[0] * k01.x + qs[1] * k01.y + qs[2] * k23.x + qs[3] * k23.y;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sdot += __shfl_xor_sync(0xffffffffu, sdot, off);
+    const float m_new = fmaxf(m, sdot);
+    const float corr = __expf(m - m_new);
+    const float p = __expf(sdot - m_new);
+    const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vu.x));
+    const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vu.y));
+    l = l * corr + p;
+    o[0] = o[0] * corr + p * v01.x;
+    o[1] = o[1] * corr + p * v01.y;
+    o[2] = o[2] * corr + p * v23.x;
+    o[3] = o[3] * corr + p * v23.y;
+    m = m_new;
+  }
+  // combine the warps of this CTA
+  if (lane == 0) {
+    s_m[warp] = m;
+    s_l[warp] = l;
+  }
+  *reinterpret_cast<float4*>(&s_o[warp][4 * lane]) = make_float4(o[0], o[1], o[2], o[3]);
+  __syncthreads();
+  float* part = ws + ((long long)bh * splits + sp) * kPartStride;
+  if (warp == 0) {
+    float M = s_m[0];
+#pragma unroll
+    for (int w = 1; w < NW; ++w) M = fmaxf(M, s_m[w]);
+    float Lsum = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float f = s_m[w] == -INFINITY ? 0.f : __expf(s_m[w] - M);
+      Lsum += f * s_l[w];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[j] += f * s_o[w][4 * lane + j];
+    }
+    *reinterpret_cast<float4*>(part + 4 * lane) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    if (lane == 0) {
+      part[D] = M;
+      part[D + 1] = Lsum;
+    }
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) s_last = atomicAdd(cnt + bh, 1) == splits - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  // last split of this (batch, head): combine every split's partial
+  if (warp == 0) {
+    __threadfence();
+    const float* base = ws + (long long)bh * splits * kPartStride;
+    float M = -INFINITY;
+    for (int t = 0; t < splits; ++t) M = fmaxf(M, __ldcg(base + t * kPartStride + D));
+    float Lsum = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int t = 0; t < splits; ++t) {
+      const float mt = __ldcg(base + t * kPartStride + D);
+      const float f = mt == -INFINITY ? 0.f : __expf(mt - M);
+      Lsum += f * __ldcg(base + t * kPartStride + D + 1);
+      const float4 ot = __ldcg(reinterpret_cast<const float4*>(base + t * kPartStride + 4 * lane));
+      acc[0] += f * ot.x; acc[1] += f * ot.y; acc[2] += f * ot.z; acc[3] += f * ot.w;
+    }
+    const float inv = 1.f / Lsum;
+    uint2 u;
+    u.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
+    u.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
+    *reinterpret_cast<uint2*>(out + (long long)b * ldo + h * D + 4 * lane) = u;
+    if (lane == 0) cnt[bh] = 0;
+  }
+}
+
 // cache[b, pos, :] = src[b, :] for k and v (pos read from device memory).
 __global__ void kv_append_kernel(const __nv_bfloat16* __restrict__ ksrc, long long ldk,
                                  const __nv_bfloat16* __restrict__ vsrc, long long ldv, __nv_bfloat16* __restrict__ kc,
@@ -188,6 +297,34 @@ void argmax_rows(torch::Tensor logits, int64_t V, torch::Tensor idx_out, c10::op
   argmax_rows_kernel<<<B, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), logits.stride(0), (int)V, idx_out.data_ptr<int>(), tk,
       ldt, counters.data_ptr<int>(), (int)start, max_new);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ws: fp32 >= B*H*splits*(D+4), 16-byte aligned; cnt: int32 >= B*H, zero before the
+// first call (left zeroed).
+void decode_attn_split(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache, torch::Tensor len, int64_t H,
+                       int64_t D, double scale, torch::Tensor out, torch::Tensor ws, torch::Tensor cnt,
+                       int64_t splits) {
+  TORCH_CHECK(D == 128, "split decode attention supports head_dim 128");
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kBFloat16 && kcache.dim() == 3 && vcache.dim() == 3, "inputs");
+  TORCH_CHECK(kcache.stride(2) == 1 && vcache.stride(2) == 1 && kcache.strides() == vcache.strides(), "cache layout");
+  auto a8 = [](const torch::Tensor& t) { return (reinterpret_cast<uintptr_t>(t.data_ptr()) & 7) == 0; };
+  TORCH_CHECK((q.stride(0) * 2) % 8 == 0 && (kcache.stride(1) * 2) % 8 == 0 && (kcache.stride(0) * 2) % 8 == 0 &&
+                  (out.stride(0) * 2) % 8 == 0 && out.stride(1) == 1 && q.stride(1) == 1,
+              "8-byte aligned rows (4 bf16 per lane)");
+  TORCH_CHECK(a8(q) && a8(kcache) && a8(vcache) && a8(out), "8-byte aligned bases");
+  const int64_t B = q.size(0);
+  TORCH_CHECK(splits >= 1 && splits <= 64, "splits 1..64");
+  TORCH_CHECK(ws.scalar_type() == at::kFloat && ws.numel() >= B * H * splits * (D + 4), "workspace size");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(ws.data_ptr()) & 15) == 0, "workspace must be 16-byte aligned");
+  TORCH_CHECK(cnt.scalar_type() == at::kInt && cnt.numel() >= B * H, "counter size");
+  c10::cuda::CUDAGuard guard(q.device());
+  decode_attn_split_kernel<128><<<(unsigned)(B * H * splits), kDecThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0),
+      reinterpret_cast<const __nv_bfloat16*>(kcache.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(vcache.data_ptr()),
+      kcache.stride(1), kcache.stride(0), len.data_ptr<int>(), (int)kcache.size(1),
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), (int)H, (float)scale, (int)splits,
+      ws.data_ptr<float>(), cnt.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -70,6 +70,9 @@ class Generator:
         self.graph = None
         self.tokens = None
         self.ws: dict = {}   # decode GEMM workspaces (zeroed fp32 sums + counters) per shape
+        self.att_splits = max(1, min(16, self.Tmax // 128))
+        self.att_ws = torch.zeros(self.B * self.H * self.att_splits * (self.D + 4), dtype=torch.float32, device=dev)
+        self.att_cnt = torch.zeros(self.B * self.H, dtype=torch.int32, device=dev)
         blocks = list(model.transformer.h)
         self.wqkv = [torch.cat([w16(b.attn.c_q.weight), w16(b.attn.c_k.weight), w16(b.attn.c_v.weight)], 0).contiguous()
                      for b in blocks]
@@ -102,7 +105,11 @@ class Generator:
         else:
             C().kv_append(qkn[:, Cd:], qkv[:, 2 * Cd:], self.kc[i], self.vc[i], self.counters[0:1])
             y = torch.empty((M, Cd), dtype=torch.bfloat16, device=self.dev)
-            C().decode_attn(qkn[:, :Cd], self.kc[i], self.vc[i], self.counters[1:2], H, D, self.scale, y)
+            if D == 128:   # cache length split over several CTAs per (batch, head)
+                C().decode_attn_split(qkn[:, :Cd], self.kc[i], self.vc[i], self.counters[1:2], H, D, self.scale, y,
+                                      self.att_ws, self.att_cnt, self.att_splits)
+            else:
+                C().decode_attn(qkn[:, :Cd], self.kc[i], self.vc[i], self.counters[1:2], H, D, self.scale, y)
         if prefill:
             x = gemm.linear_fwd(y, self.wo[i], residual=xm)
             h2 = torch.empty_like(x)
