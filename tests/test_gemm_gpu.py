@@ -68,3 +68,24 @@ def test_linear_dx_dw(cuda_device, M, N, K):
     gemm.linear_dw(dy, x, g, accumulate=False, split_k=1)
     _check(g, ref)
     check_errors()
+
+
+@pytest.mark.parametrize("M,N,K", [(32, 3840, 1280), (8, 1280, 5120), (17, 8192, 1280), (32, 200, 136)])
+def test_linear_decode_split_k(cuda_device, M, N, K):
+    """Few-row GEMM in one launch: split-K partial sums finished (plain / + residual / relu^2)
+    by the last split, the workspace left zeroed for the next call."""
+    from trainium_frontier_b200.ops import gemm
+    from trainium_frontier_b200.ops._ext import check_errors
+    torch.manual_seed(3)
+    x = torch.randn(M, K, device=cuda_device, dtype=torch.bfloat16)
+    w = torch.randn(N, K, device=cuda_device, dtype=torch.bfloat16) * K ** -0.5
+    r = torch.randn(M, N, device=cuda_device, dtype=torch.bfloat16)
+    cache = {}
+    ref = _ref(x, w)
+    for _ in range(2):  # the second round checks that the first left ws / counters clean
+        _check(gemm.linear_decode(x, w, cache), ref)
+        _check(gemm.linear_decode(x, w, cache, residual=r), ref + r.float())
+        _check(gemm.linear_decode(x, w, cache, relu2=True), torch.relu(ref.bfloat16().float()) ** 2)
+    check_errors()
+    ws, cnt, _split = next(iter(cache.values()))
+    assert float(ws.abs().sum()) == 0.0 and int(cnt.abs().sum()) == 0

@@ -102,21 +102,6 @@ def linear_dx(dy: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None
     return _gemm(dy2, False, w2, True, M, K, Nn, out, EPI_BF16, alpha_t=alpha_t, R=R)
 
 
-def linear_small_m(x: torch.Tensor, w: torch.Tensor, ws: torch.Tensor | None = None) -> torch.Tensor:
-    """fp32 x @ W^T for a handful of rows (decode): the weight read is the whole cost, so
-    the K axis is split over (nearly) every SM and partial tiles are summed with vector
-    atomics into an fp32 workspace (zeroed by the launch).  Returns the workspace."""
-    x2, w2 = _c2(x), _c2(w)
-    M, K = x2.shape
-    N = w2.shape[0]
-    if ws is None:
-        ws = torch.empty((M, N), dtype=torch.float32, device=x.device)
-    bn = 128
-    tiles = math.ceil(M / 128) * math.ceil(N / bn)
-    split = max(1, min(math.ceil(K / 64) // 2, num_sms(x.device) // max(1, tiles)))
-    return _gemm(x2, False, w2, False, M, N, K, ws, EPI_F32, beta=0.0, split_k=split, bn=bn)
-
-
 def linear_decode(x: torch.Tensor, w: torch.Tensor, cache: dict, residual: torch.Tensor | None = None,
                   relu2: bool = False, tau: float = 0.0) -> torch.Tensor:
     """bf16 x @ W^T (+ residual | relu(. - tau)^2) for a few rows in ONE launch: split-K over
