@@ -37,7 +37,7 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-BASELINE_TOKS = None  # the reference publishes no B200 number for this config
+PUBLISHED_TOKS = None  # the reference publishes no B200 number for this config
 METRIC = "train tok/s (max over ranks) at 1/2/4/8 B200; step ms; held-out bpb at fixed budget"
 CONFIGS = {
     "d20": {"model": "d20 GPT (20L, d1280, 10x128 heads, relu2 MLP 5120, vocab 8192)",

@@ -218,6 +218,7 @@ class RunConfig:
     bucket_layers: int = 4          # transformer blocks per gradient bucket
     use_cuda_graphs: bool = False
     tp: int = 1                     # tensor-parallel degree (DP = world / tp)
+    pp: int = 1                     # pipeline stages (DP = world / pp); tp and pp are exclusive
     checkpoint_activations: bool = False
 
     # ------------------------------------------------------------------------------
@@ -314,8 +315,10 @@ def validate(cfg: RunConfig) -> None:
         raise ValueError("--coalesced-swiglu and --gated-mlp are mutually exclusive")
     if cfg.adam_every_n < 1:
         raise ValueError("--adam-every-n must be >= 1")
-    if cfg.tp < 1:
-        raise ValueError("--tp must be >= 1")
+    if cfg.tp < 1 or cfg.pp < 1:
+        raise ValueError("--tp and --pp must be >= 1")
+    if cfg.tp > 1 and cfg.pp > 1:
+        raise ValueError("--tp and --pp cannot be combined")
     if cfg.parallel_block_coalesce != "none":
         raise ValueError("--parallel-block-coalesce: only 'none' is built (the fused QKV GEMM already reads "
                          "the three attention inputs as one weight); 'vfc' / 'all' change the state_dict layout")

@@ -368,6 +368,13 @@ class TrainEngine:
         local_clip = self.cfg.clip_order == "local" and self.cfg.grad_clip > 0
         if self.dist_muon is not None:
             self.dist_muon.begin_step()
+        ppc = getattr(self.model, "ppc", None)
+        if ppc is not None:
+            # pipeline: stages finish their buckets at different times, so the collectives
+            # are issued after backward, in bucket order, on every rank
+            from .parallel.pipeline import pipeline_forward_backward
+            self._sync_now = False
+            return pipeline_forward_backward(self.model, ppc, batches, loss_scale)
         for i, (x, y) in enumerate(batches):
             self._sync_now = (i == len(batches) - 1) and self.grad_sync in ("bucket", "dist_muon", "fused") \
                 and not local_clip

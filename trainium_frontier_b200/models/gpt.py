@@ -585,6 +585,14 @@ class GPT(nn.Module):
             b._tpc = tpc
             b._layer_idx = i
 
+    def enable_pp(self, ppc) -> None:
+        """Run forward/backward as pipeline stage ``ppc.stage`` (plain-family blocks; VE,
+        n-gram, Engram, pooling and masks are not staged)."""
+        if len(self.value_embeds) or len(self.ngram_embeds) or self.engram is not None or self.rc.doc_mask \
+                or any(self.layer_is_short) or self.out_pool_lambdas is not None or self.out_bigram is not None:
+            raise ValueError("pipeline parallelism supports models without VE / n-gram / Engram / masks / pooling")
+        self.ppc = ppc
+
     def disable_tp(self) -> None:
         """Back to whole-model blocks (every rank holds every weight whole), e.g. for an
         evaluation whose batches do not have the tensor-parallel row shape."""

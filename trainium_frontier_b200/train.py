@@ -71,9 +71,15 @@ class Trainer:
             rows = cfg.device_batch_size * cfg.pack_factor * cfg.seq_len
             self.tpc = TPContext(cfg.tp, self.device, rows, self.gconf.n_embd, 2 * self.gconf.n_layer)
             model.enable_tp(self.tpc)
+        self.ppc = None
+        if cfg.pp > 1:
+            from .parallel.pipeline import PipelineContext
+            self.ppc = PipelineContext(cfg.pp, self.gconf.n_layer)
+            model.enable_pp(self.ppc)
         self.opt = setup_optimizer(model, cfg, compute_dtype=self.dtype)
         self.rows_per_micro = cfg.device_batch_size * cfg.pack_factor
-        tokens_per_micro = self.rows_per_micro * cfg.seq_len * world_size
+        data_ranks = world_size // cfg.pp          # pipeline stages share their micro-batches
+        tokens_per_micro = self.rows_per_micro * cfg.seq_len * data_ranks
         if cfg.total_batch_size % tokens_per_micro:
             raise ValueError(f"total_batch_size={cfg.total_batch_size} must be a multiple of "
                              f"micro tokens x world = {tokens_per_micro}")
@@ -81,7 +87,7 @@ class Trainer:
         self.tokens_per_step = cfg.total_batch_size
         self.engine = TrainEngine(model, self.opt, cfg, self.device, self.grad_accum, cfg.grad_sync)
         self.loader = PackedRowLoader(self.rows_per_micro, cfg.seq_len, self.device, "train",
-                                      rank=rank) if build_loader else None
+                                      rank=rank // cfg.pp) if build_loader else None
         self.step_idx = 0
         self.loss_scale = cfg.loss_scale
         self.loss_scale_clean = 0
