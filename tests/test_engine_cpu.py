@@ -60,3 +60,25 @@ def test_train_main_smoke(tmp_path, monkeypatch):
                 "--num-steps", "3", "--progress-mode", "steps", "--out-dir", str(out),
                 "--eval-tokens", "512", "--rope-base", "10000"])
     assert (out / "final.pt").exists()
+
+
+def test_adamw_every_n_accumulates_between_updates():
+    """With AdamW updating every 2nd step, embedding / lm_head stay frozen on the odd steps
+    while their gradients accumulate; Muon matrices move every step."""
+    import torch
+    from trainium_frontier_b200.config import preset
+    from trainium_frontier_b200.train import Trainer
+    cfg = preset("tiny", depth=2, progress_mode="steps", num_steps=8, device_batch_size=2,
+                 total_batch_size=2 * 256 * 2, grad_sync="none", adam_every_n=2, grad_clip=0.0)
+    tr = Trainer(cfg, torch.device("cpu"))
+    wte = tr.model.transformer.wte.weight
+    cq = tr.model.transformer.h[0].attn.c_q.weight
+    w0, q0 = wte.detach().clone(), cq.detach().clone()
+    tr.train_step()
+    g1 = wte.grad.detach().clone()
+    assert torch.equal(wte.detach(), w0), "AdamW params must not move on a non-update step"
+    assert not torch.equal(cq.detach(), q0), "Muon params move every step"
+    tr.train_step()
+    assert not torch.equal(wte.detach(), w0), "AdamW applies on the second step"
+    # the applied gradient was the sum of both steps' gradients
+    assert float((wte.grad - g1).abs().sum()) > 0 and float(g1.abs().sum()) > 0

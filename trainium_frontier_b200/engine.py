@@ -347,6 +347,12 @@ class TrainEngine:
         elif self.grad_sync in ("dist_muon", "fused"):
             self.dist_muon.finish_grad_sync()
 
+    def _adamw_params(self):
+        if not hasattr(self, "_adamw_cache"):
+            self._adamw_cache = [p for g in self.opt.param_groups if g["kind"] in ("adamw", "rmsprop")
+                                 for p in g["params"]]
+        return self._adamw_cache
+
     # ------------------------------------------------------------------ step
     def clip_(self) -> torch.Tensor | None:
         if self.cfg.grad_clip <= 0:
@@ -357,9 +363,20 @@ class TrainEngine:
         g.mul_(coef)
         return total
 
-    def forward_backward(self, batches, loss_scale: float = 1.0) -> torch.Tensor:
-        """Runs the grad-accumulation micro-steps; returns the mean loss (device)."""
-        self.layout.zero_grad()
+    def forward_backward(self, batches, loss_scale: float = 1.0, zero_adamw: bool = True) -> torch.Tensor:
+        """Runs the grad-accumulation micro-steps; returns the mean loss (device).
+
+        ``zero_adamw=False`` keeps the AdamW / RMSProp gradients of the previous steps
+        (AdamW updating every N steps, train.py:481-499): they keep accumulating until the
+        step that applies them.  Averaging across ranks is linear, so re-averaging the
+        accumulated sum every step equals the reference's deferred all-reduce."""
+        if zero_adamw:
+            self.layout.zero_grad()
+        else:
+            keep = [(p, p.grad.clone()) for p in self._adamw_params() if p.grad is not None]
+            self.layout.zero_grad()
+            for p, g in keep:
+                p.grad.copy_(g)
         for b in self.layout.buckets:
             b.ready = False
             b.work = None

@@ -89,6 +89,7 @@ class Trainer:
         self.loader = PackedRowLoader(self.rows_per_micro, cfg.seq_len, self.device, "train",
                                       rank=rank // cfg.pp) if build_loader else None
         self.step_idx = 0
+        self._adamw_applied_last = True   # AdamW gradients are zeroed only after they were applied
         self.loss_scale = cfg.loss_scale
         self.loss_scale_clean = 0
         self.row_weight = None
@@ -182,7 +183,8 @@ class Trainer:
                 return _orig(x, y, row_weight=self.byte_w[y.reshape(-1).long()].contiguous())
             model.forward = fwd
         try:
-            loss = self.engine.forward_backward(batches, loss_scale=self.loss_scale)
+            loss = self.engine.forward_backward(batches, loss_scale=self.loss_scale,
+                                                zero_adamw=self._adamw_applied_last)
         finally:
             if self.byte_w is not None:
                 model.forward = orig
@@ -202,6 +204,7 @@ class Trainer:
         apply_schedules(cfg, self.opt, self.step_idx, prog, lr_scale)
         if not skip:
             self.engine.optimizer_step(update_adamw)
+            self._adamw_applied_last = update_adamw
         self.step_idx += 1
         if read_loss:
             return float(loss.item())
