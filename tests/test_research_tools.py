@@ -42,3 +42,15 @@ def test_autoresearch_short_run(tmp_path, capsys):
           "--out-dir", str(tmp_path), "--device-type", "cpu"])
     out = capsys.readouterr().out
     assert "val_bpb:" in out and (tmp_path / "final.pt").exists()
+
+
+def test_op_census_cpu(capsys):
+    from trainium_frontier_b200.utils.op_census import main, op_class
+    assert op_class("mm") == "matmul" and op_class("view") == "view" and op_class("mul") == "elementwise"
+    res = main(["--preset", "tiny", "--depth", "2", "--device", "cpu", "--warmup", "0"])
+    assert set(res) == {"fwd_bwd", "sync_clip", "optimizer"}
+    # 2 blocks x (q, k, v, proj, fc, proj) forward GEMMs plus the lm_head, and their backward
+    assert res["fwd_bwd"]["aten_matmul"] >= 13
+    # Newton-Schulz runs on the tensor path
+    assert res["optimizer"]["aten_matmul"] > 0
+    assert "launch-bound" in capsys.readouterr().out

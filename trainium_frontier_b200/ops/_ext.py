@@ -13,6 +13,7 @@ import torch
 _C = None
 _ERR: dict[int, torch.Tensor] = {}
 _LAUNCHES = [0]
+_BY_NAME: dict[str, int] = {}
 
 
 class _Counted:
@@ -28,6 +29,7 @@ class _Counted:
 
         def wrapped(*a, **k):
             _LAUNCHES[0] += 1
+            _BY_NAME[name] = _BY_NAME.get(name, 0) + 1
             return fn(*a, **k)
         return wrapped
 
@@ -47,6 +49,11 @@ def C():
 def launch_count() -> int:
     """Number of sm_100a kernel launches issued through ``C()`` so far."""
     return _LAUNCHES[0]
+
+
+def launch_counts_by_name() -> dict[str, int]:
+    """Kernel-launching calls through ``C()`` so far, per entry point name (a copy)."""
+    return dict(_BY_NAME)
 
 
 def available() -> bool:
