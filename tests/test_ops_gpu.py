@@ -168,6 +168,66 @@ def test_attention_qkv(cuda_device):
     assert rel(qkv.grad.cpu(), qr.grad) < 5e-2
 
 
+def _rope_tables(T, D, device):
+    t = torch.arange(T, dtype=torch.float32)
+    inv = 1.0 / (10000 ** (torch.arange(0, D, 2, dtype=torch.float32) / D))
+    tab = torch.outer(t, inv)
+    return tab.cos().to(BF)[None, :, None, :].to(device), tab.sin().to(BF)[None, :, None, :].to(device)
+
+
+def test_gemm_rope_epilogue(cuda_device):
+    """QKV projection GEMM with RoPE + per-head RMSNorm in the epilogue vs fp32 torch."""
+    from trainium_frontier_b200.ops import gemm
+    from trainium_frontier_b200.ops import reference as ref
+    torch.manual_seed(11)
+    B, T, H, D, K = 2, 256, 3, 128, 320
+    Cd = H * D
+    cos, sin = _rope_tables(T, D, cuda_device)
+    x = (torch.randn(B * T, K, device=cuda_device) * 0.5).to(BF)
+    w = (torch.randn(3 * Cd, K, device=cuda_device) * K ** -0.5).to(BF)
+    rstd = torch.empty(B * T * 2 * H, dtype=torch.float32, device=cuda_device)
+    out = gemm.linear_rope_fwd(x, w, cos.reshape(T, D // 2).contiguous(), sin.reshape(T, D // 2).contiguous(),
+                               T, 2 * Cd, rstd)
+    torch.cuda.synchronize()
+    raw = (x.float() @ w.float().t()).to(BF).float()           # what the epilogue rounds to first
+    qk = raw[:, :2 * Cd].view(B, T, 2 * H, D)
+    ref_qk = ref.rope_norm(qk, cos.float(), sin.float()).reshape(B * T, 2 * Cd)
+    assert rel(out[:, :2 * Cd], ref_qk) < 1e-2
+    assert rel(out[:, 2 * Cd:], raw[:, 2 * Cd:]) < 1e-2       # v columns untouched
+    rot = ref.apply_rotary_emb(qk, cos.float(), sin.float())
+    ref_r = torch.rsqrt(rot.pow(2).mean(-1) + torch.finfo(torch.float32).eps).reshape(-1)
+    assert rel(rstd, ref_r) < 1e-3
+
+
+def test_qkv_rope_attention_matches_unfused(cuda_device, monkeypatch):
+    """The projection-fused RoPE + QK-norm attention path gives the same output and the
+    same input / weight gradients as projection GEMM -> RoPE kernel -> attention."""
+    from trainium_frontier_b200 import ops
+    torch.manual_seed(12)
+    B, T, H, D = 2, 256, 4, 128
+    C = H * D
+    cos, sin = _rope_tables(T, D, cuda_device)
+    x = (torch.randn(B, T, C, device=cuda_device)).to(BF)
+    ws = [(torch.randn(C, C, device=cuda_device) * C ** -0.5) for _ in range(3)]
+    g = torch.randn(B, T, C, device=cuda_device).to(BF)
+
+    def run(flag):
+        monkeypatch.setenv("TFB_QKV_ROPE", flag)
+        xa = x.clone().requires_grad_(True)
+        wa = [w.clone().requires_grad_(True) for w in ws]
+        y = ops.qkv_attention(xa, wa, cos, sin, H, D, None)
+        y.backward(g)
+        torch.cuda.synchronize()
+        return y.detach(), xa.grad, [w.grad for w in wa]
+
+    y1, dx1, dw1 = run("1")
+    y0, dx0, dw0 = run("0")
+    assert rel(y1, y0) < 2e-2
+    assert rel(dx1, dx0) < 3e-2
+    for a, b in zip(dw1, dw0):
+        assert rel(a, b) < 3e-2
+
+
 def test_adamw_multi(cuda_device):
     from trainium_frontier_b200.ops.optim_kernels import adamw_multi
     torch.manual_seed(7)

@@ -12,6 +12,8 @@ void gemm_tp(int64_t mode, torch::Tensor A, torch::Tensor B, bool b_mn, int64_t 
              std::vector<int64_t> ag_src, std::vector<int64_t> ag_ready, c10::optional<torch::Tensor> claim,
              c10::optional<torch::Tensor> done, std::vector<int64_t> rs_recv, std::vector<int64_t> rs_flag,
              torch::Tensor sched, int64_t bn, torch::Tensor err);
+void gemm_rope(torch::Tensor A, torch::Tensor B, torch::Tensor D, torch::Tensor cos, torch::Tensor sin, int64_t T,
+               int64_t rope_cols, c10::optional<torch::Tensor> rstd, torch::Tensor err);
 void gemm_splitk_fin(torch::Tensor A, torch::Tensor B, torch::Tensor ws, torch::Tensor cnt, torch::Tensor out,
                      c10::optional<torch::Tensor> R, bool relu2, double tau, int64_t split, torch::Tensor err);
 void rmsnorm_fwd(torch::Tensor x, torch::Tensor y, c10::optional<torch::Tensor> rstd);
@@ -66,6 +68,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("bn"), py::arg("err"), py::arg("alpha_t") = py::none(), py::arg("rcoef") = 1.0);
   m.def("gemm_tp", &tfb::gemm_tp);
   m.def("gemm_splitk_fin", &tfb::gemm_splitk_fin);
+  m.def("gemm_rope", &tfb::gemm_rope, "tcgen05 bf16 GEMM with RoPE + per-head RMSNorm on the leading columns");
   m.def("rmsnorm_fwd", &tfb::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &tfb::rmsnorm_bwd);
   m.def("mix_norm_fwd", &tfb::mix_norm_fwd);

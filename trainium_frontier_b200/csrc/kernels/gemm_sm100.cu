@@ -19,6 +19,8 @@
 //
 // Epilogues (the fused ops the model needs):
 //   EPI_BF16      D = bf16(alpha * acc (+ R))               linear, linear + residual
+//   EPI_ROPE      D = bf16(acc), then RoPE + per-head RMSNorm of the leading columns
+//                 (fused QKV projection: q / k heads normalised, v stored as is)
 //   EPI_RELU2     D2 = bf16(acc) (pre-activation h), D = bf16(relu(h - tau)^2)
 //   EPI_RELU2_BWD D = bf16(bf16(alpha * acc) * 2 relu(R - tau))   (R = h)
 //   EPI_F32       D(f32) = alpha * acc (+ D if beta)        weight gradients (fp32, split-K via
@@ -53,7 +55,7 @@
 
 namespace tfb {
 
-enum GemmEpi : int { EPI_BF16 = 0, EPI_RELU2 = 1, EPI_RELU2_BWD = 2, EPI_F32 = 3 };
+enum GemmEpi : int { EPI_BF16 = 0, EPI_RELU2 = 1, EPI_RELU2_BWD = 2, EPI_F32 = 3, EPI_ROPE = 4 };
 enum GemmMode : int { MODE_PLAIN = 0, MODE_AG = 1, MODE_RS = 2 };
 
 constexpr int kTpMaxRanks = 8;
@@ -94,6 +96,12 @@ struct GemmArgs {
   long long ld_fin;
   int* fin_cnt;
   int fin_relu2;
+  // EPI_ROPE: RoPE + per-head RMSNorm of the leading rope_cols columns (BN = 256, head_dim
+  // 128: one epilogue warp's column half is one head, one thread one token of it)
+  const __nv_bfloat16* rope_cos;  // [T][64] bf16, row = position
+  const __nv_bfloat16* rope_sin;
+  int rope_T, rope_cols, rope_heads;
+  float* rope_rstd;  // [M][rope_heads] fp32, optional
   TpArgs tp;
 };
 
@@ -684,8 +692,78 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
           }
           __syncwarp();
         };
+        bool roped = false;
+        if constexpr (EPI == EPI_ROPE && MODE == MODE_PLAIN && BN == 256) {
+          const int hcol = nb * BN + hf * 128;  // first column of this warp's head
+          if (hcol < args.rope_cols) {
+            // ---- RoPE + RMSNorm of one 128-wide head per thread-row.  x = bf16(acc) (the
+            // value a separate pass would read back), y1 = x1 c + x2 s, y2 = x2 c - x1 s over
+            // the two 64-column halves, out = y / rms(y).  Pass 1 sums y^2; passes 2 and 3
+            // recompute y1 and y2 from TMEM (cheap re-reads instead of 128 live registers)
+            // and store them as two staged 64-column slabs.
+            roped = true;
+            const int pos = (row_ok ? row : 0) % args.rope_T;
+            const __nv_bfloat16* crow = args.rope_cos + (long long)pos * 64;
+            const __nv_bfloat16* srow = args.rope_sin + (long long)pos * 64;
+            const uint32_t tb = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN + hf * 128);
+            // f(k, y1, y2) for the rotated pair at half-column 32p + k, k < 32
+            auto rot = [&](int p, auto&& f) {
+              uint32_t ra[32], rb[32];
+              __syncwarp();
+              tmem_ld_32x32b_x32(tb + p * 32, ra);
+              tmem_ld_32x32b_x32(tb + 64 + p * 32, rb);
+              tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const uint4 cu = reinterpret_cast<const uint4*>(crow + p * 32)[i];
+                const uint4 su = reinterpret_cast<const uint4*>(srow + p * 32)[i];
+                const __nv_bfloat162* c2 = reinterpret_cast<const __nv_bfloat162*>(&cu);
+                const __nv_bfloat162* s2v = reinterpret_cast<const __nv_bfloat162*>(&su);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const float2 cf = __bfloat1622float2(c2[j]), sf = __bfloat1622float2(s2v[j]);
+#pragma unroll
+                  for (int e = 0; e < 2; ++e) {
+                    const int k = 8 * i + 2 * j + e;
+                    const float c = e ? cf.y : cf.x, sn = e ? sf.y : sf.x;
+                    const float x1 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(ra[k]) * alpha));
+                    const float x2 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(rb[k]) * alpha));
+                    f(k, x1 * c + x2 * sn, x2 * c - x1 * sn);
+                  }
+                }
+              }
+            };
+            float ss = 0.f;
 #pragma unroll 1
-        for (int s2 = hf * (BN / 128); s2 < (hf + 1) * (BN / 128); ++s2) {
+            for (int p = 0; p < 2; ++p)
+              rot(p, [&](int, float y1, float y2) { ss += y1 * y1 + y2 * y2; });
+            const float rn = rsqrtf(ss * (1.f / 128.f) + 1.1920928955078125e-07f);
+            if (row_ok && args.rope_rstd != nullptr)
+              args.rope_rstd[(long long)row * args.rope_heads + hcol / 128] = rn;
+#pragma unroll 1
+            for (int which = 0; which < 2; ++which) {
+#pragma unroll 1
+              for (int p = 0; p < 2; ++p) {  // 32 columns at a time into the swizzled slab
+                float v[32];
+                rot(p, [&](int k, float y1, float y2) { v[k] = (which ? y2 : y1) * rn; });
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  uint4 u;
+                  u.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+                  u.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+                  u.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+                  u.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+                  *reinterpret_cast<uint4*>(stg + lane * 128 + (((4 * p + j) ^ (lane & 7)) << 4)) = u;
+                }
+              }
+              fence_proxy_async_smem();
+              __syncwarp();
+              store(&tmD, hcol + which * 64);
+            }
+          }
+        }
+#pragma unroll 1
+        for (int s2 = hf * (BN / 128); s2 < (hf + 1) * (BN / 128) && !roped; ++s2) {
           uint32_t r0[32], r1[32];
           __syncwarp();
           tmem_ld_32x32b_x32(tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN + s2 * 64), r0);
@@ -1079,6 +1157,9 @@ static void dispatch(bool a_mn, bool b_mn, int epi, const CUtensorMap& ta, const
   TFB_CASE(true, true, EPI_BF16)
   TFB_CASE(true, false, EPI_F32)
   TFB_CASE(true, false, EPI_BF16)
+  if constexpr (BN == 256) {
+    TFB_CASE(false, false, EPI_ROPE)
+  }
 #undef TFB_CASE
   TORCH_CHECK(false, "unsupported gemm variant a_mn=", a_mn, " b_mn=", b_mn, " epi=", epi);
 }
@@ -1115,10 +1196,17 @@ static bool tma_store_ok(int64_t epi, int64_t N, const void* d, long long ldd, l
 
 // A: if !a_mn a [M, K] view (row stride lda), else a [K, M] view.  B likewise with N.
 // Operands are 2-D, or 3-D with a leading batch dimension (all of A, B, D batched alike).
-void gemm_bf16(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_mn, int64_t M, int64_t N, int64_t K,
-               torch::Tensor D, int64_t epi, double alpha, double beta, c10::optional<torch::Tensor> R,
-               c10::optional<torch::Tensor> D2, double tau, int64_t split_k, int64_t bn, torch::Tensor err,
-               c10::optional<torch::Tensor> alpha_t, double rcoef) {
+struct RopeEpi {
+  const __nv_bfloat16* cos = nullptr;
+  const __nv_bfloat16* sin = nullptr;
+  int T = 0, cols = 0, heads = 0;
+  float* rstd = nullptr;
+};
+
+static void gemm_bf16_impl(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_mn, int64_t M, int64_t N, int64_t K,
+                           torch::Tensor D, int64_t epi, double alpha, double beta, c10::optional<torch::Tensor> R,
+                           c10::optional<torch::Tensor> D2, double tau, int64_t split_k, int64_t bn, torch::Tensor err,
+                           c10::optional<torch::Tensor> alpha_t, double rcoef, const RopeEpi& rope) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && D.is_cuda(), "gemm operands must be CUDA tensors");
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm inputs must be bf16");
   const int64_t nb = A.dim() == 3 ? A.size(0) : 1;
@@ -1189,10 +1277,55 @@ void gemm_bf16(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_mn, int64_t M
     td = make_tmap_bf16(a.D, N, M, a.ldd, 64, 32, nb, d_bs);
     if (epi == EPI_RELU2) td2 = make_tmap_bf16(a.D2, N, M, a.ldd2, 64, 32, nb, a.d2_bstride);
   }
+  a.rope_cos = rope.cos; a.rope_sin = rope.sin; a.rope_T = rope.T; a.rope_cols = rope.cols;
+  a.rope_heads = rope.heads; a.rope_rstd = rope.rstd;
+  if (epi == EPI_ROPE)
+    TORCH_CHECK(rope.cos != nullptr && a.tma_store && bn == 256 && !a_mn && !b_mn && nb == 1 && a.R == nullptr,
+                "RoPE epilogue: 2-D K-major operands, bf16 TMA-store output, 256-wide tiles, no residual");
   const int grid = std::min(a.num_tiles, num_sms(A.get_device()));
   cudaStream_t s = at::cuda::getCurrentCUDAStream();
   if (bn == 256) dispatch<256>(a_mn, b_mn, (int)epi, ta, tb, td, td2, a, grid, s);
   else dispatch<128>(a_mn, b_mn, (int)epi, ta, tb, td, td2, a, grid, s);
+}
+
+void gemm_bf16(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_mn, int64_t M, int64_t N, int64_t K,
+               torch::Tensor D, int64_t epi, double alpha, double beta, c10::optional<torch::Tensor> R,
+               c10::optional<torch::Tensor> D2, double tau, int64_t split_k, int64_t bn, torch::Tensor err,
+               c10::optional<torch::Tensor> alpha_t, double rcoef) {
+  TORCH_CHECK(epi != EPI_ROPE, "the RoPE epilogue is reached through gemm_rope");
+  gemm_bf16_impl(A, a_mn, B, b_mn, M, N, K, D, epi, alpha, beta, R, D2, tau, split_k, bn, err, alpha_t, rcoef,
+                 RopeEpi{});
+}
+
+// D[M, N] = A[M, K] B[N, K]^T (bf16) with RoPE + per-head RMSNorm applied to the leading
+// rope_cols columns (heads of 128; position = row % T; cos / sin [>= T][64] bf16) and the
+// per-(row, head) reciprocal RMS written to rstd [M][rope_cols / 128] -- the q / k part of
+// a fused QKV projection, the v columns stored as they are.
+void gemm_rope(torch::Tensor A, torch::Tensor B, torch::Tensor D, torch::Tensor cos, torch::Tensor sin, int64_t T,
+               int64_t rope_cols, c10::optional<torch::Tensor> rstd, torch::Tensor err) {
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && D.dim() == 2, "2-D operands");
+  const int64_t M = A.size(0), K = A.size(1), N = B.size(0);
+  TORCH_CHECK(B.size(1) == K && D.size(0) >= M && D.size(1) >= N, "shapes");
+  TORCH_CHECK(rope_cols > 0 && rope_cols % 128 == 0 && rope_cols <= N, "rope_cols must be a multiple of 128 <= N");
+  TORCH_CHECK(T > 0 && M % T == 0, "rows must be whole sequences of length T");
+  for (const torch::Tensor* t : {&cos, &sin}) {
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->dim() == 2 && t->size(1) == 64 &&
+                    t->stride(1) == 1 && t->stride(0) == 64 && t->size(0) >= T,
+                "cos / sin must be contiguous bf16 [>= T, 64]");
+    TORCH_CHECK((reinterpret_cast<uintptr_t>(t->data_ptr()) & 15) == 0, "cos / sin must be 16-byte aligned");
+  }
+  RopeEpi r;
+  r.cos = reinterpret_cast<const __nv_bfloat16*>(cos.data_ptr());
+  r.sin = reinterpret_cast<const __nv_bfloat16*>(sin.data_ptr());
+  r.T = (int)T; r.cols = (int)rope_cols; r.heads = (int)(rope_cols / 128);
+  if (rstd.has_value()) {
+    TORCH_CHECK(rstd->is_cuda() && rstd->scalar_type() == at::kFloat && rstd->is_contiguous() &&
+                    rstd->numel() >= M * r.heads,
+                "rstd fp32 [M * heads]");
+    r.rstd = rstd->data_ptr<float>();
+  }
+  gemm_bf16_impl(A, false, B, false, M, N, K, D, EPI_ROPE, 1.0, 0.0, c10::nullopt, c10::nullopt, 0.0, 1, 256, err,
+                 c10::nullopt, 1.0, r);
 }
 
 // Few-row GEMM (decode): out[M, N] bf16 = x[M, K] W[N, K]^T (+ R | relu^2), K split over the

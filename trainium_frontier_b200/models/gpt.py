@@ -152,9 +152,8 @@ class CausalSelfAttention(nn.Module):
     def forward(self, x_q, x_k, x_v, ve, cos, sin, attn_mask, ve_bi=None, ve_tri=None):
         b, t, c = x_q.shape
         if self.plain and attn_mask is None and x_q is x_k and x_k is x_v:
-            qkv = ops.linear_multi(x_q, [self.c_q.weight, self.c_k.weight, self.c_v.weight])
-            y = ops.attention_qkv(qkv, cos, sin, self.n_head, self.head_dim, self.attn_scale)
-            return y  # c_proj (+ residual) is applied by the block
+            return ops.qkv_attention(x_q, [self.c_q.weight, self.c_k.weight, self.c_v.weight], cos, sin,
+                                     self.n_head, self.head_dim, self.attn_scale)  # c_proj: by the block
         q = ops.linear(x_q, self.c_q.weight).view(b, t, self.n_head, self.head_dim)
         k = ops.linear(x_k, self.c_k.weight).view(b, t, self.n_kv_heads, self.head_dim)
         v = ops.linear(x_v, self.c_v.weight).view(b, t, self.n_kv_heads, self.head_dim)

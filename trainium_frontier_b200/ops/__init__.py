@@ -8,6 +8,8 @@ Every op has two implementations selected by the device of its inputs:
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from . import reference as ref
@@ -104,6 +106,23 @@ def attention_qkv(qkv: torch.Tensor, cos, sin, n_head: int, head_dim: int, scale
     k = ref.rope_norm(k.view(B, T, n_head, head_dim), cos, sin)
     y = ref.attention(q, k, v.view(B, T, n_head, head_dim), True, scale)
     return y.reshape(B, T, Cd)
+
+
+def qkv_attention(x: torch.Tensor, ws: list[torch.Tensor], cos, sin, n_head: int, head_dim: int,
+                  scale: float | None):
+    """Plain-block attention from the block input x [B, T, C] and the q / k / v weights:
+    projection, RoPE + QK-norm on q and k, causal attention.  Returns [B, T, C].  On CUDA
+    with heads of 128 and ``TFB_QKV_ROPE=1`` the RoPE + QK-norm runs in the projection
+    GEMM's epilogue; otherwise it is a separate kernel after the projection."""
+    B, T, _ = x.shape
+    if _cuda(x) and x.dtype == torch.bfloat16 and os.environ.get("TFB_QKV_ROPE", "0") == "1":
+        from .fused import QKVRopeAttnFn, qkv_rope_supported
+        if qkv_rope_supported(T, n_head, head_dim):
+            c2 = cos.reshape(-1, cos.shape[-1])[:T].contiguous()
+            s2 = sin.reshape(-1, sin.shape[-1])[:T].contiguous()
+            sc = scale if scale is not None else head_dim ** -0.5
+            return QKVRopeAttnFn.apply(x, c2, s2, B, T, n_head, head_dim, sc, *ws)
+    return attention_qkv(linear_multi(x, ws), cos, sin, n_head, head_dim, scale)
 
 
 def lm_head_softcap_ce(x, w_lm, targets, softcap: float, vocab: int, reduction: str = "mean",

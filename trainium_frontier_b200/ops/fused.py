@@ -224,24 +224,8 @@ class LinearMultiFn(Function):
     @staticmethod
     def backward(ctx, dy):
         (x2,) = ctx.saved_tensors
-        ws = list(ctx.ws)
-        fg = fused_group(ws)
-        dy2 = gemm._c2(dy)
-        if fg is not None:
-            wb, gview = fg
-            dx = gemm.linear_dx(dy2, wb).view(ctx.shape) if ctx.needs_input_grad[0] else None
-            for w in ws:
-                grad_buf(w)
-            gemm.linear_dw(dy2, x2, gview)
-        else:
-            wb = torch.cat([w16(w) for w in ws], 0)
-            dx = gemm.linear_dx(dy2, wb).view(ctx.shape) if ctx.needs_input_grad[0] else None
-            g = torch.zeros(wb.shape, dtype=torch.float32, device=dy.device)
-            gemm.linear_dw(dy2, x2, g, accumulate=False)
-            for w, part in zip(ws, g.split([w.shape[0] for w in ws], 0)):
-                if w.requires_grad:
-                    grad_buf(w).add_(part)
-        return (dx,) + (None,) * len(ws)
+        dx = _multi_backward(gemm._c2(dy), x2, list(ctx.ws), ctx.shape, ctx.needs_input_grad[0])
+        return (dx,) + (None,) * len(ctx.ws)
 
 
 class MLPRelu2Fn(Function):
@@ -327,6 +311,71 @@ class AttnQKVFn(Function):
                   True, dq=dqkv[:, :Cd], dk=dqkv[:, Cd:2 * Cd], dv=dqkv[:, 2 * Cd:])
         C().rope_norm_bwd(dqkv, qkn, 0, 2 * H, D, cos, sin, T, rstd)
         return dqkv.view(B, T, 3 * Cd), None, None, None, None, None, None, None
+
+
+def _multi_backward(dy2, x2, ws, shape, need_dx):
+    """dx = dy [W_1; W_2; ...] and each W_i's gradient accumulated into W_i.grad."""
+    fg = fused_group(ws)
+    if fg is not None:
+        wb, gview = fg
+        dx = gemm.linear_dx(dy2, wb).view(shape) if need_dx else None
+        for w in ws:
+            grad_buf(w)
+        gemm.linear_dw(dy2, x2, gview)
+        return dx
+    wb = torch.cat([w16(w) for w in ws], 0)
+    dx = gemm.linear_dx(dy2, wb).view(shape) if need_dx else None
+    g = torch.zeros(wb.shape, dtype=torch.float32, device=dy2.device)
+    gemm.linear_dw(dy2, x2, g, accumulate=False)
+    for w, part in zip(ws, g.split([w.shape[0] for w in ws], 0)):
+        if w.requires_grad:
+            grad_buf(w).add_(part)
+    return dx
+
+
+def qkv_rope_supported(T: int, H: int, D: int) -> bool:
+    """Shapes the projection-fused RoPE + QK-norm epilogue takes (heads of 128, whole
+    128-row attention tiles)."""
+    return D == 128 and T % 128 == 0
+
+
+class QKVRopeAttnFn(Function):
+    """Plain-block attention from the block input in two kernels: the fused [q | k | v]
+    projection GEMM whose epilogue applies RoPE + QK-norm to the q and k heads (and writes
+    their reciprocal RMS), then causal flash attention.  The normalised q / k overwrite
+    their raw values, so no separate normalised copy is written or kept.
+
+    Backward: flash attention backward into one [M, 3C] gradient buffer, the RoPE + QK-norm
+    backward in place on its q / k columns, then dx and the three weight gradients."""
+
+    @staticmethod
+    def forward(ctx, x, cos, sin, B, T, H, D, scale, *ws):
+        from .flash_attention import flash_fwd
+        x2 = gemm._c2(x)
+        fg = fused_group(list(ws))
+        wb = fg[0] if fg is not None else torch.cat([w16(w) for w in ws], 0)
+        Cd = H * D
+        rstd = torch.empty(x2.shape[0] * 2 * H, dtype=torch.float32, device=x.device)
+        qkv = gemm.linear_rope_fwd(x2, wb, cos, sin, T, 2 * Cd, rstd)
+        o, lse = flash_fwd(qkv[:, :Cd], qkv[:, Cd:2 * Cd], qkv[:, 2 * Cd:], B, T, H, D, scale, True)
+        ctx.save_for_backward(x2, qkv, rstd, cos, sin, o, lse)
+        ctx.meta = (B, T, H, D, scale)
+        ctx.ws = ws
+        ctx.shape = x.shape
+        return o.view(B, T, Cd)
+
+    @staticmethod
+    def backward(ctx, dy):
+        from .flash_attention import flash_bwd
+        x2, qkv, rstd, cos, sin, o, lse = ctx.saved_tensors
+        B, T, H, D, scale = ctx.meta
+        Cd = H * D
+        dqkv = torch.empty((B * T, 3 * Cd), dtype=BF16, device=dy.device)
+        flash_bwd(qkv[:, :Cd], qkv[:, Cd:2 * Cd], qkv[:, 2 * Cd:], o, dy.reshape(B * T, Cd), lse, B, T, H, D,
+                  scale, True, dq=dqkv[:, :Cd], dk=dqkv[:, Cd:2 * Cd], dv=dqkv[:, 2 * Cd:])
+        C().rope_norm_bwd(dqkv, qkv, 0, 2 * H, D, cos, sin, T, rstd)
+        dx = _multi_backward(dqkv, x2, list(ctx.ws), ctx.shape, ctx.needs_input_grad[0])
+        return (dx,) + (None,) * (7 + len(ctx.ws))
 
 
 # --------------------------------------------------------------------------- lm_head + CE

@@ -75,6 +75,18 @@ def linear_fwd(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None =
     return _gemm(x2, False, w2, False, M, N, K, out, EPI_BF16, alpha=alpha, R=R)
 
 
+def linear_rope_fwd(x: torch.Tensor, w: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, T: int,
+                    rope_cols: int, rstd: torch.Tensor | None = None) -> torch.Tensor:
+    """x W^T (bf16) with RoPE + per-head RMSNorm (head_dim 128) applied in the GEMM epilogue
+    to the first ``rope_cols`` output columns; position = row % T, cos / sin [>= T, 64].
+    ``rstd`` (fp32, [rows * rope_cols / 128]) receives each head's reciprocal RMS."""
+    x2, w2 = _c2(x), _c2(w)
+    M = x2.shape[0]
+    out = torch.empty((M, w2.shape[0]), dtype=torch.bfloat16, device=x.device)
+    C().gemm_rope(x2, w2, out, cos, sin, int(T), int(rope_cols), rstd, err_word(x.device))
+    return out
+
+
 def linear_relu2_fwd(x: torch.Tensor, w: torch.Tensor, tau: float = 0.0):
     """(relu(x W^T - tau)^2, x W^T) in one pass; both bf16."""
     x2, w2 = _c2(x), _c2(w)
