@@ -112,10 +112,10 @@ def qkv_attention(x: torch.Tensor, ws: list[torch.Tensor], cos, sin, n_head: int
                   scale: float | None):
     """Plain-block attention from the block input x [B, T, C] and the q / k / v weights:
     projection, RoPE + QK-norm on q and k, causal attention.  Returns [B, T, C].  On CUDA
-    with heads of 128 and ``TFB_QKV_ROPE=1`` the RoPE + QK-norm runs in the projection
-    GEMM's epilogue; otherwise it is a separate kernel after the projection."""
+    with heads of 128 the RoPE + QK-norm runs in the projection GEMM's epilogue
+    (``TFB_QKV_ROPE=0`` makes it a separate kernel after the projection)."""
     B, T, _ = x.shape
-    if _cuda(x) and x.dtype == torch.bfloat16 and os.environ.get("TFB_QKV_ROPE", "0") == "1":
+    if _cuda(x) and x.dtype == torch.bfloat16 and os.environ.get("TFB_QKV_ROPE", "1") != "0":
         from .fused import QKVRopeAttnFn, qkv_rope_supported
         if qkv_rope_supported(T, n_head, head_dim):
             c2 = cos.reshape(-1, cos.shape[-1])[:T].contiguous()

@@ -1,8 +1,10 @@
 """Pipeline parallelism: the blocks are cut into ``pp`` contiguous stages, one per rank of a
 pipeline group, and micro-batches flow through them over point-to-point sends
-(``isend`` / ``irecv``: NCCL p2p on GPUs, gloo on CPUs), GPipe order -- every
-micro-batch forward, then every backward in reverse -- with the next activation's
-receive posted while the current micro-batch computes.
+(``batch_isend_irecv``: one NCCL group of p2p sends / receives per boundary crossing on
+GPUs, gloo on CPUs), GPipe order -- every micro-batch forward, then every backward in
+reverse -- with the next activation's receive posted while the current micro-batch
+computes.  The two tensors that cross a boundary together travel as one batch, which on
+NCCL is also what keeps p2p traffic from being serialised as separate collectives.
 
 What crosses a stage boundary is the residual stream ``x`` and the normed embedding
 ``x0`` that every block mixes in (``resid_lambda * x + x0_lambda * x0``); on the way
@@ -50,13 +52,20 @@ class PipelineContext:
         self.lo, self.hi = stage_bounds(n_layer, pp, self.stage)
 
 
-def _send(t: torch.Tensor, dst: int):
-    return dist.isend(t, dst)
+def _send(ts: list[torch.Tensor], dst: int) -> list:
+    """Send the tensors to ``dst`` as one batch; returns the requests."""
+    return dist.batch_isend_irecv([dist.P2POp(dist.isend, t, dst) for t in ts])
 
 
-def _recv(shape, dtype, device, src: int):
-    buf = torch.empty(shape, dtype=dtype, device=device)
-    return buf, dist.irecv(buf, src)
+def _recv(n: int, shape, dtype, device, src: int):
+    """Post ``n`` receives from ``src`` as one batch; returns (buffers, requests)."""
+    bufs = [torch.empty(shape, dtype=dtype, device=device) for _ in range(n)]
+    return bufs, dist.batch_isend_irecv([dist.P2POp(dist.irecv, b, src) for b in bufs])
+
+
+def _wait(reqs) -> None:
+    for r in reqs:
+        r.wait()
 
 
 def pipeline_forward_backward(model, ppc: PipelineContext, batches, loss_scale: float = 1.0) -> torch.Tensor:
@@ -77,18 +86,17 @@ def pipeline_forward_backward(model, ppc: PipelineContext, batches, loss_scale: 
     pending = []
     keep = []           # tensors with a send in flight stay referenced until it completes
     # ------------------------------------------------------------------ forward
-    nxt = _recv(shape, dt, dev, ppc.prev) + _recv(shape, dt, dev, ppc.prev) if not ppc.first else None
+    nxt = _recv(2, shape, dt, dev, ppc.prev) if not ppc.first else None
     for m, (x_ids, y_ids) in enumerate(batches):
         if ppc.first:
             x0 = ops.embed_norm(x_ids, model.transformer.wte.weight, dt)
             x = x0
             x_in = x0_in = None
         else:
-            xb, hx, x0b, hx0 = nxt
-            hx.wait()
-            hx0.wait()
+            (xb, x0b), reqs = nxt
+            _wait(reqs)
             if m + 1 < n:  # post the next receive while this micro-batch computes
-                nxt = _recv(shape, dt, dev, ppc.prev) + _recv(shape, dt, dev, ppc.prev)
+                nxt = _recv(2, shape, dt, dev, ppc.prev)
             x_in = xb.requires_grad_(True)
             x0_in = x0b.requires_grad_(True)
             x, x0 = x_in, x0_in
@@ -105,7 +113,7 @@ def pipeline_forward_backward(model, ppc: PipelineContext, batches, loss_scale: 
         else:
             xs, x0s = x.detach(), x0.detach()
             keep += [xs, x0s]
-            pending += [_send(xs, ppc.next), _send(x0s, ppc.next)]
+            pending += _send([xs, x0s], ppc.next)
             saved.append((x_in, x0_in, (x, x0)))
     # ------------------------------------------------------------------ backward
     for m in reversed(range(n)):
@@ -113,10 +121,8 @@ def pipeline_forward_backward(model, ppc: PipelineContext, batches, loss_scale: 
         if ppc.last:
             (out * (inv * loss_scale * ppc.pp)).backward()
         else:
-            gx, hg = _recv(shape, dt, dev, ppc.next)
-            gx0, hg0 = _recv(shape, dt, dev, ppc.next)
-            hg.wait()
-            hg0.wait()
+            (gx, gx0), reqs = _recv(2, shape, dt, dev, ppc.next)
+            _wait(reqs)
             x_out, x0_out = out
             if ppc.first:
                 torch.autograd.backward([x_out, x0_out], [gx, gx0])
@@ -130,10 +136,9 @@ def pipeline_forward_backward(model, ppc: PipelineContext, batches, loss_scale: 
             gx0i = x0_in.grad if x0_in.grad is not None else torch.zeros(shape, dtype=dt, device=dev)
             gxi, gx0i = gxi.contiguous(), gx0i.contiguous()
             keep += [gxi, gx0i]
-            pending += [_send(gxi, ppc.prev), _send(gx0i, ppc.prev)]
+            pending += _send([gxi, gx0i], ppc.prev)
         saved[m] = None
-    for h in pending:
-        h.wait()
+    _wait(pending)
     # every rank reports the step's mean loss (the last stages hold it; average over the
     # data-parallel pipelines)
     dist.all_reduce(total)
