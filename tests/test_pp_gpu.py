@@ -14,7 +14,8 @@ pytestmark = [pytest.mark.gpu,
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 WORKER = r'''
-import json, os, sys, torch, torch.distributed as dist
+import faulthandler, json, os, sys, torch, torch.distributed as dist
+faulthandler.enable()   # a host-side crash in a rank prints its Python stack
 sys.path.insert(0, os.environ["TFB_ROOT"])
 from trainium_frontier_b200.config import preset
 from trainium_frontier_b200.runtime import init_runtime
@@ -60,7 +61,7 @@ def test_pp2_matches_single_gpu(tmp_path):
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
            "--master-addr", "127.0.0.1", "--master-port", "29547", str(script)]
     p = subprocess.run(["timeout", "-k", "30", "300"] + cmd, env=env, capture_output=True, text=True)
-    assert p.returncode == 0, p.stderr[-4000:]
+    assert p.returncode == 0, p.stdout[-2000:] + "\n" + p.stderr[-6000:]
     res = json.loads([ln for ln in p.stdout.splitlines() if ln.startswith("RESULT ")][-1][len("RESULT "):])
     assert res["checks"][0] == res["checks"][1]
     from trainium_frontier_b200.config import preset
