@@ -39,6 +39,7 @@ xb = torch.randint(1, 8192, (2, 2, 257), generator=gen).to(dev)
 batches = [(r[:, :-1], r[:, 1:]) for r in xb]
 losses = []
 for step in range(4):
+    print("STEP", step, flush=True)
     losses.append(float(eng.forward_backward(batches)))
     eng.sync_and_clip()
     eng.optimizer_step()
