@@ -3,7 +3,9 @@
 Both models start from the same weights (the reference's init, loaded into ours by
 state_dict -- the key layout is shared) and see the same synthetic batches; both
 optimizers get the same per-step lr / momentum / weight-decay schedule.  ws=1 here;
-the gloo ws=2 variant lives in test_parity_reference_dist.py.
+the gloo ws=2 variant is ``test_dist_cpu.py::test_loss_parity_with_reference_ws2``.
+After training, both models are scored by the same ``evaluate_bpb`` on the same held-out
+tokens (parity of held-out bpb at equal training tokens).
 """
 import math
 
@@ -116,3 +118,10 @@ def test_training_loss_parity_ws1(n_steps):
         assert math.isfinite(b)
         assert abs(a - b) <= 1e-3 * abs(a), (i, a, b)
     assert lo_hist[-1] < lo_hist[0] - 1.0
+    # held-out bpb at equal training tokens, scored by the same trusted evaluation
+    from trainium_frontier_b200.eval import evaluate_bpb
+    with torch.no_grad():
+        r_ref = evaluate_bpb(ref, None, 8, 256, "cpu", max_tokens=8192)
+        r_our = evaluate_bpb(ours, None, 8, 256, "cpu", max_tokens=8192)
+    assert r_ref["num_tokens"] == r_our["num_tokens"] >= 8192
+    assert abs(r_ref["val_bpb"] - r_our["val_bpb"]) <= 1e-3 * r_ref["val_bpb"], (r_ref, r_our)
