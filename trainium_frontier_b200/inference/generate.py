@@ -15,6 +15,9 @@
 
 ``generate_reference`` recomputes the full forward for every new token; it is the
 oracle the cached path is tested against and the path for non-plain members.
+
+The reference has no generation path; its forward (``GPT.forward``, ``train.py:3412-3485``)
+is what prefill and the oracle reproduce.
 """
 from __future__ import annotations
 

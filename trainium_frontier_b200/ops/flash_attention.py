@@ -4,6 +4,10 @@
 columns ``[h*D, h*D + D)`` -- exactly the fused projection buffers -- so no
 transposes or copies are made on the way in or out.  Requirements: T % 128 == 0,
 head_dim in {64, 128}.
+
+Reference counterparts: the SDPA call of ``CausalSelfAttention`` (``train.py:2564-2567``)
+and the research NKI kernels it never shipped (``research/scratch/nki_attn_fwd.py:41-132``,
+``research/scratch/nki_attn_bwd.py:1-367``).
 """
 from __future__ import annotations
 

@@ -10,6 +10,12 @@ kernel writes the cache directly, so in training it is never re-cast here).
 The gradient of x0 (the normed embedding, an input of every block's residual mix) is
 accumulated in fp32 across layers through a side buffer owned by the embedding node,
 so 20+ bf16 partial sums are never rounded on the way.
+
+Reference counterparts: relu² (``train.py:1465-1515``, eager ``train.py:2218-2234``),
+RoPE + QK-norm forward / backward (``train.py:1543-1702``, wrapper ``train.py:2423-2436``),
+softcapped cross-entropy (``train.py:1768-1925``, wrapper ``train.py:2163-2215``), the
+bf16 weight cache of ``Linear`` (``train.py:2237-2267``), parameter-free RMSNorm
+(``train.py:1432-1433``).
 """
 from __future__ import annotations
 

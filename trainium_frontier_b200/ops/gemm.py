@@ -8,6 +8,9 @@ The three products of a linear layer read their operands in place:
                                                          split-K over the token axis
 Fused epilogues: residual add, relu^2 (with the pre-activation kept for backward),
 relu^2 backward, fp32 accumulate into the gradient buffer.
+
+Reference counterpart: ``Linear.forward`` (``train.py:2237-2267``), which reaches cuBLAS
+through ``F.linear`` on CUDA; the Newton-Schulz matmul chain (``train.py:3629-3636``).
 """
 from __future__ import annotations
 

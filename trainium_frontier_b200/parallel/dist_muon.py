@@ -20,6 +20,10 @@ Everything outside the blocks' Muon matrices (embeddings, lm_head, scalars, gate
 is all-reduced and updated with AdamW on every rank.  Gradient clipping uses the global
 norm of the averaged gradient (owner partial sums of squares + the all-reduced rest,
 one scalar all-reduce).
+
+Reference counterparts: the per-rank ``_muon_step`` that runs Newton-Schulz on every
+matrix (``train.py:4130-4336``) and the per-parameter ``all_reduce(AVG)`` of
+``sync_gradients`` (``train.py:4412-4420``); the reference has no sharded Muon.
 """
 from __future__ import annotations
 

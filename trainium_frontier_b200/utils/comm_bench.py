@@ -21,6 +21,9 @@ Roofline per path = max(bytes crossing NVLink into this GPU / link bandwidth, lo
 bytes / HBM bandwidth), with the link bandwidth the measured 770 GB/s per direction peer
 copy (nominal 900) and the HBM bandwidth from the measured peaks file when present.
 The default size is the d20 model's Muon matrices (20 x (4 x 1280^2 + 2 x 1280 x 5120)).
+
+Reference counterparts: its only gradient collectives, the per-parameter and flat-buffer
+all-reduces (``train.py:4412-4460``).
 """
 from __future__ import annotations
 

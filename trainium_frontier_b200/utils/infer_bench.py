@@ -16,6 +16,9 @@ Two workloads, both through the public API (``checkpoint.load_for_eval``):
 The reference arm loads the same checkpoint with the reference's own ``load_for_eval`` and
 scores it with its own ``evaluate_bpb`` (its loader and byte table pointed at the same
 synthetic stream); the reference has no generation path, so its decode entry says so.
+
+Reference counterparts: ``load_for_eval`` (``train.py:4706-4743``) and ``evaluate_bpb``
+(``prepare.py:595-659``).
 """
 from __future__ import annotations
 

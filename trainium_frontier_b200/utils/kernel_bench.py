@@ -7,6 +7,9 @@ buffer larger than the 126 MB L2) between them, CUDA events on the launching str
 with a synchronize on both sides.  Reports achieved TFLOP/s or GB/s and the fraction
 of the measured peaks in MEASURED_PEAKS.json (the torch cuBLAS GEMM is timed the same
 way alongside as a reference point).
+
+Reference counterparts: the research micro-benchmarks ``research/scratch/muon_nki_bench.py``
+and ``research/scratch/embed_gather_bench.py``.
 """
 from __future__ import annotations
 

@@ -5,6 +5,9 @@
 Runs ``--warmup`` steps, then brackets exactly one step with cudaProfilerStart/Stop
 (so ``ncu --profile-from-start off`` sees only that step) and NVTX ranges per phase.
 Without a profiler attached it prints the per-phase CUDA-event times of that step.
+
+Reference counterpart: ``research/scratch/phase_timer.py`` (per-phase synchronized
+timing of a steady-state step).
 """
 from __future__ import annotations
 
