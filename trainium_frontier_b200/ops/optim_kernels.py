@@ -1,4 +1,5 @@
 """Python front-end of the optimizer kernels (``csrc/kernels/optim_kernels.cu``).
+
 Reference counterpart: the foreach AdamW / RMSProp of ``MuonAdamW`` (``train.py:3961-4127``).
 """
 from __future__ import annotations
