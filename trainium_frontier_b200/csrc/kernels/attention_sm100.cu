@@ -21,6 +21,8 @@
 // dQ drained by dedicated warps).  TFB_FA_FWD_ONE_TILE / TFB_FA_BWD_SERIAL select the
 // simple forms above (kept as the reference the fast forms are tested against).
 // Every wait is bounded (see sm100_common.cuh); every TMA load is a plain per-CTA load.
+// Reference counterparts: the SDPA call of CausalSelfAttention (train.py:2564-2567) and the
+// research NKI kernels research/scratch/nki_attn_fwd.py:41-132 and nki_attn_bwd.py:1-367.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>

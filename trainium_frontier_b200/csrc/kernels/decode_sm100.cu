@@ -9,6 +9,8 @@
 //   phase 2  thread-per-dimension output o[d] = sum_k p_k v_k[d] / l (coalesced rows).
 // kv_append: writes this step's k and v rows into the caches at the device-side
 // position; step_advance: increments the device-side position / length counters.
+// The reference has no decode path; the attention is the math of train.py:2564-2567 over a
+// key/value cache.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>

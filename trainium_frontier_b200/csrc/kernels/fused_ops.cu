@@ -9,6 +9,9 @@
 //     bf16 logits (the per-row gradient overwrites the logits in place).
 // Rows are processed one warp per row with 16-byte vector loads; eps = FLT_EPSILON as
 // in F.rms_norm with fp32 opmath.
+// Reference counterparts: norm (train.py:1432-1433), RoPE + QK-norm (train.py:1543-1702),
+// softcapped cross-entropy (train.py:1768-1925), the embedding lookup and residual mix of
+// GPT.forward / Block (train.py:3412-3485, train.py:2631-2764).
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>

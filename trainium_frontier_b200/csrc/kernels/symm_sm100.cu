@@ -19,6 +19,8 @@
 //                    cache in the same pass.
 // Every wait is bounded (2 s) and reports into the device error word; the peer loads
 // are plain ld.global (no TMA, no cluster broadcast).
+// Reference counterparts: sync_gradients (train.py:4412-4420), the Muon math
+// (train.py:3540-3647) and its update kernel (train.py:2023-2078).
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
