@@ -132,10 +132,15 @@ def pipeline_forward_backward(model, ppc: PipelineContext, batches, loss_scale: 
             (gx, gx0), reqs = _recv(2, shape, dt, dev, ppc.next)
             _wait(reqs)
             x_out, x0_out = out
+            # Driven through the scalar <x_out, gx> (+ <x0, gx0> on the first stage): its
+            # gradient with respect to x_out is exactly the received gx (the fp32 product's
+            # backward casts gx back to bf16 without rounding), and the first backward node
+            # is a plain PyTorch op, as in the single-device step.
+            root = (x_out.float() * gx.float()).sum()
             if ppc.first:
-                torch.autograd.backward([x_out, x0_out], [gx, gx0])
-            else:
-                torch.autograd.backward([x_out], [gx])
+                root = root + (x0_out.float() * gx0.float()).sum()
+            root.backward()
+            if not ppc.first:
                 # x0 passes through this stage unchanged: add the gradient arriving from
                 # the later stages to what this stage's blocks contributed
                 x0_in.grad = gx0 if x0_in.grad is None else x0_in.grad + gx0
