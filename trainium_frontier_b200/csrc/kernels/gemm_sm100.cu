@@ -1080,6 +1080,25 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
+// cuTensorMapEncodeTiled is a driver call and runs against whatever context is current on
+// the calling thread.  The runtime makes a device's primary context current lazily, on the
+// first runtime call of a thread that needs one, and the device guard skips cudaSetDevice
+// when the requested index already equals the runtime's current one (0 on a fresh thread).
+// So on a thread whose first CUDA work is a tensor-map encode -- PyTorch's autograd thread
+// for device 0 when a backward pass starts in one of these ops -- no context is current
+// yet, and the encode crashed the process there.  cudaSetDevice binds the primary context;
+// it is issued once per thread and device (so never during a graph capture that follows
+// warm-up calls).
+static void bind_device_context() {
+  thread_local int bound = -1;
+  int dev = 0;
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  if (bound != dev) {
+    C10_CUDA_CHECK(cudaSetDevice(dev));
+    bound = dev;
+  }
+}
+
 // 2-D bf16 tensor map with 128-byte swizzle.  inner/outer are element extents,
 // row_stride_elems the distance between consecutive outer indices.
 CUtensorMap make_tmap_bf16(const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
@@ -1087,6 +1106,7 @@ CUtensorMap make_tmap_bf16(const void* ptr, uint64_t inner, uint64_t outer, uint
   TORCH_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "TMA base address must be 16-byte aligned");
   TORCH_CHECK((row_stride_elems * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
   TORCH_CHECK(batch == 1 || (batch_stride_elems * 2) % 16 == 0, "TMA batch stride must be a multiple of 16 bytes");
+  bind_device_context();
   CUtensorMap m;
   cuuint64_t dims[3] = {inner, outer, batch};
   cuuint64_t strides[2] = {row_stride_elems * 2, (batch > 1 ? batch_stride_elems : row_stride_elems * outer) * 2};
@@ -1105,6 +1125,7 @@ CUtensorMap make_tmap_f32(const void* ptr, uint64_t inner, uint64_t outer, uint6
   TORCH_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "TMA base address must be 16-byte aligned");
   TORCH_CHECK((row_stride_elems * 4) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
   TORCH_CHECK(box_inner * 4 <= 128, "128-byte swizzle: inner box of at most 32 fp32");
+  bind_device_context();
   CUtensorMap m;
   cuuint64_t dims[3] = {inner, outer, 1};
   cuuint64_t strides[2] = {row_stride_elems * 4, row_stride_elems * outer * 4};
