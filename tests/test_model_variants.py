@@ -65,3 +65,21 @@ def test_variant_trains(name):
     assert all(l == l for l in losses) and losses[-1] < losses[0], losses
     if name == "block_nudge_qk":
         assert all(float(b.block_nudge.abs().sum()) == 0.0 for b in m.transformer.h)
+
+
+def test_qkv_attention_entry_matches_composition():
+    """ops.qkv_attention (projection + RoPE + QK-norm + attention from the block input)
+    equals the projection followed by attention_qkv on the CPU oracle path."""
+    from trainium_frontier_b200 import ops
+    torch.manual_seed(5)
+    B, T, H, D = 2, 128, 2, 64
+    C = H * D
+    t = torch.arange(T, dtype=torch.float32)
+    inv = 1.0 / (10000 ** (torch.arange(0, D, 2, dtype=torch.float32) / D))
+    tab = torch.outer(t, inv)
+    cos, sin = tab.cos()[None, :, None, :], tab.sin()[None, :, None, :]
+    x = torch.randn(B, T, C)
+    ws = [torch.randn(C, C) * C ** -0.5 for _ in range(3)]
+    a = ops.qkv_attention(x, ws, cos, sin, H, D, None)
+    b = ops.attention_qkv(ops.linear_multi(x, ws), cos, sin, H, D, None)
+    assert a.shape == (B, T, C) and torch.allclose(a, b)
