@@ -8,8 +8,11 @@ with a synchronize on both sides.  Reports achieved TFLOP/s or GB/s and the frac
 of the measured peaks in MEASURED_PEAKS.json (the torch cuBLAS GEMM is timed the same
 way alongside as a reference point).
 
-Reference counterparts: the research micro-benchmarks ``research/scratch/muon_nki_bench.py``
-and ``research/scratch/embed_gather_bench.py``.
+Reference counterparts: its research micro-benchmarks (``research/scratch/muon_nki_bench.py``,
+``research/scratch/embed_gather_bench.py``) time the Muon and embedding-gather kernels,
+which this file does not cover; here the Newton-Schulz GEMMs and the embedding kernels
+are timed inside their step phases by ``utils/profile_step.py`` (and listed per launch
+by an ``ncu`` launch capture of it).
 """
 from __future__ import annotations
 
