@@ -48,6 +48,7 @@ CONFIGS = {
             "global_batch": 1048576, "seq_len": 4096},
 }
 CONFIG = CONFIGS["d20"]
+L2_NOTE = "inputs larger than L2 (multi-GB activations per micro-step); no flush"
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -199,9 +200,8 @@ def run_ours(args) -> dict:
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded Zipf(1.1) token stream, BOS=0 docs of geometric mean length 200; random-init weights)",
         "config": dict(CONFIG, parallelism=f"dp{world}" if args.tp == 1 else f"tp{args.tp}xdp{world // args.tp}",
-                       micro_batch_rows=rows_micro, grad_accum=tr.grad_accum,
-                       grad_sync=tr.engine.grad_sync, n_params=n_params,
-                       l2="inputs larger than L2 (multi-GB activations per micro-step); no flush"),
+                       micro_batch_rows=rows_micro, grad_accum=tr.grad_accum, l2=L2_NOTE),
+        "detail": {"grad_sync": tr.engine.grad_sync, "n_params": n_params, "clip_order": "global"},
         "e2e": {"value": tok / (e2e_ms / 1000.0), "unit": "tokens/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": tr.h2d_bytes_per_step, "d2h_bytes_per_step": 4,
                 "api": "trainium_frontier_b200.train.Trainer.train_step"},
@@ -214,7 +214,31 @@ def run_ours(args) -> dict:
 
 
 # ----------------------------------------------------------------------------- reference
+def zipf_rows(n_rows: int, seq_len: int, seed: int, vocab: int = 8192, s: float = 1.1,
+              mean_doc: float = 200.0):
+    """[n_rows, seq_len + 1] int32 rows of the benchmark's token statistics, written with
+    numpy only so the reference process maps nothing of this framework: ids Zipf(s) over
+    [1, vocab) by inverse CDF, a BOS (id 0) opening every document, document lengths
+    geometric with mean ``mean_doc``, documents concatenated and cut into rows."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    k = np.arange(1, vocab, dtype=np.float64)
+    cdf = np.cumsum(k ** -s)
+    cdf /= cdf[-1]
+    n = n_rows * (seq_len + 1)
+    toks = (np.searchsorted(cdf, rng.random(n), side="right") + 1).clip(1, vocab - 1)
+    starts = np.cumsum(rng.geometric(1.0 / mean_doc, size=n // 8 + 16) + 1) - 1
+    toks[0] = 0
+    toks[starts[starts < n]] = 0
+    return toks.astype(np.int32).reshape(n_rows, seq_len + 1)
+
+
 def run_reference(args) -> dict:
+    """The unmodified reference module (installed under baseline/_ref) driven through its
+    own GPT / init_weights / torch.compile(inductor) / setup_optimizer / clip /
+    sync_gradients (per-parameter all-reduce) / MuonAdamW.step path, as its main() does
+    (train.py:5846-5885 build, :5999-6258 step loop, :4412-4420 sync).  Nothing of this
+    framework is imported here: token rows come from ``zipf_rows`` (numpy)."""
     ref_dir = os.path.join(ROOT, "baseline", "_ref")
     if not os.path.exists(os.path.join(ref_dir, "train.py")):
         return {"impl": "reference", "unavailable": "baseline/_ref not installed"}
@@ -223,10 +247,9 @@ def run_reference(args) -> dict:
     sys.path.insert(0, ref_dir)
     saved_argv = sys.argv
     sys.argv = ["train.py"]
-    import prepare as rprep  # noqa: E402
+    import prepare as rprep  # noqa: E402,F401
     import train as rtrain  # noqa: E402
     sys.argv = saved_argv
-    from trainium_frontier_b200.data.loader import PackedRowLoader
     CONFIG = CONFIGS[args.preset]
     # the plain family at the preset's shape, through the reference's own globals / API
     rtrain.DEPTH, rtrain.N_EMBD = {"d20": (20, 1280), "d12": (12, 768), "d26": (26, 1664)}[args.preset]
@@ -237,48 +260,75 @@ def run_reference(args) -> dict:
     rtrain.USE_LOCAL_CONV = False
     rtrain.USE_QK_SHIFT = False
     rtrain.COMPUTE_DTYPE = rtrain.compute_dtype_for(dev)
-    rows_micro = args.ref_micro_rows
-    rtrain.DEVICE_BATCH_SIZE = rows_micro
     rtrain.PACK_FACTOR = 1
-    world_tokens_micro = rows_micro * CONFIG["seq_len"] * world
-    grad_accum = CONFIG["global_batch"] // world_tokens_micro
-    torch.manual_seed(42)
-    config = rtrain.build_config()
-    model = rtrain.GPT(config)
-    model.init_weights()
-    model.to(dev)
-    orig = model
-    model = torch.compile(model, backend="inductor", dynamic=False)
-    opt = orig.setup_optimizer()
-    cached = [m for m in orig.modules() if isinstance(m, rtrain.Linear)]
-    loader = PackedRowLoader(rows_micro, CONFIG["seq_len"], dev, "train", rank=rank)
-    staged = []
-    for _ in range(grad_accum):
-        r = loader.next().clone()
-        staged.append((r[:, :-1].contiguous(), r[:, 1:].long().contiguous()))
-    clip_main, clip_ng = rtrain.split_clip_params(orig)
+    per_gpu_rows = CONFIG["global_batch"] // (CONFIG["seq_len"] * world)
+    rows_micro = min(args.ref_micro_rows or args.micro_rows, per_gpu_rows)
 
-    def step(batches, i):
-        opt.zero_grad(set_to_none=True)
-        last = None
-        for x, y in batches:
-            loss = model(x, y)
-            last = loss.detach()
-            (loss / grad_accum).backward()
-        torch.nn.utils.clip_grad_norm_(clip_main, rtrain.GRAD_CLIP, foreach=True)
-        rtrain.sync_gradients(model)
-        lrm = rtrain.lr_multiplier(i, elapsed=0.0, max_train_seconds=rtrain.MAX_TRAIN_SECONDS)
-        for group in opt.param_groups:
-            group["lr"] = group["initial_lr"] * lrm
-            if group["kind"] == "muon":
-                group["momentum"] = rtrain.muon_momentum(i, 0.0)
-                group["weight_decay"] = rtrain.WEIGHT_DECAY
-        opt.step()
-        for m in cached:
-            m.refresh_weight_cache(rtrain.COMPUTE_DTYPE)
-        return last
+    def build(rows):
+        rtrain.DEVICE_BATCH_SIZE = rows
+        torch.manual_seed(42)
+        model = rtrain.GPT(rtrain.build_config())
+        model.init_weights()
+        model.to(dev)
+        return model
 
-    for i in range(args.warmup):
+    def stage(rows, n, seed):
+        blk = torch.from_numpy(zipf_rows(rows * n, CONFIG["seq_len"], seed))
+        out = []
+        for i in range(n):
+            r = blk[i * rows:(i + 1) * rows].to(dev, non_blocking=False)
+            out.append((r[:, :-1].contiguous(), r[:, 1:].long().contiguous()))
+        return out
+
+    # Largest micro-batch (starting at this framework's) whose warm-up fits in memory.
+    while True:
+        grad_accum = CONFIG["global_batch"] // (rows_micro * CONFIG["seq_len"] * world)
+        orig = build(rows_micro)
+        model = torch.compile(orig, backend="inductor", dynamic=False)
+        opt = orig.setup_optimizer()
+        cached = [m for m in orig.modules() if isinstance(m, rtrain.Linear)]
+        clip_main, _clip_ng = rtrain.split_clip_params(orig)
+        staged = stage(rows_micro, grad_accum, 1234 + 7919 * (rank + 1))
+
+        def step(batches, i):
+            opt.zero_grad(set_to_none=True)
+            last = None
+            for x, y in batches:
+                loss = model(x, y)
+                last = loss.detach()
+                (loss / grad_accum).backward()
+            torch.nn.utils.clip_grad_norm_(clip_main, rtrain.GRAD_CLIP, foreach=True)
+            rtrain.sync_gradients(model)
+            lrm = rtrain.lr_multiplier(i, elapsed=0.0, max_train_seconds=rtrain.MAX_TRAIN_SECONDS)
+            for group in opt.param_groups:
+                group["lr"] = group["initial_lr"] * lrm
+                if group["kind"] == "muon":
+                    group["momentum"] = rtrain.muon_momentum(i, 0.0)
+                    group["weight_decay"] = rtrain.WEIGHT_DECAY
+            opt.step()
+            for m in cached:
+                m.refresh_weight_cache(rtrain.COMPUTE_DTYPE)
+            return last
+
+        oom = 0
+        try:
+            step(staged, 0)
+        except torch.cuda.OutOfMemoryError:
+            oom = 1
+        # every rank takes the same branch
+        if world > 1:
+            import torch.distributed as dist
+            t = torch.tensor([oom], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            oom = int(t.item())
+        if not oom or rows_micro == 1:
+            break
+        del model, orig, opt, cached, clip_main, staged
+        torch._dynamo.reset()
+        torch.cuda.empty_cache()
+        rows_micro //= 2
+
+    for i in range(1, args.warmup):
         step(staged, i)
     barrier_sync(dev)
     clocks = ClockSampler(local)
@@ -292,27 +342,33 @@ def run_reference(args) -> dict:
     barrier_sync(dev)
     clk = clocks.stop()
     ms = max_over_ranks(start.elapsed_time(end) / args.steps, dev)
-    # end to end: fresh rows each step via H2D, loss read back.  The reference's step is
-    # tens of seconds on one GPU, so this loop is capped at two steps to bound the arm's time.
+    # end to end: fresh rows each step, copied host->device from pinned memory, loss read
+    # back.  The reference's step is seconds to tens of seconds, so this loop is capped at
+    # two steps to bound the arm's time.
     n_e2e = min(args.steps, 2)
+    host = [torch.from_numpy(zipf_rows(rows_micro * grad_accum, CONFIG["seq_len"], 99 + 13 * rank + i)).pin_memory()
+            for i in range(n_e2e)]
     barrier_sync(dev)
     t0 = time.perf_counter()
     for i in range(n_e2e):
         bs = []
-        for _ in range(grad_accum):
-            r = loader.next()
+        for j in range(grad_accum):
+            r = host[i][j * rows_micro:(j + 1) * rows_micro].to(dev, non_blocking=True)
             bs.append((r[:, :-1].contiguous(), r[:, 1:].long().contiguous()))
-        float(step(bs, i).item())
+        float(step(bs, args.warmup + args.steps + i).item())
     barrier_sync(dev)
     e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1000.0 / n_e2e, dev)
     tok = CONFIG["global_batch"]
     return {
         "metric": METRIC, "value": tok / (ms / 1000.0), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "fp32 blocks (the reference's shape-[1] fp32 lambdas promote its residual stream to fp32 on CUDA, so every block matmul runs in fp32; embeddings / rotary tables bf16)",
-        "data": "synthetic (seeded Zipf(1.1) token stream; random-init weights)",
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16 weights; block GEMMs in fp32 (the reference's shape-[1] fp32 resid/x0 lambdas promote its residual stream to fp32 on CUDA, TF32 off)",
+        "data": "synthetic (seeded Zipf(1.1) token stream, BOS=0 docs of geometric mean length 200; random-init weights)",
         "config": dict(CONFIG, parallelism=f"dp{world}", micro_batch_rows=rows_micro, grad_accum=grad_accum,
-                       path="reference train.py: torch.compile(inductor) + SDPA + eager Muon + per-param all_reduce"),
+                       l2=L2_NOTE),
+        "detail": {"path": "reference train.py: torch.compile(inductor) + SDPA + eager Muon + per-parameter all_reduce",
+                   "grad_sync": "per-parameter all_reduce", "requested_micro_rows": args.ref_micro_rows or args.micro_rows},
         "e2e": {"value": tok / (e2e_ms / 1000.0), "unit": "tokens/s", "ms_per_step": e2e_ms, "steps": n_e2e,
                 "h2d_bytes_per_step": grad_accum * rows_micro * (CONFIG["seq_len"] + 1) * 4, "d2h_bytes_per_step": 4},
         "gpu_launches": 0,
@@ -344,7 +400,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--micro-rows", type=int, default=0,
                     help="sequences per micro-step per GPU (default: 32 at seq 2048, 4 for d26 at seq 4096)")
-    ap.add_argument("--ref-micro-rows", type=int, default=4, help="reference arm sequences per micro-step")
+    ap.add_argument("--ref-micro-rows", type=int, default=0,
+                    help="reference arm sequences per micro-step (default: the same as --micro-rows; halved "
+                         "until its first step fits in memory)")
     ap.add_argument("--grad-sync", default="auto")
     ap.add_argument("--preset", default="d20", choices=sorted(CONFIGS), help="model / batch configuration")
     ap.add_argument("--tp", type=int, default=1, help="tensor-parallel degree (ours; DP = N / tp)")

@@ -27,3 +27,35 @@ def test_validation():
         RunConfig(n_embd=100, head_dim=64).model_config()
     with pytest.raises(ValueError):
         RunConfig(depth=6, n_kv_heads=3).model_config()
+
+
+def test_reference_only_flags_parse():
+    """Launch commands written for the reference carry switches whose effect this
+    framework always has; they parse, and the ones with an effect here map to it."""
+    from trainium_frontier_b200.config import ACCEPTED_NO_EFFECT_FLAGS
+    argv = []
+    for flag in ACCEPTED_NO_EFFECT_FLAGS:
+        argv.append(flag)
+    argv += ["--no-nki-muon", "--grad-bucket", "--no-transposed-linear", "--epoch-shuffle",
+             "--epoch-shuffle-seed", "77", "--attn-cproj-init", "0.25", "--no-out-bigram-bf16",
+             "--coalesced-swiglu-hidden", "256"]
+    cfg = parse_args(argv)
+    assert cfg.grad_sync == "bucket"
+    assert cfg.epoch_shuffle and cfg.epoch_shuffle_seed == 77
+    assert cfg.attn_cproj_init_scale == 0.25 and cfg.out_bigram_bf16 is False
+    assert cfg.coalesced_swiglu_hidden == 256
+    with pytest.raises(ValueError, match="transposed-linear"):
+        parse_args(["--transposed-linear"])
+    with pytest.raises(ValueError):
+        parse_args(["--coalesced-swiglu-hidden", "100"])
+
+
+def test_coalesced_swiglu_hidden_and_bigram_dtype_shape_the_model():
+    import torch
+    from trainium_frontier_b200.models.gpt import GPT
+    rc = preset("tiny", depth=2, coalesced_swiglu=True, coalesced_swiglu_hidden=384, out_bigram=True)
+    m = GPT(rc.model_config(), rc)
+    assert m.transformer.h[0].mlp.c_fc.weight.shape == (2 * 384, 256)
+    assert m.out_bigram.weight.dtype == torch.bfloat16
+    rc2 = rc.replace(out_bigram_bf16=False)
+    assert GPT(rc2.model_config(), rc2).out_bigram.weight.dtype == torch.float32

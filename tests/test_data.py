@@ -66,3 +66,31 @@ def test_eval_loader_tail_padding():
     assert (y == -1).any()
     total_valid = sum(int((b[1] >= 0).sum()) for b in batches)
     assert total_valid == 999  # a stream of 1000 tokens has 999 next-token targets
+
+
+def test_epochs_replay_or_reshuffle():
+    """A finite synthetic epoch replays in the same order without shuffling and takes a
+    fresh seeded order from epoch 2 with it; the loader reports the epoch."""
+    T, per_epoch = 128, 5
+
+    def rows(shuffle, seed=1234, n=3):
+        ld = PackedRowLoader(per_epoch, T, torch.device("cpu"), "train", seed=9, rank=0,
+                             epoch_tokens=per_epoch * (T + 1), epoch_shuffle=shuffle, epoch_shuffle_seed=seed)
+        return [ld.next().clone() for _ in range(n)], ld
+
+    plain, _ = rows(False)
+    assert torch.equal(plain[0], plain[1]) and torch.equal(plain[1], plain[2])
+    shuf, ld = rows(True)
+    assert not torch.equal(shuf[0], shuf[1]) and not torch.equal(shuf[1], shuf[2])
+    shuf2, _ = rows(True)
+    assert all(torch.equal(a, b) for a, b in zip(shuf, shuf2))   # deterministic per seed
+    shuf3, _ = rows(True, seed=99)
+    assert torch.equal(shuf3[0], shuf[0]) and not torch.equal(shuf3[1], shuf[1])
+    assert ld.epoch >= 3
+    # an epoch boundary inside a batch: 3-row batches over 5-row epochs
+    ld = PackedRowLoader(3, T, torch.device("cpu"), "train", seed=9, rank=0, epoch_tokens=5 * (T + 1))
+    a, b = ld.next().clone(), ld.next().clone()
+    assert torch.equal(b[2], a[0])   # row 6 of the stream is row 1 of epoch 2
+    tok = syn.SyntheticTokenizer()
+    it = make_dataloader(tok, 2, T, "train", "cpu", epoch_tokens=2 * (T + 1))
+    assert [next(it)[2]["epoch"] for _ in range(3)] == [1, 2, 3]

@@ -182,6 +182,7 @@ class RunConfig:
     relu2_tau: float = 0.0
     gated_mlp: bool = False
     coalesced_swiglu: bool = False
+    coalesced_swiglu_hidden: int = 0   # forced coalesced-SwiGLU hidden width (multiple of 128); 0 = parameter-matched
     parallel_block: bool = False
     doc_mask: bool = False
     window_pattern: str = "L"
@@ -189,6 +190,7 @@ class RunConfig:
     out_bigram: bool = False
     out_bigram_gate_bias: float = -2.0
     out_bigram_lr: float = 0.0
+    out_bigram_bf16: bool = True       # store the [V, V] output-bigram table in bf16
     engram: bool = False
     engram_table_mult: int = 32
     engram_mem_dim: int = 128
@@ -220,6 +222,13 @@ class RunConfig:
     tp: int = 1                     # tensor-parallel degree (DP = world / tp)
     pp: int = 1                     # pipeline stages (DP = world / pp); tp and pp are exclusive
     checkpoint_activations: bool = False
+    # ---- data ----------------------------------------------------------------------
+    synthetic_epoch_tokens: int = 0    # tokens per epoch of the synthetic train stream per rank; 0 = endless
+    epoch_shuffle: bool = False        # from epoch 2 on, a fresh order (seed + epoch) instead of epoch 1 replayed
+    epoch_shuffle_seed: int = 1234
+    # ---- reference switches with a real effect here --------------------------------
+    grad_bucket: bool = False          # one flat-buffer gradient all-reduce: maps to grad_sync=bucket under auto
+    transposed_linear: bool = False    # [in, out] weight storage: not built (changes the checkpoint layout)
 
     # ------------------------------------------------------------------------------
     def model_config(self) -> GPTConfig:
@@ -254,7 +263,7 @@ SHAPE_CRITICAL_TOGGLES = (
     "ve", "ngram_ve", "ngram_ve_layers", "ngram_ve_table_mult", "ngram_ve_trigram",
     "ngram_ve_dim", "ngram_ve_bf16", "local_conv", "local_conv_kernel", "qk_shift",
     "head_gate", "out_pool", "out_pool_layers", "x0_gate", "gated_mlp", "coalesced_swiglu",
-    "parallel_block", "out_bigram", "engram", "engram_table_mult", "engram_mem_dim",
+    "coalesced_swiglu_hidden", "parallel_block", "out_bigram", "engram", "engram_table_mult", "engram_mem_dim",
     "engram_conv_kernel", "engram_site", "engram_orders", "engram_heads", "engram_key_dim",
     "engram_share_ngram_tables", "engram_bf16", "parallel_block_coalesce", "block_nudge", "block_nudge_site",
     "selective_gate", "selective_gate_channels",
@@ -263,7 +272,7 @@ ARCH_TOGGLE_NAMES = SHAPE_CRITICAL_TOGGLES + (
     "rope_base", "logit_softcap", "ve_gate_channels", "qk_shift_beta", "qk_shift_freeze",
     "head_gate_norm", "head_gate_channels", "head_gate_bias", "head_gate_mul",
     "mlp_sandwich_norm", "relu2_tau", "doc_mask", "window_pattern", "short_window_frac",
-    "out_bigram_gate_bias",
+    "out_bigram_gate_bias", "out_bigram_bf16",
 )
 
 
@@ -292,12 +301,37 @@ def build_parser(base: RunConfig | None = None) -> argparse.ArgumentParser:
     # reference-compatible aliases
     p.add_argument("--compile", dest="_compile", action=argparse.BooleanOptionalAction, default=False,
                    help="accepted for launch-command compatibility; the B200 path has no tracing compiler")
+    p.add_argument("--attn-cproj-init", dest="attn_cproj_init_scale", type=float,
+                   default=_env_default("attn_cproj_init", getattr(base, "attn_cproj_init_scale")),
+                   help="the reference's name of --attn-cproj-init-scale")
+    # Reference switches (train.py:5014-5110, :5341, :5470) whose effect this framework
+    # always has on CUDA, so they are accepted and change nothing:
+    for flag, why in ACCEPTED_NO_EFFECT_FLAGS.items():
+        p.add_argument(flag, dest="_ref_" + flag[2:].replace("-", "_"), action=argparse.BooleanOptionalAction,
+                       default=None, help="accepted; no effect here: " + why)
     return p
+
+
+# Reference flags accepted for launch-command compatibility, each with why it has no
+# effect on this framework's path.
+ACCEPTED_NO_EFFECT_FLAGS = {
+    "--compile-muon": "Muon's math always runs as fused sm_100a kernels (no tracing compiler)",
+    "--foreach-optim": "AdamW is always one multi-tensor launch per group",
+    "--clip-foreach": "the clip norm is one fused reduction over the flat gradient buffer",
+    "--tensor-lr-scalars": "learning rates and decays always live in device scalars",
+    "--nki-relu2": "relu^2 always runs in the MLP GEMM's epilogue on CUDA",
+    "--nki-rope-norm": "RoPE + QK-norm always runs fused (QKV GEMM epilogue or its own kernel) on CUDA",
+    "--nki-softcap-ce": "softcap + cross-entropy always runs as the fused kernel on CUDA",
+    "--nki-muon": "Muon's elementwise steps always run in GEMM epilogues / fused kernels on CUDA",
+    "--qkv-norm-cse": "the fused QKV projection normalises its input once by construction",
+}
 
 
 def parse_args(argv: list[str] | None = None, base: RunConfig | None = None) -> RunConfig:
     ns = build_parser(base).parse_args(argv)
     kw = {f.name: getattr(ns, f.name) for f in fields(RunConfig)}
+    if kw["grad_bucket"] and kw["grad_sync"] == "auto":
+        kw["grad_sync"] = "bucket"
     cfg = RunConfig(**kw)
     validate(cfg)
     return cfg
@@ -311,6 +345,14 @@ def validate(cfg: RunConfig) -> None:
         raise ValueError("--progress-mode must be 'time' or 'steps'")
     if cfg.grad_sync not in ("auto", "per_param", "bucket", "dist_muon", "fused"):
         raise ValueError(f"unknown --grad-sync {cfg.grad_sync}")
+    if cfg.transposed_linear:
+        raise ValueError("--transposed-linear ([in, out] weight storage) is not built: the tcgen05 GEMM reads "
+                         "[out, in] weights K-major in place, and the flag would change every Linear's "
+                         "state_dict shape; use --no-transposed-linear (the reference's default)")
+    if cfg.coalesced_swiglu_hidden % 128 or cfg.coalesced_swiglu_hidden < 0:
+        raise ValueError("--coalesced-swiglu-hidden must be 0 (auto) or a positive multiple of 128")
+    if cfg.synthetic_epoch_tokens < 0:
+        raise ValueError("--synthetic-epoch-tokens must be >= 0")
     if cfg.coalesced_swiglu and cfg.gated_mlp:
         raise ValueError("--coalesced-swiglu and --gated-mlp are mutually exclusive")
     if cfg.adam_every_n < 1:

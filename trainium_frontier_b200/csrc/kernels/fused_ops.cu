@@ -433,22 +433,21 @@ __global__ void softcap_ce_kernel(__nv_bfloat16* __restrict__ logits, long long 
   const long long c_ll = (long long)tgt[(long long)b * tgt_ld + t];
   __nv_bfloat16* z = logits + (long long)row * ld;
   __shared__ float red[32];
-  __shared__ float s_yc;
   const int tid = threadIdx.x, nt = blockDim.x;
   const float invS = 1.f / S;
+  const bool valid = c_ll >= 0 && c_ll < V;
+  // The target's capped logit, read by the thread that writes the loss before any
+  // thread can reach the gradient pass (which overwrites the row after two barriers).
+  float yc = 0.f;
+  if (tid == 0 && valid) yc = S * tanhf(__bfloat162float(z[c_ll]) * invS);
   float sum = 0.f;
-  if (tid == 0) s_yc = 0.f;
   for (int j0 = tid * 8; j0 < Vpad; j0 += nt * 8) {
     float f[8];
     load8(z + j0, f);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const int j = j0 + k;
-      if (j < V) {
-        const float y = S * tanhf(f[k] * invS);
-        sum += __expf(y - S);
-        if (j == c_ll) s_yc = y;
-      }
+      if (j < V) sum += __expf(S * tanhf(f[k] * invS) - S);
     }
   }
   sum = warp_sum(sum);
@@ -461,9 +460,8 @@ __global__ void softcap_ce_kernel(__nv_bfloat16* __restrict__ logits, long long 
   }
   __syncthreads();
   const float total = red[0];
-  const bool valid = c_ll >= 0 && c_ll < V;
   const float w = valid ? (row_w ? row_w[row] : 1.f) : 0.f;
-  if (tid == 0) loss_out[row] = valid ? w * (S + logf(total) - s_yc) : 0.f;
+  if (tid == 0) loss_out[row] = valid ? w * (S + logf(total) - yc) : 0.f;
   if (!write_grad) return;
   const float inv_total = 1.f / total;
   const float gs = w * scale;

@@ -1,4 +1,4 @@
-// Allocation-free AdamW entry point (C ABI).
+// Allocation-free AdamW entry point (C ABI); declarations in noalloc_adamw.h.
 //
 // This file has no counterpart in the reference implementation; it is an addition
 // for callers of this library that must not allocate device memory.
@@ -19,25 +19,34 @@
 //    with TFB_NOALLOC_TOO_MANY_TENSORS and nothing is launched.  The array costs
 //    1024 * 64 B = 64 KiB of device memory on every GPU that loads the library, held
 //    until the process exits.
-//  * The first call on a device looks up the array's device address with
-//    cudaGetSymbolAddress (with that device current) and caches it; that set-up call
-//    should happen before any stream capture begins.
+//  * Every call looks up the array's device address with cudaGetSymbolAddress, with
+//    the caller's device current (a lookup allocates nothing), so the address is
+//    never stale, e.g. after a cudaDeviceReset.
 //  * Every call shares the one array and it keeps the last call's contents.  Each call
 //    writes every table entry it reads, so nothing in the array has to start at zero.
 //    Two calls whose work overlaps on the GPU (for example on two streams) race on the
 //    table: serialize them on one stream.
-//  * No cudaMalloc, cudaFree or allocating library routine is called.  The table is
-//    staged in a host-side static buffer and copied with cudaMemcpyAsync on the
-//    caller's stream (from pageable memory, which the runtime stages before returning,
-//    so the host buffer may be rewritten by the next call).
+//  * Host threads may call concurrently: a process-wide lock covers the host staging
+//    buffer, the table copy and the launch, and the error message is kept per thread.  Their GPU
+//    work still shares the one table, so the rule above applies across threads too.
+//  * The table is copied with cudaMemcpyAsync on the caller's stream from a pageable
+//    host buffer.  The runtime stages that copy before returning, so the buffer can be
+//    reused at once, but it may first wait for the stream's earlier work: a call can
+//    block the host until the stream drains.  For the same reason a call made while
+//    the stream is being captured into a CUDA graph is not supported.
+//  * No cudaMalloc, cudaFree or allocating library routine is called.
+#include "noalloc_adamw.h"
+
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdio.h>
 #include <string.h>
+
+#include <mutex>
 
 namespace {
 
 constexpr int kNoallocMaxTensors = 1024;
-constexpr int kNoallocMaxDevices = 64;
 constexpr int kNoallocChunk = 8192;
 
 struct __align__(64) NoallocAdamEntry {
@@ -53,10 +62,11 @@ struct __align__(64) NoallocAdamEntry {
 // The scratch: the tensor table every call of the entry point writes and reads.
 static __device__ __align__(256) NoallocAdamEntry g_noalloc_adamw_table[kNoallocMaxTensors];
 
-// Host-side staging of the table (host memory; no device allocation involved).
+// Host-side staging of the table (host memory; no device allocation involved), guarded
+// by g_stage_lock from the first write until the copy has been staged by the runtime.
 static NoallocAdamEntry g_host_table[kNoallocMaxTensors];
-static NoallocAdamEntry* g_table_dev_ptr[kNoallocMaxDevices] = {nullptr};
-static char g_last_error[256] = "";
+static std::mutex g_stage_lock;
+static thread_local char g_last_error[256] = "";
 
 __device__ __forceinline__ float lerp_torch(float a, float b, float w) {
   return (fabsf(w) < 0.5f) ? a + w * (b - a) : b - (b - a) * (1.f - w);
@@ -101,21 +111,19 @@ void set_error(const char* msg) {
   g_last_error[sizeof(g_last_error) - 1] = '\0';
 }
 
+void set_cuda_error(const char* what, cudaError_t e) {
+  snprintf(g_last_error, sizeof(g_last_error), "tfb_adamw_multi_noalloc: %s: %s (%s)", what, cudaGetErrorName(e),
+           cudaGetErrorString(e));
+}
+
 }  // namespace
 
 extern "C" {
 
-enum {
-  TFB_NOALLOC_OK = 0,
-  TFB_NOALLOC_TOO_MANY_TENSORS = 1,
-  TFB_NOALLOC_BAD_ARGUMENT = 2,
-  TFB_NOALLOC_CUDA_ERROR = 3,
-};
-
 // Largest tensor count one call accepts.
 __attribute__((visibility("default"))) int tfb_adamw_noalloc_max_tensors(void) { return kNoallocMaxTensors; }
 
-// Text of the last error reported by tfb_adamw_multi_noalloc (empty after success).
+// Text of the calling thread's last error from tfb_adamw_multi_noalloc (empty after success).
 __attribute__((visibility("default"))) const char* tfb_adamw_noalloc_last_error(void) { return g_last_error; }
 
 // One AdamW step over `n_tensors` fp32 tensors, in place, on `stream`.
@@ -141,19 +149,17 @@ __attribute__((visibility("default"))) int tfb_adamw_multi_noalloc(
     return TFB_NOALLOC_TOO_MANY_TENSORS;
   }
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoallocMaxDevices) {
-    set_error("tfb_adamw_multi_noalloc: no usable current CUDA device");
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_cuda_error("cudaGetDevice", e);
     return TFB_NOALLOC_CUDA_ERROR;
   }
-  if (g_table_dev_ptr[dev] == nullptr) {
-    // Once per device, with that device current: the array's device address.
-    void* ptr = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_adamw_table);
-    if (e != cudaSuccess || ptr == nullptr) {
-      set_error("tfb_adamw_multi_noalloc: cudaGetSymbolAddress of the static table failed");
-      return TFB_NOALLOC_CUDA_ERROR;
-    }
-    g_table_dev_ptr[dev] = static_cast<NoallocAdamEntry*>(ptr);
+  // The array's device address on the current device (looked up on every call).
+  void* table_dev = nullptr;
+  e = cudaGetSymbolAddress(&table_dev, g_noalloc_adamw_table);
+  if (e != cudaSuccess || table_dev == nullptr) {
+    set_cuda_error("cudaGetSymbolAddress of the static table", e);
+    return TFB_NOALLOC_CUDA_ERROR;
   }
   long long chunks = 0;
   for (int i = 0; i < n_tensors; ++i) {
@@ -161,32 +167,41 @@ __attribute__((visibility("default"))) int tfb_adamw_multi_noalloc(
       set_error("tfb_adamw_multi_noalloc: empty tensor or null pointer in the table");
       return TFB_NOALLOC_BAD_ARGUMENT;
     }
-    g_host_table[i].p = params[i];
-    g_host_table[i].g = grads[i];
-    g_host_table[i].m = exp_avgs[i];
-    g_host_table[i].v = exp_avg_sqs[i];
-    g_host_table[i].n = numels[i];
-    g_host_table[i].chunk0 = chunks;
-    g_host_table[i].bc1 = bias1[i];
-    g_host_table[i].bc2 = bias2[i];
     chunks += (numels[i] + kNoallocChunk - 1) / kNoallocChunk;
   }
   if (chunks > 0x7fffffffLL) {
     set_error("tfb_adamw_multi_noalloc: too many elements for one launch");
     return TFB_NOALLOC_BAD_ARGUMENT;
   }
-  cudaError_t e = cudaMemcpyAsync(g_table_dev_ptr[dev], g_host_table, sizeof(NoallocAdamEntry) * n_tensors,
-                                  cudaMemcpyHostToDevice, stream);
-  if (e != cudaSuccess) {
-    set_error("tfb_adamw_multi_noalloc: table copy failed");
-    return TFB_NOALLOC_CUDA_ERROR;
+  {
+    std::lock_guard<std::mutex> lock(g_stage_lock);
+    long long c = 0;
+    for (int i = 0; i < n_tensors; ++i) {
+      g_host_table[i].p = params[i];
+      g_host_table[i].g = grads[i];
+      g_host_table[i].m = exp_avgs[i];
+      g_host_table[i].v = exp_avg_sqs[i];
+      g_host_table[i].n = numels[i];
+      g_host_table[i].chunk0 = c;
+      g_host_table[i].bc1 = bias1[i];
+      g_host_table[i].bc2 = bias2[i];
+      c += (numels[i] + kNoallocChunk - 1) / kNoallocChunk;
+    }
+    // From pageable memory: staged by the runtime before this returns.  The launch stays
+    // under the lock too, so on one stream every copy is followed by its own kernel.
+    e = cudaMemcpyAsync(table_dev, g_host_table, sizeof(NoallocAdamEntry) * n_tensors, cudaMemcpyHostToDevice,
+                        stream);
+    if (e != cudaSuccess) {
+      set_cuda_error("table copy (cudaMemcpyAsync)", e);
+      return TFB_NOALLOC_CUDA_ERROR;
+    }
+    adamw_noalloc_kernel<<<(unsigned)chunks, 256, 0, stream>>>(static_cast<const NoallocAdamEntry*>(table_dev),
+                                                               n_tensors, lr_dev, (float)(1.0 - beta1),
+                                                               (float)(1.0 - beta2), eps, weight_decay, cautious);
+    e = cudaGetLastError();
   }
-  adamw_noalloc_kernel<<<(unsigned)chunks, 256, 0, stream>>>(g_table_dev_ptr[dev], n_tensors, lr_dev,
-                                                             (float)(1.0 - beta1), (float)(1.0 - beta2),
-                                                             eps, weight_decay, cautious);
-  e = cudaGetLastError();
   if (e != cudaSuccess) {
-    set_error("tfb_adamw_multi_noalloc: kernel launch failed");
+    set_cuda_error("kernel launch", e);
     return TFB_NOALLOC_CUDA_ERROR;
   }
   return TFB_NOALLOC_OK;

@@ -27,13 +27,57 @@ def _packer(split: str, rank: int, seed: int | None = None, vocab: int = 8192):
                                       syn.rank_seed(base, rank), syn.BOS_ID, 512)
 
 
+class EpochPacker:
+    """The train split as a corpus of finite epochs (``epoch_rows`` packed rows per rank).
+
+    With ``epoch_rows == 0`` the stream is endless (one epoch).  Otherwise epoch 1 is the
+    split's seeded order, and when it is used up the next epoch begins: without shuffling
+    it replays epoch 1 exactly (the same documents in the same order, as a finite corpus
+    read twice would), with ``shuffle`` epoch ``e`` is a fresh order seeded by
+    ``shuffle_seed + e`` -- the reference's requeue packer reshuffles its row groups
+    from epoch 2 on in the same way (``train.py:106-196``, ``--epoch-shuffle``)."""
+
+    def __init__(self, split: str, rank: int, seed: int | None = None, vocab: int = 8192,
+                 epoch_rows: int = 0, shuffle: bool = False, shuffle_seed: int = 1234):
+        self.split, self.rank, self.seed, self.vocab = split, rank, seed, vocab
+        self.epoch_rows, self.shuffle, self.shuffle_seed = int(epoch_rows), bool(shuffle), int(shuffle_seed)
+        self.epoch = 1
+        self.rows_left = self.epoch_rows
+        self.packer = _packer(split, rank, seed, vocab)
+
+    def _start_next_epoch(self) -> None:
+        self.epoch += 1
+        seed = self.seed
+        if self.shuffle:
+            base = seed if seed is not None else (syn.TRAIN_SEED if self.split == "train" else syn.VAL_SEED)
+            seed = base + self.shuffle_seed + self.epoch
+        self.packer = _packer(self.split, self.rank, seed, self.vocab)
+        self.rows_left = self.epoch_rows
+
+    def fill(self, rows: torch.Tensor) -> None:
+        if self.epoch_rows <= 0:
+            self.packer.fill(rows)
+            return
+        done = 0
+        while done < rows.shape[0]:
+            if self.rows_left == 0:
+                self._start_next_epoch()
+            n = min(self.rows_left, rows.shape[0] - done)
+            self.packer.fill(rows[done:done + n])
+            done += n
+            self.rows_left -= n
+
+
 def make_dataloader(tokenizer, batch_size: int, seq_len: int, split: str,
-                    device: torch.device | str, seed: int | None = None, **_unused):
-    """BOS-aligned best-fit packed loader with the reference's yield contract."""
+                    device: torch.device | str, seed: int | None = None, epoch_tokens: int = 0,
+                    epoch_shuffle: bool = False, epoch_shuffle_seed: int = 1234, **_unused):
+    """BOS-aligned best-fit packed loader with the reference's yield contract; the third
+    item's ``epoch`` counts epochs of ``epoch_tokens`` tokens per rank (see ``EpochPacker``)."""
     assert batch_size > 0 and seq_len > 1
     _ddp, rank, _lr, _ws = get_dist_info()
     vocab = tokenizer.get_vocab_size() if tokenizer is not None else 8192
-    packer = _packer(split, rank, seed, vocab)
+    packer = EpochPacker(split, rank, seed, vocab, epoch_rows=_epoch_rows(epoch_tokens, seq_len),
+                         shuffle=epoch_shuffle, shuffle_seed=epoch_shuffle_seed)
     dev = torch.device(device)
     pin = dev.type == "cuda"
     rows = torch.empty((batch_size, seq_len + 1), dtype=torch.int32)
@@ -47,7 +91,11 @@ def make_dataloader(tokenizer, batch_size: int, seq_len: int, split: str,
         cpu_targets.copy_(rows[:, 1:])
         inputs.copy_(cpu_inputs, non_blocking=pin)
         targets.copy_(cpu_targets, non_blocking=pin)
-        yield inputs, targets, {"epoch": 1}
+        yield inputs, targets, {"epoch": packer.epoch}
+
+
+def _epoch_rows(epoch_tokens: int, seq_len: int) -> int:
+    return 0 if epoch_tokens <= 0 else max(1, epoch_tokens // (seq_len + 1))
 
 
 class PackedRowLoader:
@@ -60,12 +108,14 @@ class PackedRowLoader:
     """
 
     def __init__(self, batch_size: int, seq_len: int, device: torch.device, split: str = "train",
-                 seed: int | None = None, rank: int | None = None, vocab: int = 8192, depth: int = 2):
+                 seed: int | None = None, rank: int | None = None, vocab: int = 8192, depth: int = 2,
+                 epoch_tokens: int = 0, epoch_shuffle: bool = False, epoch_shuffle_seed: int = 1234):
         if rank is None:
             rank = get_dist_info()[1]
         self.B, self.T = batch_size, seq_len
         self.device = torch.device(device)
-        self.packer = _packer(split, rank, seed, vocab)
+        self.packer = EpochPacker(split, rank, seed, vocab, epoch_rows=_epoch_rows(epoch_tokens, seq_len),
+                                  shuffle=epoch_shuffle, shuffle_seed=epoch_shuffle_seed)
         cuda = self.device.type == "cuda"
         self.depth = depth
         self.host = [torch.empty((batch_size, seq_len + 1), dtype=torch.int32, pin_memory=cuda)
@@ -114,9 +164,14 @@ class PackedRowLoader:
     def __iter__(self):
         return self
 
+    @property
+    def epoch(self) -> int:
+        """Epoch of the most recently packed rows (one block ahead of ``next()``)."""
+        return self.packer.epoch
+
     def __next__(self):
         rows = self.next()
-        return rows[:, :-1], rows[:, 1:], {"epoch": 1}
+        return rows[:, :-1], rows[:, 1:], {"epoch": self.packer.epoch}
 
 
 def _to_dev(bx, by, dev):

@@ -191,8 +191,11 @@ class MLP(nn.Module):
         hidden = config.mlp_ratio * config.n_embd
         self.swiglu_hidden = 0
         if rc.coalesced_swiglu:
-            exact = (2.0 / 3.0) * config.mlp_ratio * config.n_embd
-            self.swiglu_hidden = max(128, int(round(exact / 128.0)) * 128)
+            if rc.coalesced_swiglu_hidden > 0:
+                self.swiglu_hidden = int(rc.coalesced_swiglu_hidden)
+            else:
+                exact = (2.0 / 3.0) * config.mlp_ratio * config.n_embd
+                self.swiglu_hidden = max(128, int(round(exact / 128.0)) * 128)
             hidden = self.swiglu_hidden
         fc_out = 2 * hidden if self.swiglu_hidden else hidden
         self.c_fc = Linear(config.n_embd, fc_out)
@@ -414,7 +417,8 @@ class GPT(nn.Module):
                                         if self.ngram_dim != config.n_embd else {})
         self.ngram_pad_id = V
         if rc.out_bigram:
-            self.out_bigram = nn.Embedding(V, V, _weight=torch.zeros(V, V))
+            self.out_bigram = nn.Embedding(V, V, _weight=torch.zeros(
+                V, V, dtype=torch.bfloat16 if rc.out_bigram_bf16 else torch.float32))
             self.out_bigram_gate = Linear(config.n_embd, 1)
             self.out_bigram_gate_bias = nn.Parameter(torch.full((1,), float(rc.out_bigram_gate_bias)))
         else:

@@ -31,7 +31,7 @@ from .eval import causality_check, evaluate_bpb
 from .models.gpt import GPT
 from .optim.muon_adamw import setup_optimizer
 from .optim.schedules import apply_schedules, batch_ramp_grad_accum
-from .parallel.ddp import grads_finite_, loss_scale_transition, unscale_grads_
+from .parallel.ddp import grads_finite_, next_loss_scale, unscale_grads_
 from .runtime import cleanup_runtime, compute_dtype_for, detect_device_type, init_runtime, print0, synchronize
 
 _PROCESS_STARTED = time.monotonic()
@@ -87,7 +87,9 @@ class Trainer:
         self.tokens_per_step = cfg.total_batch_size
         self.engine = TrainEngine(model, self.opt, cfg, self.device, self.grad_accum, cfg.grad_sync)
         self.loader = PackedRowLoader(self.rows_per_micro, cfg.seq_len, self.device, "train",
-                                      rank=rank // cfg.pp) if build_loader else None
+                                      rank=rank // cfg.pp, epoch_tokens=cfg.synthetic_epoch_tokens,
+                                      epoch_shuffle=cfg.epoch_shuffle,
+                                      epoch_shuffle_seed=cfg.epoch_shuffle_seed) if build_loader else None
         self.step_idx = 0
         self._adamw_applied_last = True   # AdamW gradients are zeroed only after they were applied
         self.loss_scale = cfg.loss_scale
@@ -194,7 +196,7 @@ class Trainer:
             ov = torch.tensor([0.0 if finite else 1.0], device=self.device)
             if dist.is_available() and dist.is_initialized():
                 dist.all_reduce(ov, op=dist.ReduceOp.MAX)
-            self.loss_scale, self.loss_scale_clean, skip = loss_scale_transition(
+            self.loss_scale, self.loss_scale_clean, skip = next_loss_scale(
                 self.loss_scale, self.loss_scale_clean, bool(ov.item() == 0.0),
                 cfg.loss_scale_growth_interval, cfg.loss_scale_max)
             if skip:
