@@ -89,3 +89,42 @@ def test_linear_decode_split_k(cuda_device, M, N, K):
     check_errors()
     ws, cnt, _split = next(iter(cache.values()))
     assert float(ws.abs().sum()) == 0.0 and int(cnt.abs().sum()) == 0
+
+
+@pytest.mark.parametrize("M", [130, 384, 640])
+def test_pair_tiles_row_tails(cuda_device, M):
+    """256-wide tiles run on CTA pairs (tcgen05 cta_group::2, 256 rows per pair): row counts
+    that leave the second CTA of the last pair partly or wholly past M."""
+    from trainium_frontier_b200.ops import gemm
+    torch.manual_seed(4)
+    N, K = 512, 320
+    x = torch.randn(M, K, device=cuda_device, dtype=torch.bfloat16)
+    w = torch.randn(N, K, device=cuda_device, dtype=torch.bfloat16) * K ** -0.5
+    _check(gemm.linear_fwd(x, w), _ref(x, w))
+    dy = torch.randn(M, N, device=cuda_device, dtype=torch.bfloat16)
+    _check(gemm.linear_dx(dy, w), dy.float() @ w.float())
+    g = torch.zeros(N, K, device=cuda_device, dtype=torch.float32)
+    gemm.linear_dw(dy, x, g, accumulate=False, split_k=1)
+    _check(g, dy.float().t() @ x.float())
+
+
+def test_pair_tiles_batched(cuda_device):
+    """Batched products of the Newton-Schulz iteration (all three operand layouts) on CTA
+    pairs, with a batch whose row count is not a multiple of 256."""
+    from trainium_frontier_b200.ops import gemm
+    from trainium_frontier_b200.ops._ext import check_errors
+    torch.manual_seed(5)
+    Bt, M, N, K = 3, 640, 512, 384
+    a = torch.randn(Bt, M, K, device=cuda_device, dtype=torch.bfloat16)
+    b = torch.randn(Bt, N, K, device=cuda_device, dtype=torch.bfloat16) * K ** -0.5
+    r = torch.randn(Bt, M, N, device=cuda_device, dtype=torch.bfloat16)
+    out = torch.empty(Bt, M, N, device=cuda_device, dtype=torch.bfloat16)
+    gemm.bmm_nt(a, b, out, residual=r, alpha=0.5, rcoef=2.0)
+    _check(out, 0.5 * (a.float() @ b.float().mT) + 2.0 * r.float())
+    bk = torch.randn(Bt, K, N, device=cuda_device, dtype=torch.bfloat16) * K ** -0.5
+    gemm.bmm_nn(a, bk, out)
+    _check(out, a.float() @ bk.float())
+    at = torch.randn(Bt, K, M, device=cuda_device, dtype=torch.bfloat16)
+    gemm.bmm_tn(at, bk, out)
+    _check(out, at.float().mT @ bk.float())
+    check_errors()

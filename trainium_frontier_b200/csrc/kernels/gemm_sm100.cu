@@ -107,12 +107,16 @@ struct GemmArgs {
   TpArgs tp;
 };
 
-template <int BN>
+// PAIR: the tile is computed by a 2-CTA cluster (tcgen05 cta_group::2): 256 rows x BN,
+// each CTA holding 128 rows of A and BN / 2 rows of B per stage, so per CTA a stage is
+// 32 KB and six fit.
+template <int BN, bool PAIR = false>
 struct GemmCfg {
   static constexpr int BM = 128, BK = 64;
-  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int BNH = PAIR ? BN / 2 : BN;  // rows of B this CTA loads per stage
+  static constexpr int STAGES = PAIR ? 6 : (BN == 256) ? 4 : 6;
   static constexpr uint32_t A_BYTES = BM * BK * 2;
-  static constexpr uint32_t B_BYTES = BN * BK * 2;
+  static constexpr uint32_t B_BYTES = BNH * BK * 2;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
   static constexpr int QSLOTS = 4;  // tile-id ring
   static constexpr size_t SMEM = 1024 + STAGES * (A_BYTES + B_BYTES) + (2 * STAGES + 5 + 2 * QSLOTS) * 8 + 64;
@@ -276,14 +280,15 @@ struct ModeThreads {
   static constexpr int value = MODE == MODE_AG ? 384 : 320;
 };
 
-template <int BN, bool A_MN, bool B_MN, int EPI, int MODE>
+template <int BN, bool A_MN, bool B_MN, int EPI, int MODE, bool PAIR = false>
 __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmD2,
                      const __grid_constant__ GemmArgs args) {
-  using C = GemmCfg<BN>;
-  constexpr int BM = C::BM, BK = C::BK, STAGES = C::STAGES, QS = C::QSLOTS;
-  constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN, A_MN, B_MN);
+  static_assert(!PAIR || (MODE == MODE_PLAIN && BN == 256), "CTA pairs: plain GEMMs with 256-wide tiles");
+  using C = GemmCfg<BN, PAIR>;
+  constexpr int BM = C::BM, BK = C::BK, STAGES = C::STAGES, QS = C::QSLOTS, BNH = C::BNH;
+  constexpr uint32_t IDESC = umma_idesc_bf16(PAIR ? 2 * BM : BM, BN, A_MN, B_MN);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -306,6 +311,10 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // CTA pair: rank 0 (the leader) issues the MMAs for both; its full[] barriers count
+  // both CTAs' TMA bytes and its tempty[] barriers both CTAs' epilogue warps.
+  const uint32_t crank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = crank == 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -314,11 +323,12 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 256);
+      mbar_init(&tempty[i], PAIR ? 16 : 256);  // pair: lane 0 of the 8 epilogue warps of each CTA
     }
     for (int i = 0; i < QS; ++i) {
       mbar_init(&qfull[i], 1);
-      mbar_init(&qempty[i], 9);  // MMA thread + one lane of each epilogue warp
+      // MMA thread (the pair's leader only) + one lane of each epilogue warp
+      mbar_init(&qempty[i], (PAIR && !leader) ? 8 : 9);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -327,11 +337,17 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, C::TMEM_COLS);  // the same warp of both CTAs
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // barrier inits visible to the peer before any remote arrive
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -345,12 +361,13 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
       bool ok = true;
       uint32_t out_valid = 0, out_parity = 0;  // per-stage: a load is in flight / its phase parity
       int ready_mb = -1;
-      int static_t = blockIdx.x;
+      int static_t = PAIR ? (int)cluster_id_x() : (int)blockIdx.x;
+      const int t_stride = PAIR ? (int)nclusters_x() : (int)gridDim.x;
       while (ok) {
         int t;
         if constexpr (MODE == MODE_PLAIN) {
           t = static_t;
-          static_t += gridDim.x;
+          static_t += t_stride;
         } else {
           t = (int)atomicAdd(args.tp.sched, 1u);
         }
@@ -368,6 +385,7 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
         if (t < 0) break;
         int mb, nb, ks, bi;
         decode_tile<MODE>(t, args, mb, nb, ks, bi);
+        if constexpr (PAIR) mb = 2 * mb + (int)crank;  // this CTA's 128-row half of the pair tile
         if constexpr (MODE == MODE_AG) {
           if (mb / (args.tp.rows_per_rank >> 7) != args.tp.rank && mb != ready_mb) {
             if (!wait_epoch<false>(args.tp.ag_done + mb, args.tp.epoch, abort_flag, args.err, ERR_TIMEOUT_PRODUCER)) {
@@ -385,11 +403,39 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
             ok = false;
             break;
           }
+          uint8_t* a_dst = sA + stage * C::A_BYTES;
+          uint8_t* b_dst = sB + stage * C::B_BYTES;
+          if constexpr (PAIR) {
+            // Each CTA loads its own halves into its own shared memory; the leader's full[]
+            // barrier counts the bytes of both.
+            if (leader) {
+              mbar_arrive_expect_tx(&full[stage], 2 * (C::A_BYTES + C::B_BYTES));
+              out_valid |= 1u << stage;
+              out_parity = (out_parity & ~(1u << stage)) | (phase << stage);
+            }
+            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+            if (!A_MN) {
+              tma_load_3d_pair(a_dst, &tmA, fb, kb * BK, mb * BM, bi);
+            } else {
+#pragma unroll
+              for (int p = 0; p < BM / 64; ++p) tma_load_3d_pair(a_dst + p * 8192, &tmA, fb, mb * BM + p * 64, kb * BK, bi);
+            }
+            const int n0 = nb * BN + (int)crank * BNH;
+            if (!B_MN) {
+              tma_load_3d_pair(b_dst, &tmB, fb, kb * BK, n0, bi);
+            } else {
+#pragma unroll
+              for (int p = 0; p < BNH / 64; ++p) tma_load_3d_pair(b_dst + p * 8192, &tmB, fb, n0 + p * 64, kb * BK, bi);
+            }
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            continue;
+          }
           mbar_arrive_expect_tx(&full[stage], C::A_BYTES + C::B_BYTES);
           out_valid |= 1u << stage;
           out_parity = (out_parity & ~(1u << stage)) | (phase << stage);
-          uint8_t* a_dst = sA + stage * C::A_BYTES;
-          uint8_t* b_dst = sB + stage * C::B_BYTES;
           if (!A_MN) {
             tma_load_3d(a_dst, &tmA, &full[stage], kb * BK, mb * BM, bi);
           } else {
@@ -410,6 +456,13 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
       }
       if (!ok) {
         *abort_flag = 1;
+        if constexpr (PAIR) {
+          // This CTA's loads complete on the leader's barriers, which it cannot wait on:
+          // give any copy still in flight a bounded moment to land before the CTA exits.
+          const unsigned long long t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 5000000ull) {
+          }
+        }
         // Drain: wait (bounded) until every load issued into a stage has landed, so no
         // bulk copy is still writing shared memory when the CTA exits.
         for (int s = 0; s < STAGES; ++s) {
@@ -423,7 +476,7 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -468,16 +521,29 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
             else adesc = umma_desc_sw128(a_addr + kk * 2048, 8192, 1024);
             if (!B_MN) bdesc = umma_desc_sw128(b_addr + kk * 32, 16, 1024);
             else bdesc = umma_desc_sw128(b_addr + kk * 2048, 8192, 1024);
-            umma_bf16(d_tmem, adesc, bdesc, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+            if constexpr (PAIR) umma_bf16_pair(d_tmem, adesc, bdesc, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+            else umma_bf16(d_tmem, adesc, bdesc, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
           }
-          umma_commit(&empty[stage]);  // stage is free once these MMAs have read it
+          // stage is free (in both CTAs of a pair) once these MMAs have read it
+          if constexpr (PAIR) {
+            umma_commit_pair(smem_u32(&empty[stage]));
+            umma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 1));
+          } else {
+            umma_commit(&empty[stage]);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&tfull[acc]);  // accumulator ready for the epilogue
+        // accumulator ready for the epilogue (of both CTAs of a pair)
+        if constexpr (PAIR) {
+          umma_commit_pair(smem_u32(&tfull[acc]));
+          umma_commit_pair(mapa_shared(smem_u32(&tfull[acc]), 1));
+        } else {
+          umma_commit(&tfull[acc]);
+        }
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
@@ -485,7 +551,8 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
       }
       if (!ok) {
         // Let every MMA already issued finish before TMEM is released.
-        umma_commit(drain);
+        if constexpr (PAIR) umma_commit_pair(smem_u32(drain));
+        else umma_commit(drain);
         const unsigned long long t0 = globaltimer_ns();
         while (!mbar_try_wait(drain, 0)) {
           if (globaltimer_ns() - t0 > 100000000ull) break;
@@ -501,6 +568,19 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
     uint32_t acc_phase = 0;
     int qs = 0;
     uint32_t qph = 0;
+    // Hand accumulator a back to the MMA issuer (after tc_fence_before): every thread of a
+    // single CTA, or lane 0 of each warp of both CTAs on the pair leader's barrier.
+    auto release_acc = [&](int a_) {
+      if constexpr (PAIR) {
+        __syncwarp();
+        if (lane == 0) {
+          if (leader) mbar_arrive(&tempty[a_]);
+          else mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[a_]), 0));
+        }
+      } else {
+        mbar_arrive(&tempty[a_]);
+      }
+    };
     while (true) {
       if (!mbar_wait_warp(&qfull[qs], qph, abort_flag, args.err, ERR_TIMEOUT_EPILOGUE)) break;
       const int t = qtile[qs];
@@ -513,6 +593,7 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
       if (t < 0) break;
       int mb, nb, ks, bi;
       decode_tile<MODE>(t, args, mb, nb, ks, bi);
+      if constexpr (PAIR) mb = 2 * mb + (int)crank;
       if (!mbar_wait_warp(&tfull[acc], acc_phase, abort_flag, args.err, ERR_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const int row = mb * BM + q * 32 + lane;
@@ -622,7 +703,7 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
           }
         }
         tc_fence_before();
-        mbar_arrive(&tempty[acc]);
+        release_acc(acc);
         if (owner != rank) {
           // This lane quarter of the tile is in the owner's receive buffer: announce it.  The
           // warp barrier orders every lane's stores before lane 0's system-scope release
@@ -665,7 +746,7 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
         if (lane == 0) bulk_wait_group<0>();
         __syncwarp();
         tc_fence_before();
-        mbar_arrive(&tempty[acc]);
+        release_acc(acc);
       } else if (EPI != EPI_F32 && args.tma_store) {
         // ---- bf16 outputs through TMA stores: each warp stages its 32 rows x 64 columns
         // (128-byte swizzle) and one lane stores the slab, so global writes are whole lines
@@ -839,7 +920,7 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
         if (lane == 0) bulk_wait_group<0>();
         __syncwarp();
         tc_fence_before();
-        mbar_arrive(&tempty[acc]);
+        release_acc(acc);
       } else {
         const bool row_ok = row < args.M;
 #pragma unroll 1
@@ -967,7 +1048,7 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
       }
 
         tc_fence_before();
-        mbar_arrive(&tempty[acc]);
+        release_acc(acc);
         if constexpr (EPI == EPI_F32) {
           if (args.fin_out != nullptr) split_finish<BN>(args, mb, nb, bi, q, hf, warp, lane);
         }
@@ -1045,10 +1126,14 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  // A pair's CTAs read each other's shared memory and arrive on each other's barriers:
+  // neither may exit (or free TMEM) before both are done.
+  if constexpr (PAIR) cluster_sync();
+  else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+    else tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
   if constexpr (MODE != MODE_PLAIN) {
     if (threadIdx.x == 0) {
@@ -1148,28 +1233,57 @@ int num_sms(int dev) {
   return cache[dev];
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, int MODE = MODE_PLAIN>
+template <int BN, bool A_MN, bool B_MN, int EPI, int MODE = MODE_PLAIN, bool PAIR = false>
 static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const CUtensorMap& td2,
                         const GemmArgs& a, int grid, cudaStream_t stream) {
-  using C = GemmCfg<BN>;
-  auto kern = gemm_bf16_kernel<BN, A_MN, B_MN, EPI, MODE>;
+  using C = GemmCfg<BN, PAIR>;
+  auto kern = gemm_bf16_kernel<BN, A_MN, B_MN, EPI, MODE, PAIR>;
   // every epilogue stages through the same per-warp tiles (TMA stores / reduce-adds, the
   // TP reduce-scatter)
   constexpr size_t smem = C::SMEM_ALL;
+  static_assert(smem <= 232448, "dynamic shared memory above the 227 KB per-CTA limit");
   static bool attr_set = false;  // one per instantiation
+  static int max_clusters = 0;
   if (!attr_set) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr_set = true;
+  }
+  if constexpr (PAIR) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(ModeThreads<MODE>::value, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (max_clusters == 0) {
+      // Persistent grid: as many pairs as can be resident at once (GPCs need not hold an
+      // even number of free SMs, so this can be below SMs / 2).
+      cfg.gridDim = dim3(2 * 74, 1, 1);
+      int n = 0;
+      C10_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+      max_clusters = n > 0 ? n : 1;
+    }
+    const int pairs = std::max(1, std::min(a.num_tiles, max_clusters));
+    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, td, td2, a));
+    (void)grid;
+    return;
   }
   kern<<<grid, ModeThreads<MODE>::value, smem, stream>>>(ta, tb, td, td2, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-template <int BN>
+template <int BN, bool PAIR = false>
 static void dispatch(bool a_mn, bool b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
                      const CUtensorMap& td, const CUtensorMap& td2, const GemmArgs& a, int grid, cudaStream_t s) {
 #define TFB_CASE(AM, BM_, E) \
-  if (a_mn == AM && b_mn == BM_ && epi == E) return launch_gemm<BN, AM, BM_, E>(ta, tb, td, td2, a, grid, s);
+  if (a_mn == AM && b_mn == BM_ && epi == E) \
+    return launch_gemm<BN, AM, BM_, E, MODE_PLAIN, PAIR>(ta, tb, td, td2, a, grid, s);
   TFB_CASE(false, false, EPI_BF16)
   TFB_CASE(false, false, EPI_RELU2)
   TFB_CASE(false, false, EPI_F32)
@@ -1252,13 +1366,19 @@ static void gemm_bf16_impl(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_m
   TORCH_CHECK(bn == 128 || bn == 256, "bn must be 128 or 256");
   c10::cuda::CUDAGuard guard(A.device());
   const int BM = 128, BK = 64;
+  // 256-wide tiles over more than one 128-row block run on CTA pairs (tcgen05 cta_group::2:
+  // 256 x 256 per pair, each CTA loading half of B), which halves the shared-memory /
+  // L2 traffic of B per MMA; TFB_GEMM_PAIR=0 keeps one CTA per 128 x 256 tile.
+  static const bool pair_on = getenv("TFB_GEMM_PAIR") == nullptr || getenv("TFB_GEMM_PAIR")[0] != '0';
+  const bool pair = pair_on && bn == 256 && M > BM;
+  const uint32_t b_rows = pair ? (uint32_t)bn / 2 : (uint32_t)bn;
   CUtensorMap ta = !a_mn ? make_tmap_bf16(A.data_ptr(), K, M, A.stride(0), 64, BM, nb, a_bs)
                          : make_tmap_bf16(A.data_ptr(), M, K, A.stride(0), 64, 64, nb, a_bs);
-  CUtensorMap tb = !b_mn ? make_tmap_bf16(B.data_ptr(), K, N, B.stride(0), 64, (uint32_t)bn, nb, b_bs)
+  CUtensorMap tb = !b_mn ? make_tmap_bf16(B.data_ptr(), K, N, B.stride(0), 64, b_rows, nb, b_bs)
                          : make_tmap_bf16(B.data_ptr(), N, K, B.stride(0), 64, 64, nb, b_bs);
   GemmArgs a{};
   a.M = (int)M; a.N = (int)N; a.K = (int)K;
-  a.tiles_m = (int)((M + BM - 1) / BM);
+  a.tiles_m = (int)((M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM));
   a.tiles_n = (int)((N + bn - 1) / bn);
   a.kb_total = (int)((K + BK - 1) / BK);
   int sk = (int)std::max<int64_t>(1, std::min<int64_t>(split_k, a.kb_total));
@@ -1307,7 +1427,8 @@ static void gemm_bf16_impl(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_m
                 "RoPE epilogue: 2-D K-major operands, bf16 TMA-store output, 256-wide tiles, no residual");
   const int grid = std::min(a.num_tiles, num_sms(A.get_device()));
   cudaStream_t s = at::cuda::getCurrentCUDAStream();
-  if (bn == 256) dispatch<256>(a_mn, b_mn, (int)epi, ta, tb, td, td2, a, grid, s);
+  if (pair) dispatch<256, true>(a_mn, b_mn, (int)epi, ta, tb, td, td2, a, grid, s);
+  else if (bn == 256) dispatch<256>(a_mn, b_mn, (int)epi, ta, tb, td, td2, a, grid, s);
   else dispatch<128>(a_mn, b_mn, (int)epi, ta, tb, td, td2, a, grid, s);
 }
 

@@ -108,10 +108,18 @@ def bench_attention(dev, peaks, B=16, T=2048, H=10, D=128):
     fl_fwd = 4.0 * B * H * T * T * D / 2
     t_f = t.time(lambda: flash_fwd(q, k, v, B, T, H, D, D ** -0.5, True))
     t_b = t.time(lambda: flash_bwd(q, k, v, o, do, lse, B, T, H, D, D ** -0.5, True))
-    qs, ks, vs = (x.view(B, T, H, D).transpose(1, 2) for x in (q, k, v))
-    t_ref = t.time(lambda: torch.nn.functional.scaled_dot_product_attention(qs, ks, vs, is_causal=True))
-    rows = [dict(name="flash fwd", ms=t_f, tflops=fl_fwd / t_f / 1e9, torch_sdpa_ms=t_ref),
-            dict(name="flash bwd", ms=t_b, tflops=2.5 * fl_fwd / t_b / 1e9)]
+    qs, ks, vs = (x.view(B, T, H, D).transpose(1, 2).detach().requires_grad_(True) for x in (q, k, v))
+    dos = do.view(B, T, H, D).transpose(1, 2)
+    sdpa = torch.nn.functional.scaled_dot_product_attention
+    with torch.no_grad():
+        t_ref = t.time(lambda: sdpa(qs, ks, vs, is_causal=True))
+    # the library's backward alone: forward once, then time autograd.grad over the saved graph
+    o_ref = sdpa(qs, ks, vs, is_causal=True)
+    t_ref_b = t.time(lambda: torch.autograd.grad(o_ref, (qs, ks, vs), dos, retain_graph=True))
+    rows = [dict(name="flash fwd", ms=t_f, tflops=fl_fwd / t_f / 1e9, torch_sdpa_ms=t_ref,
+                 torch_sdpa_tflops=fl_fwd / t_ref / 1e9),
+            dict(name="flash bwd", ms=t_b, tflops=2.5 * fl_fwd / t_b / 1e9, torch_sdpa_ms=t_ref_b,
+                 torch_sdpa_tflops=2.5 * fl_fwd / t_ref_b / 1e9)]
     for r in rows:
         r["frac_of_measured"] = r["tflops"] / peaks["bf16_tflops"]
     return rows
@@ -168,7 +176,7 @@ def main():
         out["attention"] = bench_attention(dev, peaks)
         for r in out["attention"]:
             print(f"{r['name']:>20s}  {r['ms']:8.3f} ms  {r['tflops']:7.1f} TF/s ({r['frac_of_measured']:.2f} of "
-                  f"{peaks['source']})" + (f"   torch sdpa fwd {r['torch_sdpa_ms']:.3f} ms" if 'torch_sdpa_ms' in r else ""))
+                  f"{peaks['source']})   torch sdpa {r['torch_sdpa_ms']:.3f} ms {r['torch_sdpa_tflops']:7.1f} TF/s")
     from ..ops._ext import check_errors
     check_errors(dev)
     if args.json:
