@@ -312,3 +312,50 @@ def test_model_cpu_vs_gpu(cuda_device):
     scale = max(abs(b) for _, _, b in lam)
     for n, a, b in lam:
         assert abs(a - b) < 0.15 * scale, (n, a, b, scale)
+
+
+@pytest.mark.parametrize("K", [2, 4])
+def test_causal_conv(cuda_device, K):
+    """Depthwise causal conv1d kernel (forward, dx, deterministic dw) against the fp32
+    conv1d of the same bf16-rounded inputs and weight."""
+    from trainium_frontier_b200 import ops
+    from trainium_frontier_b200.ops import reference as ref
+    torch.manual_seed(6)
+    B, T, C = 3, 300, 1280
+    x = torch.randn(B, T, C, device=cuda_device).to(BF)
+    w = (torch.randn(C, 1, K, device=cuda_device) * 0.3).requires_grad_(True)
+    g = torch.randn(B, T, C, device=cuda_device).to(BF)
+    xb = x.clone().requires_grad_(True)
+    y = ops.causal_conv(xb, w)
+    y.backward(g)
+    xr = x.float().requires_grad_(True)
+    wr = w.detach().to(BF).float().requires_grad_(True)
+    yr = ref.causal_conv(xr, wr)
+    yr.backward(g.float())
+    assert rel(y, yr) < 1e-2
+    assert rel(xb.grad, xr.grad) < 1e-2
+    assert rel(w.grad, wr.grad) < 1e-3
+    dw1 = w.grad.clone()
+    w.grad = None
+    ops.causal_conv(x.clone().requires_grad_(True), w).backward(g)
+    assert torch.equal(w.grad, dw1)  # the weight gradient is bitwise reproducible
+
+
+@pytest.mark.parametrize("order", [2, 3])
+def test_ngram_lookup(cuda_device, order):
+    """Fused n-gram hash + gather against the reference hash and indexing; the backward's
+    scatter-add against index_add into an fp32 table gradient."""
+    from trainium_frontier_b200 import ops
+    from trainium_frontier_b200.ops import reference as ref
+    torch.manual_seed(7)
+    B, T, V, rows, Dn = 4, 512, 8192, 65521, 128
+    idx = torch.randint(0, V, (B, T), device=cuda_device, dtype=torch.int32)
+    table = torch.randn(rows, Dn, device=cuda_device).requires_grad_(True)
+    primes = (31033, 53087, 71023)[:order]
+    out = ops.ngram_lookup(idx, table, order, primes, rows, V, BF)
+    rid = ref.ngram_rows(idx, order, primes, rows, V)
+    assert torch.equal(out, table.detach()[rid].to(BF))
+    g = torch.randn(B, T, Dn, device=cuda_device).to(BF)
+    out.backward(g)
+    gr = torch.zeros(rows, Dn, device=cuda_device).index_add_(0, rid.reshape(-1), g.reshape(-1, Dn).float())
+    assert rel(table.grad, gr) < 1e-5

@@ -27,6 +27,12 @@ void mix_norm_bwd(torch::Tensor dxm, torch::Tensor dh, torch::Tensor x, torch::T
 void embed_norm_fwd(torch::Tensor idx, torch::Tensor wte, torch::Tensor out, torch::Tensor rstd);
 void embed_norm_bwd(torch::Tensor idx, torch::Tensor wte, torch::Tensor rstd, c10::optional<torch::Tensor> gacc,
                     c10::optional<torch::Tensor> gb, torch::Tensor dwte);
+void causal_conv_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor y);
+void causal_conv_bwd(torch::Tensor x, torch::Tensor w, torch::Tensor dy, torch::Tensor dx, torch::Tensor dw,
+                     torch::Tensor part, bool accumulate);
+void ngram_gather(torch::Tensor idx, int64_t order, int64_t p1, int64_t p2, int64_t p3, int64_t mod, int64_t pad,
+                  torch::Tensor table, torch::Tensor out, torch::Tensor rows);
+void ngram_scatter(torch::Tensor rows, torch::Tensor dout, torch::Tensor grad);
 void rope_norm_fwd(torch::Tensor buf, int64_t head0, int64_t nheads, int64_t D, torch::Tensor cos,
                    torch::Tensor sin, int64_t T, int64_t pos_offset, c10::optional<torch::Tensor> rstd,
                    c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> pos_t);
@@ -91,6 +97,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_rs", &tfb::symm_rs);
   m.def("muon_pre", &tfb::muon_pre);
   m.def("symm_ag_apply", &tfb::symm_ag_apply);
+  m.def("causal_conv_fwd", &tfb::causal_conv_fwd, "causal depthwise conv1d forward (bf16)");
+  m.def("causal_conv_bwd", &tfb::causal_conv_bwd, "causal depthwise conv1d backward (dx, deterministic dw)");
+  m.def("ngram_gather", &tfb::ngram_gather, "hashed n-gram row ids + gather (bf16 out)");
+  m.def("ngram_scatter", &tfb::ngram_scatter, "n-gram table gradient scatter-add (fp32)");
   m.def("fa_fwd", &tfb::fa_fwd, "tcgen05 causal flash attention forward");
   m.def("fa_bwd", &tfb::fa_bwd, "tcgen05 causal flash attention backward");
 }

@@ -57,8 +57,7 @@ class CausalConv(nn.Module):
         self.weight = nn.Parameter(torch.zeros(channels, 1, kernel))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:  # [B, T, C]
-        xt = F.pad(x.transpose(1, 2), (self.kernel - 1, 0))
-        return F.conv1d(xt, self.weight.to(x.dtype), groups=x.shape[-1]).transpose(1, 2)
+        return ops.causal_conv(x, self.weight)
 
 
 def causal_shift_1(x: torch.Tensor) -> torch.Tensor:
@@ -566,8 +565,17 @@ class GPT(nn.Module):
             out[key] = (hsh % self.ngram_mod)
         return out
 
-    def _ngram_lookup(self, key: str, ids: torch.Tensor, dtype: torch.dtype, raw: dict | None = None) -> torch.Tensor:
-        rows = self.ngram_embeds[key].weight[ids].to(dtype)
+    def _ngram_lookup(self, key: str, ids: torch.Tensor, dtype: torch.dtype, raw: dict | None = None,
+                      idx: torch.Tensor | None = None) -> torch.Tensor:
+        table = self.ngram_embeds[key].weight
+        if idx is not None and table.is_cuda:
+            # hash + gather in one kernel (the ids computed above are the same rows)
+            order = 2 if key[0] == "b" else 3
+            p = _ngram_primes(int(key[1:]))
+            rows = ops.ngram_lookup(idx, table, order, p[:2] if order == 2 else p, self.ngram_mod,
+                                    self.ngram_pad_id, dtype)
+        else:
+            rows = table[ids].to(dtype)
         if raw is not None:
             raw[key] = rows   # pre-projection rows, what a shared Engram memory reads
         if key in self.ngram_proj:
@@ -621,9 +629,9 @@ class GPT(nn.Module):
             ve_bi = ve_tri = None
             if ngram_idx is not None:
                 if f"b{i}" in self.ngram_embeds:
-                    ve_bi = self._ngram_lookup(f"b{i}", ngram_idx[f"b{i}"], dt, engram_raw)
+                    ve_bi = self._ngram_lookup(f"b{i}", ngram_idx[f"b{i}"], dt, engram_raw, idx)
                 if f"t{i}" in self.ngram_embeds:
-                    ve_tri = self._ngram_lookup(f"t{i}", ngram_idx[f"t{i}"], dt, engram_raw)
+                    ve_tri = self._ngram_lookup(f"t{i}", ngram_idx[f"t{i}"], dt, engram_raw, idx)
             if doc_mask is None and not self.layer_is_short[i]:
                 attn_mask = None
             else:

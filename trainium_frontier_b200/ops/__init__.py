@@ -125,6 +125,26 @@ def qkv_attention(x: torch.Tensor, ws: list[torch.Tensor], cos, sin, n_head: int
     return attention_qkv(linear_multi(x, ws), cos, sin, n_head, head_dim, scale)
 
 
+def causal_conv(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """Depthwise causal conv1d over time: x [B, T, C], w [C, 1, K]."""
+    if _cuda(x) and x.dtype == torch.bfloat16 and w.dtype == torch.float32 and x.shape[-1] % 8 == 0 \
+            and w.shape[-1] <= 8:
+        from .fused import CausalConvFn
+        return CausalConvFn.apply(x, w)
+    return ref.causal_conv(x, w)
+
+
+def ngram_lookup(idx: torch.Tensor, table: torch.Tensor, order: int, primes, mod: int, pad: int,
+                 dtype: torch.dtype) -> torch.Tensor:
+    """Rows of a hashed n-gram table for every position of idx [B, T] (see
+    ``reference.ngram_rows``), cast to ``dtype``: [B, T, Dn].  On CUDA the hash and the
+    gather are one kernel and the backward scatters into the fp32 table gradient."""
+    if _cuda(table) and table.dtype == torch.float32 and dtype == torch.bfloat16 and table.shape[1] % 4 == 0:
+        from .fused import NgramLookupFn
+        return NgramLookupFn.apply(idx, table, int(order), tuple(int(p) for p in primes), int(mod), int(pad))
+    return table[ref.ngram_rows(idx, order, primes, mod, pad)].to(dtype)
+
+
 def lm_head_softcap_ce(x, w_lm, targets, softcap: float, vocab: int, reduction: str = "mean",
                        row_weight=None):
     """Fused lm_head GEMM + softcap + cross-entropy (+ its backward)."""

@@ -443,3 +443,54 @@ def softcap_ce_rows(x, w, targets, softcap: float, vocab: int) -> torch.Tensor:
     tg = targets if targets.dim() == 2 else targets.view(1, -1)
     C().softcap_ce(logits, tg.contiguous(), tg.shape[1], None, vocab, float(softcap), 1.0, loss_rows, False)
     return loss_rows.view(targets.shape)
+
+
+# --------------------------------------------------------------------------- conv / n-gram
+class CausalConvFn(Function):
+    """Depthwise causal conv1d (x bf16 [B, T, C], w fp32 [C, 1, K]); the weight gradient is
+    reduced deterministically and added straight into ``w``'s fp32 gradient buffer."""
+
+    @staticmethod
+    def forward(ctx, x, w):
+        xc = x.contiguous()
+        y = torch.empty_like(xc)
+        C().causal_conv_fwd(xc, w.detach(), y)
+        ctx.save_for_backward(xc)
+        ctx.w = w
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        (xc,) = ctx.saved_tensors
+        w = ctx.w
+        B, T, Cc = xc.shape
+        K = w.shape[-1]
+        dx = torch.empty_like(xc)
+        runs = B * ((T + 63) // 64)
+        part = torch.empty(runs * Cc * K, dtype=torch.float32, device=xc.device)
+        C().causal_conv_bwd(xc, w.detach(), dy.contiguous(), dx, grad_buf(w).view(-1), part, True)
+        return dx, None
+
+
+class NgramLookupFn(Function):
+    """Hashed n-gram row ids computed and the fp32 rows gathered (bf16 out) in one kernel;
+    the backward adds every position's gradient row into the table's fp32 gradient."""
+
+    @staticmethod
+    def forward(ctx, idx, table, order, primes, mod, pad):
+        B, T = idx.shape
+        Dn = table.shape[1]
+        idx32 = idx.to(torch.int32).contiguous()
+        out = torch.empty((B, T, Dn), dtype=BF16, device=table.device)
+        rows = torch.empty((B, T), dtype=torch.int32, device=table.device)
+        p = tuple(primes) + (0,) * (3 - len(primes))
+        C().ngram_gather(idx32, order, p[0], p[1], p[2], mod, pad, table.detach(), out, rows)
+        ctx.save_for_backward(rows)
+        ctx.table = table
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        (rows,) = ctx.saved_tensors
+        C().ngram_scatter(rows, dout.contiguous(), grad_buf(ctx.table))
+        return None, None, None, None, None, None

@@ -63,6 +63,28 @@ def attention(q, k, v, causal: bool = True, scale: float | None = None, attn_mas
     return y.transpose(1, 2)
 
 
+def causal_conv(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """Depthwise causal conv1d over time of x [B, T, C] with w [C, 1, K] (K-1 zeros of left
+    padding, the weight cast to x's dtype), train.py:1316-1329."""
+    k = w.shape[-1]
+    xt = F.pad(x.transpose(1, 2), (k - 1, 0))
+    return F.conv1d(xt, w.to(x.dtype), groups=x.shape[-1]).transpose(1, 2)
+
+
+def ngram_rows(idx: torch.Tensor, order: int, primes, mod: int, pad: int) -> torch.Tensor:
+    """Hashed n-gram table rows of every position (train.py:3087-3140): the token and its
+    one (bigram) or two (trigram) predecessors, each times a layer prime, XORed, modulo
+    the table's prime row count; a missing predecessor is the pad id."""
+    cur = idx.long()
+    prev = F.pad(cur[:, :-1], (1, 0), value=pad)
+    if order == 2:
+        h = (prev * primes[0]) ^ (cur * primes[1])
+    else:
+        prev2 = F.pad(cur[:, :-2], (2, 0), value=pad)
+        h = (prev2 * primes[0]) ^ (prev * primes[1]) ^ (cur * primes[2])
+    return h % mod
+
+
 def softcap_logits(x, w_lm, softcap: float, vocab_size: int):
     logits = F.linear(x, w_lm.to(x.dtype))[..., :vocab_size].float()
     return softcap * torch.tanh(logits / softcap)
