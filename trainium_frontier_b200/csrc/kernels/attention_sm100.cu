@@ -65,6 +65,22 @@ struct FaCfg {
   static constexpr size_t BWD_SMEM = 1024 + TILE * 4 + PTILE * 2 + 2 * 128 * 4 + 20 * 8 + 16;
 };
 
+// Grid order of the two-tile forward and pipelined backward: work items (head, tile) are
+// taken in groups of G heads with G * tiles ~ 128 CTAs, heaviest tiles first inside a
+// group and heads fastest.  The CTAs resident at any time then cover a few heads whole,
+// so each K / V (forward) or Q / dO (backward) tile is read from HBM once and served to
+// that head's other CTAs from L2, instead of every CTA streaming its own head.
+__device__ __forceinline__ void grouped_item(int idx, int BH, int tiles, bool heavy_high, int& bh, int& tile) {
+  const int G = max(1, 128 / tiles);
+  const int group = idx / (G * tiles);
+  const int g0 = group * G;
+  const int gsz = min(G, BH - g0);
+  const int r = idx - group * G * tiles;
+  const int t = r / gsz;
+  bh = g0 + r % gsz;
+  tile = heavy_high ? tiles - 1 - t : t;
+}
+
 // K-major operand tile with K = 128 elements (two 64-element panels): k-step kk of 16.
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t base, int kk) {
   return umma_desc_sw128(base + (uint32_t)(kk >> 2) * kPanel + (uint32_t)(kk & 3) * 32u, 16, 1024);
@@ -327,20 +343,54 @@ __global__ void __launch_bounds__(192, 1)
 // One CTA per (batch*head, pair of 128-query tiles), heaviest pairs first.  The two tiles
 // share every K/V tile load and ping-pong on the tensor core: while softmax warpgroup 0
 // turns S0 = Q0 K_j^T into P0, the MMA warp runs S1 / P1 V for tile 1, and vice versa.
-//   warp 0      TMA: Q0 + Q1 once, then K_0, V_0, K_1, V_1, ... through a 3-slot ring
+//   warp 0      TMA: Q0 + Q1 once, then K_0, V_0, K_1, V_1, ... through a 4-slot ring, so
+//               each K / V load has more than a full step of lead before its MMA
 //   warp 1      MMA: S0(j+1), P0 V(j), S1(j+1), P1 V(j) per step j
 //   warps 2-5   softmax of tile 0 (one query row per thread = TMEM lane)
 //   warps 6-9   softmax of tile 1
+// The two groups write P into ONE shared-memory tile in turn (P0(j), P1(j), P0(j+1), ...):
+// each waits for the P V MMA of the other tile's previous turn, which the ping-pong order
+// has already issued, and the 32 KB saved go to the K / V ring.
 // TMEM: S0 | S1 | O0 | O1 (4 x 128 columns).  The row max used as the exponent reference
 // only moves when it grows by more than 8 (log2 units), so O is rarely rescaled; p values
-// stay below 2^8.  exp2 is one FFMA feeding ex2.approx.ftz.
+// stay below 2^8.  Softmax math runs on packed fp32 pairs (fma / add .f32x2) with a
+// three-input max; a quarter of the exponentials is computed on the FMA pipe
+// (exp2_poly) so the MUFU unit, whose 16 results per clock per SM match the tensor core's
+// 16 score elements per clock at head_dim 128, is not the limit.
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 
-constexpr size_t kFwd2Smem = 1024 + 2 * 32768 + 3 * 32768 + 2 * 32768 + 24 * 8 + 16;
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^v on the FMA pipe for v <= 8 (0 below -126): v = n + f with n the nearest integer
+// (added and subtracted 1.5 * 2^23, whose low mantissa bits then hold n) and f in
+// [-1/2, 1/2]; 2^f from a degree-3 polynomial fitted here for relative error on that
+// interval (max relative error 7.5e-5, far below the bf16 rounding of P); 2^n added
+// into the exponent field as n << 23, which is the magic sum's bits shifted by 23.
+// Clamping v at -126 keeps that exponent field from underflowing.
+__device__ __forceinline__ float2 exp2_poly2(float2 v) {
+  const float2 vc = make_float2(fmaxf(v.x, -126.f), fmaxf(v.y, -126.f));
+  const float2 t = __fadd2_rn(vc, make_float2(12582912.f, 12582912.f));
+  const float2 n = __fadd2_rn(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = __fadd2_rn(vc, make_float2(-n.x, -n.y));
+  float2 p = __ffma2_rn(make_float2(0.055170949548482895f, 0.055170949548482895f), f,
+                        make_float2(0.2426096349954605f, 0.2426096349954605f));
+  p = __ffma2_rn(p, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
+  p = __ffma2_rn(p, f, make_float2(0.9999281764030457f, 0.9999281764030457f));
+  const float rx = __int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23));
+  const float ry = __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23));
+  return make_float2(v.x < -126.f ? 0.f : rx, v.y < -126.f ? 0.f : ry);
+}
+
+constexpr int kFwd2Slots = 4;  // K / V ring depth
+constexpr size_t kFwd2Smem = 1024 + 2 * 32768 + kFwd2Slots * 32768 + 32768 + 24 * 8 + 16;
 
 __global__ void __launch_bounds__(320, 1)
     fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -352,26 +402,27 @@ __global__ void __launch_bounds__(320, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int NS = kFwd2Slots;
   uint8_t* sQ = smem;                 // [2] tiles
-  uint8_t* sKV = sQ + 2 * TILE;       // [3] slots
-  uint8_t* sP = sKV + 3 * TILE;       // [2] tiles
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * TILE);
+  uint8_t* sKV = sQ + 2 * TILE;       // [NS] slots
+  uint8_t* sP = sKV + NS * TILE;      // one tile, used by the two softmax groups in turn
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + TILE);
   uint64_t* bar_q = bars + 0;
-  uint64_t* kv_full = bars + 1;    // [3]
-  uint64_t* kv_empty = bars + 4;   // [3]
-  uint64_t* s_full = bars + 7;     // [2]
-  uint64_t* s_free = bars + 9;     // [2]
-  uint64_t* p_full = bars + 11;    // [2]
-  uint64_t* pv_done = bars + 13;   // [2]
-  uint64_t* drain = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* kv_full = bars + 1;          // [NS]
+  uint64_t* kv_empty = bars + 1 + NS;    // [NS]
+  uint64_t* s_full = bars + 1 + 2 * NS;  // [2]
+  uint64_t* s_free = s_full + 2;         // [2]
+  uint64_t* p_full = s_free + 2;         // [2]
+  uint64_t* pv_done = p_full + 2;        // [2]
+  uint64_t* drain = pv_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int BH = a.B * a.H;
   const int n_pairs = a.n_tiles >> 1;
-  const int pc = n_pairs - 1 - (int)(blockIdx.x / BH);
-  const int bh = (int)(blockIdx.x % BH);
+  int pc, bh;
+  grouped_item((int)blockIdx.x, BH, n_pairs, true, bh, pc);
   const int b = bh / a.H, h = bh % a.H;
   const int qt0 = 2 * pc;
   const int row0 = b * a.T + qt0 * 128;
@@ -380,7 +431,7 @@ __global__ void __launch_bounds__(320, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q, 1);
-    for (int i = 0; i < 3; ++i) {
+    for (int i = 0; i < NS; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
@@ -419,21 +470,21 @@ __global__ void __launch_bounds__(320, 1)
           tma_load_3d(sQ + t * TILE + p * kPanel, &tmQ, bar_q, h * D + p * 64, row0 + t * 128, 0);
       const int items = 2 * n1;
       for (int i = 0; i < items && ok; ++i) {
-        const int slot = i % 3;
-        if (i >= 3 && !mbar_wait(&kv_empty[slot], ((i / 3) + 1) & 1, abort_flag, a.err, ERR_TIMEOUT_PRODUCER)) {
+        const int slot = i % NS;
+        if (i >= NS && !mbar_wait(&kv_empty[slot], ((i / NS) + 1) & 1, abort_flag, a.err, ERR_TIMEOUT_PRODUCER)) {
           ok = false;
           break;
         }
         mbar_arrive_expect_tx(&kv_full[slot], TILE);
         out_valid |= 1u << slot;
-        out_parity = (out_parity & ~(1u << slot)) | ((uint32_t)((i / 3) & 1) << slot);
+        out_parity = (out_parity & ~(1u << slot)) | ((uint32_t)((i / NS) & 1) << slot);
         const int krow = b * a.T + (i >> 1) * 128;
         const CUtensorMap* map = (i & 1) ? &tmV : &tmK;
 #pragma unroll
         for (int p = 0; p < 2; ++p) tma_load_3d(sKV + slot * TILE + p * kPanel, map, &kv_full[slot], h * D + p * 64, krow, 0);
       }
       if (!ok) {
-        for (int s = 0; s < 3; ++s) {
+        for (int s = 0; s < NS; ++s) {
           if (!((out_valid >> s) & 1u)) continue;
           const unsigned long long t0 = globaltimer_ns();
           while (!mbar_try_wait(&kv_full[s], (out_parity >> s) & 1u))
@@ -449,15 +500,15 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0) {
       bool ok = mbar_wait(bar_q, 0, abort_flag, a.err, ERR_TIMEOUT_MMA);
       const uint32_t q_addr[2] = {smem_u32(sQ), smem_u32(sQ + TILE)};
-      const uint32_t p_addr[2] = {smem_u32(sP), smem_u32(sP + TILE)};
+      const uint32_t p_addr[2] = {smem_u32(sP), smem_u32(sP)};
       auto kv_wait = [&](int item) -> bool {
-        return mbar_wait(&kv_full[item % 3], (item / 3) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA);
+        return mbar_wait(&kv_full[item % NS], (item / NS) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA);
       };
       auto issue_s = [&](int t, int j) -> bool {
         if (!kv_wait(2 * j)) return false;
         if (j >= 1 && !mbar_wait(&s_free[t], (j - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) return false;
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(sKV + ((2 * j) % 3) * TILE);
+        const uint32_t k_addr = smem_u32(sKV + ((2 * j) % NS) * TILE);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
           umma_bf16(tmem + t * 128, desc_kmajor(q_addr[t], kk), desc_kmajor(k_addr, kk), IDESC_S, kk > 0 ? 1u : 0u);
@@ -468,7 +519,7 @@ __global__ void __launch_bounds__(320, 1)
         if (!kv_wait(2 * j + 1)) return false;
         if (!mbar_wait(&p_full[t], j & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) return false;
         tc_fence_after();
-        const uint32_t v_addr = smem_u32(sKV + ((2 * j + 1) % 3) * TILE);
+        const uint32_t v_addr = smem_u32(sKV + ((2 * j + 1) % NS) * TILE);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           umma_bf16(tmem + 256 + t * 128, desc_kmajor(p_addr[t], kk), desc_mnmajor(v_addr, kk), IDESC_O,
@@ -483,10 +534,10 @@ __global__ void __launch_bounds__(320, 1)
         if (j < n0 && !issue_pv(0, j)) { ok = false; break; }
         if (j + 1 < n1) {
           if (!issue_s(1, j + 1)) { ok = false; break; }
-          umma_commit(&kv_empty[(2 * (j + 1)) % 3]);  // K_{j+1} done
+          umma_commit(&kv_empty[(2 * (j + 1)) % NS]);  // K_{j+1} done
         }
         if (!issue_pv(1, j)) { ok = false; break; }
-        umma_commit(&kv_empty[(2 * j + 1) % 3]);      // V_j done
+        umma_commit(&kv_empty[(2 * j + 1) % NS]);      // V_j done
       }
       if (!ok) {
         *abort_flag = 1;
@@ -503,7 +554,6 @@ __global__ void __launch_bounds__(320, 1)
     const int r = q4 * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     const uint32_t tS = tmem + t * 128, tO = tmem + 256 + t * 128;
-    uint8_t* myP = sP + t * TILE;
     const int n_t = t == 0 ? n0 : n1;
     const int qt = qt0 + t;
     const float c = a.scale_log2;
@@ -529,35 +579,43 @@ __global__ void __launch_bounds__(320, 1)
         for (int i = 0; i < 128; ++i)
           if (i > r) x[i] = -INFINITY;
       }
-      // eight independent max / sum chains (a single 128-long chain is latency-bound)
-      float mx8[8];
+      // four independent max chains, two new elements per three-input max
+      float mx4[4] = {x[0], x[1], x[2], x[3]};
 #pragma unroll
-      for (int k = 0; k < 8; ++k) mx8[k] = x[k];
+      for (int i = 4; i < 128; i += 8)
 #pragma unroll
-      for (int i = 8; i < 128; i += 8)
-#pragma unroll
-        for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(mx8[k], x[i + k]);
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-      const float mxs = mx * c;
+        for (int k = 0; k < 4; ++k) mx4[k] = max3f(mx4[k], x[i + k], x[i + 4 + k]);
+      const float mxs = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * c;
       float alpha = 1.f;
       const bool grow = mxs > m_run + 8.f;
       if (grow) {
         alpha = ex2_approx(m_run - mxs);
         m_run = mxs;
       }
-      float sm8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // p = 2^(x c - m): packed pairs; columns 96..127 of every row on the FMA pipe
+      const float2 c2 = make_float2(c, c), nm2 = make_float2(-m_run, -m_run);
+      float2 sm4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      uint32_t pk[64];  // the row of P as packed bf16 pairs
 #pragma unroll
-      for (int i = 0; i < 128; i += 8)
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const float p = ex2_approx(fmaf(x[i + k], c, -m_run));
-          x[i + k] = p;
-          sm8[k] += p;
-        }
-      l = l * alpha + (((sm8[0] + sm8[1]) + (sm8[2] + sm8[3])) + ((sm8[4] + sm8[5]) + (sm8[6] + sm8[7])));
+      for (int i = 0; i < 128; i += 2) {
+        const float2 v = __ffma2_rn(make_float2(x[i], x[i + 1]), c2, nm2);
+        float2 p2;
+        if (i >= 96) p2 = exp2_poly2(v);
+        else p2 = make_float2(ex2_approx(v.x), ex2_approx(v.y));
+        pk[i >> 1] = pack_bf16x2(p2.x, p2.y);
+        sm4[(i >> 1) & 3] = __fadd2_rn(sm4[(i >> 1) & 3], p2);
+      }
+      const float2 s01 = __fadd2_rn(__fadd2_rn(sm4[0], sm4[1]), __fadd2_rn(sm4[2], sm4[3]));
+      l = l * alpha + (s01.x + s01.y);
+      // The shared P tile is free once the P V MMA of the other tile's previous turn has
+      // completed (P0(j) follows P1(j-1), P1(j) follows P0(j)); by then this tile's own
+      // previous P V has completed too (issued earlier), so O_t can be rescaled.
+      {
+        const int ot = t == 0 ? 1 : (j < n0 ? 0 : 1);
+        const int oj = t == 0 ? j - 1 : (j < n0 ? j : j - 1);
+        if (oj >= 0 && !mbar_wait_warp(&pv_done[ot], oj & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      }
       if (j >= 1) {
-        if (!mbar_wait_warp(&pv_done[t], (j - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
         tc_fence_after();
         if (__any_sync(0xffffffffu, grow)) {
 #pragma unroll 1
@@ -573,7 +631,10 @@ __global__ void __launch_bounds__(320, 1)
           tmem_st_wait();
         }
       }
-      store_row_bf16_sw128(myP, r, x);
+#pragma unroll
+      for (int cc = 0; cc < 16; ++cc)
+        *reinterpret_cast<uint4*>(sP + (cc >> 3) * kPanel + sw128_chunk_offset(r, cc & 7)) =
+            make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full[t]);
@@ -879,8 +940,8 @@ __global__ void __launch_bounds__(192, 1)
 //   * Q_i / LSE_i / Dvec_i are double-buffered (tile i+1 loads during tile i); dO_i is
 //     single-buffered and reloaded as soon as the dV MMA of tile i has read it;
 //   * P^T and dS^T share one shared-memory tile (dS is written once the dV MMA has read P);
-//   * TMEM: R0 = S^T, R1 = dP^T then dQ, dV, dK.  S^T(i+1) is issued as soon as the softmax
-//     warps have read S^T(i); dQ(i) lands in R1 once dP^T(i) has been read;
+//   * TMEM: R0 = S^T, R1 = dP^T then dQ, dV, dK.  S^T(i+1) is issued right after dV(i),
+//     before the wait for dS(i); dQ(i) lands in R1 once dP^T(i) has been read;
 //   * four dedicated warps drain dQ: 32-column slices are staged (scaled, 128-byte swizzle)
 //     in a double-buffered shared tile and added into the fp32 dQ accumulator by TMA bulk
 //     reduce-adds, so no per-thread global atomics remain.
@@ -938,8 +999,8 @@ __global__ void __launch_bounds__(320, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int BH = a.B * a.H;
-  const int kt = (int)(blockIdx.x / BH);
-  const int bh = (int)(blockIdx.x % BH);
+  int kt, bh;
+  grouped_item((int)blockIdx.x, BH, a.n_tiles, false, bh, kt);  // small key tiles have the most work
   const int b = bh / a.H, h = bh % a.H;
   const int krow0 = b * a.T + kt * 128;
   const int i0 = a.causal ? kt : 0;
@@ -1038,19 +1099,27 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
+    // Order per query tile i: dP^T(i), dV(i), S^T(i+1), dK(i), dQ(i) -- S^T(i+1) goes out
+    // before the wait for dS(i), so the softmax warps find it done when they move on and
+    // compute P(i+1) while the tensor core runs dK(i) and dQ(i).
     if (lane == 0) {
       bool ok = mbar_wait(bar_kv, 0, abort_flag, a.err, ERR_TIMEOUT_MMA);
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), pd_addr = smem_u32(sPD), do_addr = smem_u32(sDO);
+      auto issue_s = [&](int it) -> bool {  // S^T(it) = K Q_it^T into R0
+        if (!mbar_wait(&q_full[it & 1], (it >> 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) return false;
+        if (it >= 1 && !mbar_wait(s_free, (it - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) return false;
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(sQ + (it & 1) * TILE);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_bf16(tR0, desc_kmajor(k_addr, kk), desc_kmajor(q_addr, kk), IDESC_SS, kk > 0 ? 1u : 0u);
+        umma_commit(s_full);
+        return true;
+      };
+      if (ok && n_it > 0) ok = issue_s(0);
       for (int it = 0; it < n_it && ok; ++it) {
         const int bf = it & 1;
         const uint32_t q_addr = smem_u32(sQ + bf * TILE);
-        if (!mbar_wait(&q_full[bf], (it >> 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
-        if (it >= 1 && !mbar_wait(s_free, (it - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)  // S^T = K Q^T
-          umma_bf16(tR0, desc_kmajor(k_addr, kk), desc_kmajor(q_addr, kk), IDESC_SS, kk > 0 ? 1u : 0u);
-        umma_commit(s_full);
         if (!mbar_wait(do_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
         if (it >= 1 && !mbar_wait(dq_free, (it - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
         tc_fence_after();
@@ -1065,6 +1134,7 @@ __global__ void __launch_bounds__(320, 1)
           umma_bf16(tDV, desc_kmajor(pd_addr, kk), desc_mnmajor(do_addr, kk), IDESC_KV, (it > 0 || kk > 0) ? 1u : 0u);
         umma_commit(dv_done);
         umma_commit(do_empty);  // dO read by dP^T and dV
+        if (it + 1 < n_it && !issue_s(it + 1)) { ok = false; break; }
         if (!mbar_wait(ds_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
@@ -1089,44 +1159,59 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else if (warp < 6) {
     // ------------------------------------------------------------------ P, dS, epilogue
+    // TMEM rows are read 64 columns (two 32-column loads) per wait; LSE is turned into
+    // -LSE * log2(e) once per query tile (one element per thread) and read with the Dvec
+    // terms as 16-byte broadcasts; the math runs on packed fp32 pairs, and a quarter of
+    // the exponentials on the FMA pipe (exp2_poly2).
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     const float c = a.scale_log2;
+    const float2 c2 = make_float2(c, c);
     bool ok = true;
     for (int it = 0; it < n_it; ++it) {
       const int bf = it & 1;
       const int i = i0 + it;
-      const float* lse = sLse + bf * 128;
+      float* nlse = sLse + bf * 128;
       const float* dvec = sDv + bf * 128;
       if (!mbar_wait_warp(&q_full[bf], (it >> 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      nlse[r] = -nlse[r] * kLog2e;
+      named_bar_sync(1, 128);
       if (!mbar_wait_warp(s_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
       tc_fence_after();
       const bool diag = a.causal && (i == kt);
       uint32_t pk[64];  // P^T row as packed bf16 pairs (kept for dS)
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint32_t sv[32];
+      for (int h2 = 0; h2 < 2; ++h2) {
+        uint32_t sv[64];
         __syncwarp();
-        tmem_ld_32x32b_x32(tR0 + lane_off + c4 * 32, sv);
+        tmem_ld_32x32b_x32(tR0 + lane_off + h2 * 64, *reinterpret_cast<uint32_t(*)[32]>(sv));
+        tmem_ld_32x32b_x32(tR0 + lane_off + h2 * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
         tmem_ld_wait();
-        if (diag) {
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const int cc = c4 * 32 + e;
-            float p0 = ex2_approx(fmaf(__uint_as_float(sv[e]), c, -lse[cc] * kLog2e));
-            float p1 = ex2_approx(fmaf(__uint_as_float(sv[e + 1]), c, -lse[cc + 1] * kLog2e));
-            if (cc < r) p0 = 0.f;  // query cc precedes key r: no attention
-            if (cc + 1 < r) p1 = 0.f;
-            pk[cc >> 1] = pack_bf16x2(p0, p1);
+        for (int e = 0; e < 64; e += 4) {
+          const int cc = h2 * 64 + e;
+          const float4 n4 = *reinterpret_cast<const float4*>(nlse + cc);
+          const float2 v0 = __ffma2_rn(make_float2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), c2,
+                                       make_float2(n4.x, n4.y));
+          const float2 v1 = __ffma2_rn(make_float2(__uint_as_float(sv[e + 2]), __uint_as_float(sv[e + 3])), c2,
+                                       make_float2(n4.z, n4.w));
+          float2 p0, p1;
+          if (cc >= 96) {
+            p0 = exp2_poly2(v0);
+            p1 = exp2_poly2(v1);
+          } else {
+            p0 = make_float2(ex2_approx(v0.x), ex2_approx(v0.y));
+            p1 = make_float2(ex2_approx(v1.x), ex2_approx(v1.y));
           }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const int cc = c4 * 32 + e;
-            pk[cc >> 1] = pack_bf16x2(ex2_approx(fmaf(__uint_as_float(sv[e]), c, -lse[cc] * kLog2e)),
-                                      ex2_approx(fmaf(__uint_as_float(sv[e + 1]), c, -lse[cc + 1] * kLog2e)));
+          if (diag) {  // query cc precedes key r: no attention
+            if (cc < r) p0.x = 0.f;
+            if (cc + 1 < r) p0.y = 0.f;
+            if (cc + 2 < r) p1.x = 0.f;
+            if (cc + 3 < r) p1.y = 0.f;
           }
+          pk[cc >> 1] = pack_bf16x2(p0.x, p0.y);
+          pk[(cc >> 1) + 1] = pack_bf16x2(p1.x, p1.y);
         }
       }
       tc_fence_before();
@@ -1144,22 +1229,29 @@ __global__ void __launch_bounds__(320, 1)
       if (!mbar_wait_warp(dv_done, it & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
       tc_fence_after();
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
+      for (int h2 = 0; h2 < 4; ++h2) {
         uint32_t dv[32];
         __syncwarp();
-        tmem_ld_32x32b_x32(tR1 + lane_off + c4 * 32, dv);
+        tmem_ld_32x32b_x32(tR1 + lane_off + h2 * 32, dv);
         tmem_ld_wait();
         uint32_t dsk[16];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const int cc = c4 * 32 + e;
-          const float2 pf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&pk[cc >> 1]));
-          dsk[e >> 1] = pack_bf16x2(pf.x * (__uint_as_float(dv[e]) - dvec[cc]),
-                                    pf.y * (__uint_as_float(dv[e + 1]) - dvec[cc + 1]));
+        for (int e = 0; e < 32; e += 4) {
+          const int cc = h2 * 32 + e;
+          const float4 d4 = *reinterpret_cast<const float4*>(dvec + cc);
+          const float2 pa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&pk[cc >> 1]));
+          const float2 pb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&pk[(cc >> 1) + 1]));
+          const float2 da = __fadd2_rn(make_float2(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])),
+                                       make_float2(-d4.x, -d4.y));
+          const float2 db = __fadd2_rn(make_float2(__uint_as_float(dv[e + 2]), __uint_as_float(dv[e + 3])),
+                                       make_float2(-d4.z, -d4.w));
+          const float2 sa = __fmul2_rn(pa, da), sb = __fmul2_rn(pb, db);
+          dsk[e >> 1] = pack_bf16x2(sa.x, sa.y);
+          dsk[(e >> 1) + 1] = pack_bf16x2(sb.x, sb.y);
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const int ch = c4 * 4 + q;
+          const int ch = h2 * 4 + q;
           *reinterpret_cast<uint4*>(sPD + (ch >> 3) * kPanel + sw128_chunk_offset(r, ch & 7)) =
               make_uint4(dsk[4 * q], dsk[4 * q + 1], dsk[4 * q + 2], dsk[4 * q + 3]);
         }

@@ -14,6 +14,9 @@ void gemm_tp(int64_t mode, torch::Tensor A, torch::Tensor B, bool b_mn, int64_t 
              torch::Tensor sched, int64_t bn, torch::Tensor err);
 void gemm_rope(torch::Tensor A, torch::Tensor B, torch::Tensor D, torch::Tensor cos, torch::Tensor sin, int64_t T,
                int64_t rope_cols, c10::optional<torch::Tensor> rstd, torch::Tensor err);
+void gemm_ce(torch::Tensor A, torch::Tensor B, torch::Tensor D, torch::Tensor tgt, int64_t T,
+             c10::optional<torch::Tensor> roww, int64_t V, double S, torch::Tensor part, torch::Tensor yc,
+             torch::Tensor cnt, torch::Tensor loss, bool write_dz, torch::Tensor err);
 void gemm_splitk_fin(torch::Tensor A, torch::Tensor B, torch::Tensor ws, torch::Tensor cnt, torch::Tensor out,
                      c10::optional<torch::Tensor> R, bool relu2, double tau, int64_t split, torch::Tensor err);
 void rmsnorm_fwd(torch::Tensor x, torch::Tensor y, c10::optional<torch::Tensor> rstd);
@@ -33,6 +36,9 @@ void causal_conv_bwd(torch::Tensor x, torch::Tensor w, torch::Tensor dy, torch::
 void ngram_gather(torch::Tensor idx, int64_t order, int64_t p1, int64_t p2, int64_t p3, int64_t mod, int64_t pad,
                   torch::Tensor table, torch::Tensor out, torch::Tensor rows);
 void ngram_scatter(torch::Tensor rows, torch::Tensor dout, torch::Tensor grad);
+void muon_fro_scale(torch::Tensor x, torch::Tensor fro);
+void normuon_tail(torch::Tensor gq, torch::Tensor second, torch::Tensor one_b2, c10::optional<torch::Tensor> out,
+                  c10::optional<torch::Tensor> w, c10::optional<torch::Tensor> lr, c10::optional<torch::Tensor> lrwd);
 void rope_norm_fwd(torch::Tensor buf, int64_t head0, int64_t nheads, int64_t D, torch::Tensor cos,
                    torch::Tensor sin, int64_t T, int64_t pos_offset, c10::optional<torch::Tensor> rstd,
                    c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> pos_t);
@@ -74,6 +80,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("bn"), py::arg("err"), py::arg("alpha_t") = py::none(), py::arg("rcoef") = 1.0);
   m.def("gemm_tp", &tfb::gemm_tp);
   m.def("gemm_splitk_fin", &tfb::gemm_splitk_fin);
+  m.def("gemm_ce", &tfb::gemm_ce, "lm_head GEMM with softcap + cross-entropy (+ dlogits) in the epilogue");
   m.def("gemm_rope", &tfb::gemm_rope, "tcgen05 bf16 GEMM with RoPE + per-head RMSNorm on the leading columns");
   m.def("rmsnorm_fwd", &tfb::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &tfb::rmsnorm_bwd);
@@ -101,6 +108,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("causal_conv_bwd", &tfb::causal_conv_bwd, "causal depthwise conv1d backward (dx, deterministic dw)");
   m.def("ngram_gather", &tfb::ngram_gather, "hashed n-gram row ids + gather (bf16 out)");
   m.def("ngram_scatter", &tfb::ngram_scatter, "n-gram table gradient scatter-add (fp32)");
+  m.def("muon_fro_scale", &tfb::muon_fro_scale, "Muon Frobenius normalisation (reference bf16 op order)");
+  m.def("normuon_tail", &tfb::normuon_tail, "NorMuon second moment + scaled update (or its apply)");
   m.def("fa_fwd", &tfb::fa_fwd, "tcgen05 causal flash attention forward");
   m.def("fa_bwd", &tfb::fa_bwd, "tcgen05 causal flash attention backward");
 }

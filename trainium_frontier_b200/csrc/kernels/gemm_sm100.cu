@@ -25,6 +25,13 @@
 //   EPI_RELU2_BWD D = bf16(bf16(alpha * acc) * 2 relu(R - tau))   (R = h)
 //   EPI_F32       D(f32) = alpha * acc (+ D if beta)        weight gradients (fp32, split-K via
 //                                                          vector atomics into the gradient)
+//   EPI_CE        lm_head + logit softcap + cross-entropy: z = bf16(acc) (stored only when
+//                 the gradient is wanted), y = S tanh(z / S); each tile adds its rows'
+//                 partial sum of exp(y - S) and the target's y to small per-row buffers, and
+//                 the warp that completes a 32-row slab (an arrival counter per slab)
+//                 writes the rows' losses and turns the slab's stored z into
+//                 dz = w (softmax(y) - onehot)(1 - t^2) in place, while it is still in L2 --
+//                 no separate pass over the [tokens, vocab] logits.
 // Modes (the tensor-parallel collectives fused into the GEMM, over NVLink peer memory):
 //   MODE_PLAIN    the GEMM above.
 //   MODE_AG       all-gather -> GEMM.  A is the [M, K] gather buffer of which every rank
@@ -57,7 +64,7 @@
 
 namespace tfb {
 
-enum GemmEpi : int { EPI_BF16 = 0, EPI_RELU2 = 1, EPI_RELU2_BWD = 2, EPI_F32 = 3, EPI_ROPE = 4 };
+enum GemmEpi : int { EPI_BF16 = 0, EPI_RELU2 = 1, EPI_RELU2_BWD = 2, EPI_F32 = 3, EPI_ROPE = 4, EPI_CE = 5 };
 enum GemmMode : int { MODE_PLAIN = 0, MODE_AG = 1, MODE_RS = 2 };
 
 constexpr int kTpMaxRanks = 8;
@@ -104,6 +111,18 @@ struct GemmArgs {
   const __nv_bfloat16* rope_sin;
   int rope_T, rope_cols, rope_heads;
   float* rope_rstd;  // [M][rope_heads] fp32, optional
+  // EPI_CE (2-D, N = padded vocab, BN = 256)
+  const void* ce_tgt;      // targets (int64 if ce_tgt_i64 else int32), row m = b * ce_T + t
+  int ce_tgt_i64, ce_T;
+  long long ce_tgt_ld;
+  const float* ce_roww;    // per-row loss weight or null
+  int ce_V;                // real classes (columns >= V are padding)
+  float ce_S;              // softcap
+  float* ce_part;          // [M][2 * tiles_n] partial sums of exp(y - S)
+  float* ce_yc;            // [M] target's capped logit
+  int* ce_cnt;             // [ceil(M / 32)] arrival counters per 32-row slab, zero between launches
+  float* ce_loss;          // [M] w * (S + log(sum) - y_c), 0 for ignored targets
+  int ce_write_dz;         // store z and rewrite it as dz
   TpArgs tp;
 };
 
@@ -273,6 +292,57 @@ __device__ __noinline__ void split_finish(const GemmArgs& a, int mb, int nb, int
   }
   __syncwarp();
   if (lane == 0) a.fin_cnt[slot] = 0;
+}
+
+// The warp that completes a 32-row slab of the lm_head GEMM (EPI_CE): every tile of the
+// slab has added its partial sums and (if the gradient is wanted) stored z.  One row at a
+// time: total, loss, and dz over the row's stored z (L2-resident reads, 16-byte vectors).
+__device__ __noinline__ void ce_finish(const GemmArgs& a, int slab, int lane) {
+  const int parts = 2 * a.tiles_n;
+  const float S = a.ce_S, invS = 1.f / S;
+#pragma unroll 1
+  for (int rr = 0; rr < 32; ++rr) {
+    const int row = slab * 32 + rr;
+    if (row >= a.M) break;
+    float tot = 0.f;
+    for (int k = lane; k < parts; k += 32) tot += __ldcg(a.ce_part + (long long)row * parts + k);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+    const long long ti = (long long)(row / a.ce_T) * a.ce_tgt_ld + row % a.ce_T;
+    const long long cls = a.ce_tgt_i64 ? reinterpret_cast<const long long*>(a.ce_tgt)[ti]
+                                       : (long long)reinterpret_cast<const int*>(a.ce_tgt)[ti];
+    const bool valid = cls >= 0 && cls < a.ce_V;
+    const float wgt = valid ? (a.ce_roww ? a.ce_roww[row] : 1.f) : 0.f;
+    if (lane == 0) a.ce_loss[row] = valid ? wgt * (S + logf(tot) - __ldcg(a.ce_yc + row)) : 0.f;
+    if (!a.ce_write_dz) continue;
+    const float inv_tot = 1.f / tot;
+    __nv_bfloat16* zrow = reinterpret_cast<__nv_bfloat16*>(a.D) + (long long)row * a.ldd;
+    for (int j0 = lane * 8; j0 < a.N; j0 += 256) {
+      uint4 u = __ldcg(reinterpret_cast<const uint4*>(zrow + j0));
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 z = __bfloat1622float2(h[q]);
+        float o[2];
+        const float zz[2] = {z.x, z.y};
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int j = j0 + 2 * q + e;
+          if (j < a.ce_V && wgt != 0.f) {
+            const float th = tanhf(zz[e] * invS);
+            const float p = __expf(S * th - S) * inv_tot;
+            o[e] = wgt * (p - (j == cls ? 1.f : 0.f)) * (1.f - th * th);
+          } else {
+            o[e] = 0.f;
+          }
+        }
+        h[q] = __floats2bfloat162_rn(o[0], o[1]);
+      }
+      *reinterpret_cast<uint4*>(zrow + j0) = u;
+    }
+  }
+  __syncwarp();
+  if (lane == 0) a.ce_cnt[slab] = 0;  // clean for the next launch
 }
 
 template <int MODE>
@@ -776,6 +846,16 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
           __syncwarp();
         };
         bool roped = false;
+        // EPI_CE: this thread's row target and its running partial sum over the tile half
+        long long ce_cls = -1;
+        float ce_sum = 0.f;
+        if constexpr (EPI == EPI_CE) {
+          if (row_ok) {
+            const long long ti = (long long)(row / args.ce_T) * args.ce_tgt_ld + row % args.ce_T;
+            ce_cls = args.ce_tgt_i64 ? reinterpret_cast<const long long*>(args.ce_tgt)[ti]
+                                     : (long long)reinterpret_cast<const int*>(args.ce_tgt)[ti];
+          }
+        }
         if constexpr (EPI == EPI_ROPE && MODE == MODE_PLAIN && BN == 256) {
           const int hcol = nb * BN + hf * 128;  // first column of this warp's head
           if (hcol < args.rope_cols) {
@@ -913,14 +993,49 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
               const float h = hf8[i] - args.tau;
               v[i] = h > 0.f ? g * (2.f * h) : 0.f;
             }
+          } else if constexpr (EPI == EPI_CE) {
+            const float S = args.ce_S, invS = 1.f / S;
+#pragma unroll
+            for (int i = 0; i < 64; ++i) {
+              const float z = __bfloat162float(__float2bfloat16_rn(v[i]));
+              const int j = col0 + i;
+              if (j < args.ce_V) {
+                const float y = S * tanhf(z * invS);
+                ce_sum += __expf(y - S);
+                if (j == ce_cls) args.ce_yc[row] = y;
+              }
+            }
+            if (!args.ce_write_dz) continue;
           }
           stage(v);
           store(&tmD, col0);
+        }
+        if constexpr (EPI == EPI_CE) {
+          if (row_ok) args.ce_part[(long long)row * (2 * args.tiles_n) + nb * 2 + hf] = ce_sum;
         }
         if (lane == 0) bulk_wait_group<0>();
         __syncwarp();
         tc_fence_before();
         release_acc(acc);
+        if constexpr (EPI == EPI_CE) {
+          // Publish this warp's stores (TMA, async proxy; complete after the wait above) and
+          // partials, count them for its 32-row slab (two column halves per tile), and the
+          // warp that completes the slab finishes its rows.  No wait on any other warp.
+          if (lane == 0) fence_proxy_async_global();
+          __threadfence();
+          __syncwarp();
+          const int slab = mb * 4 + q;
+          int last = 0;
+          if (lane == 0) {
+            __threadfence();
+            last = atomicAdd(args.ce_cnt + slab, 1) == 2 * args.tiles_n - 1;
+          }
+          last = __shfl_sync(0xffffffffu, last, 0);
+          if (last) {
+            __threadfence();
+            ce_finish(args, slab, lane);
+          }
+        }
       } else {
         const bool row_ok = row < args.M;
 #pragma unroll 1
@@ -1296,6 +1411,7 @@ static void dispatch(bool a_mn, bool b_mn, int epi, const CUtensorMap& ta, const
   TFB_CASE(true, false, EPI_BF16)
   if constexpr (BN == 256) {
     TFB_CASE(false, false, EPI_ROPE)
+    TFB_CASE(false, false, EPI_CE)
   }
 #undef TFB_CASE
   TORCH_CHECK(false, "unsupported gemm variant a_mn=", a_mn, " b_mn=", b_mn, " epi=", epi);
@@ -1331,6 +1447,20 @@ static bool tma_store_ok(int64_t epi, int64_t N, const void* d, long long ldd, l
   return true;
 }
 
+struct CeEpi {
+  const void* tgt = nullptr;
+  int tgt_i64 = 1, T = 1;
+  long long tgt_ld = 0;
+  const float* roww = nullptr;
+  int V = 0;
+  float S = 15.f;
+  float* part = nullptr;
+  float* yc = nullptr;
+  int* cnt = nullptr;
+  float* loss = nullptr;
+  int write_dz = 1;
+};
+
 // A: if !a_mn a [M, K] view (row stride lda), else a [K, M] view.  B likewise with N.
 // Operands are 2-D, or 3-D with a leading batch dimension (all of A, B, D batched alike).
 struct RopeEpi {
@@ -1343,7 +1473,8 @@ struct RopeEpi {
 static void gemm_bf16_impl(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_mn, int64_t M, int64_t N, int64_t K,
                            torch::Tensor D, int64_t epi, double alpha, double beta, c10::optional<torch::Tensor> R,
                            c10::optional<torch::Tensor> D2, double tau, int64_t split_k, int64_t bn, torch::Tensor err,
-                           c10::optional<torch::Tensor> alpha_t, double rcoef, const RopeEpi& rope) {
+                           c10::optional<torch::Tensor> alpha_t, double rcoef, const RopeEpi& rope,
+                           const CeEpi& ce = CeEpi{}) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && D.is_cuda(), "gemm operands must be CUDA tensors");
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm inputs must be bf16");
   const int64_t nb = A.dim() == 3 ? A.size(0) : 1;
@@ -1420,6 +1551,13 @@ static void gemm_bf16_impl(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_m
     td = make_tmap_bf16(a.D, N, M, a.ldd, 64, 32, nb, d_bs);
     if (epi == EPI_RELU2) td2 = make_tmap_bf16(a.D2, N, M, a.ldd2, 64, 32, nb, a.d2_bstride);
   }
+  if (epi == EPI_CE) {
+    TORCH_CHECK(a.tma_store && bn == 256 && !a_mn && !b_mn && nb == 1 && a.R == nullptr && ce.tgt != nullptr,
+                "CE epilogue: 2-D K-major operands, bf16 TMA-store output, 256-wide tiles");
+    a.ce_tgt = ce.tgt; a.ce_tgt_i64 = ce.tgt_i64; a.ce_T = ce.T; a.ce_tgt_ld = ce.tgt_ld; a.ce_roww = ce.roww;
+    a.ce_V = ce.V; a.ce_S = ce.S; a.ce_part = ce.part; a.ce_yc = ce.yc; a.ce_cnt = ce.cnt; a.ce_loss = ce.loss;
+    a.ce_write_dz = ce.write_dz;
+  }
   a.rope_cos = rope.cos; a.rope_sin = rope.sin; a.rope_T = rope.T; a.rope_cols = rope.cols;
   a.rope_heads = rope.heads; a.rope_rstd = rope.rstd;
   if (epi == EPI_ROPE)
@@ -1436,7 +1574,7 @@ void gemm_bf16(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_mn, int64_t M
                torch::Tensor D, int64_t epi, double alpha, double beta, c10::optional<torch::Tensor> R,
                c10::optional<torch::Tensor> D2, double tau, int64_t split_k, int64_t bn, torch::Tensor err,
                c10::optional<torch::Tensor> alpha_t, double rcoef) {
-  TORCH_CHECK(epi != EPI_ROPE, "the RoPE epilogue is reached through gemm_rope");
+  TORCH_CHECK(epi != EPI_ROPE && epi != EPI_CE, "the RoPE / CE epilogues are reached through gemm_rope / gemm_ce");
   gemm_bf16_impl(A, a_mn, B, b_mn, M, N, K, D, epi, alpha, beta, R, D2, tau, split_k, bn, err, alpha_t, rcoef,
                  RopeEpi{});
 }
@@ -1470,6 +1608,41 @@ void gemm_rope(torch::Tensor A, torch::Tensor B, torch::Tensor D, torch::Tensor 
   }
   gemm_bf16_impl(A, false, B, false, M, N, K, D, EPI_ROPE, 1.0, 0.0, c10::nullopt, c10::nullopt, 0.0, 1, 256, err,
                  c10::nullopt, 1.0, r);
+}
+
+// lm_head GEMM with the softcapped cross-entropy in the epilogue (EPI_CE).
+//   A = x [M, K] bf16, B = W [N, K] bf16 (N = padded vocab, a multiple of 256, >= V);
+//   tgt [B, T] int64 / int32 (row m = b * T + t; < 0 or >= V ignored); roww fp32 [M] or none;
+//   part fp32 [M * 2 * ceil(N / 256)], yc fp32 [M], cnt int32 [ceil(M / 32)] zeroed once
+//   (left zeroed), loss fp32 [M] <- w * (S + log sum_j exp(y_j - S) - y_c).
+//   With write_dz, D [M, N] bf16 receives dz = w (softmax(y) - onehot)(1 - tanh^2) (scale 1;
+//   the mean's 1 / denominator goes into the backward GEMMs' alpha); without, D is not
+//   touched and may be any bf16 tensor.
+void gemm_ce(torch::Tensor A, torch::Tensor B, torch::Tensor D, torch::Tensor tgt, int64_t T,
+             c10::optional<torch::Tensor> roww, int64_t V, double S, torch::Tensor part, torch::Tensor yc,
+             torch::Tensor cnt, torch::Tensor loss, bool write_dz, torch::Tensor err) {
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && D.dim() == 2, "2-D operands");
+  const int64_t M = A.size(0), K = A.size(1), N = B.size(0);
+  TORCH_CHECK(B.size(1) == K && N % 256 == 0 && V > 0 && V <= N, "N: padded vocab (multiple of 256) >= V");
+  TORCH_CHECK(tgt.is_cuda() && (tgt.scalar_type() == at::kLong || tgt.scalar_type() == at::kInt) && tgt.dim() == 2 &&
+                  tgt.stride(1) == 1 && T == tgt.size(1) && tgt.numel() == M,
+              "targets [B, T] int64 / int32 with unit inner stride");
+  const int64_t tiles_n = N / 256;
+  TORCH_CHECK(part.scalar_type() == at::kFloat && part.numel() >= M * 2 * tiles_n, "part fp32 [M * 2 * tiles_n]");
+  TORCH_CHECK(yc.scalar_type() == at::kFloat && yc.numel() >= M, "yc fp32 [M]");
+  TORCH_CHECK(loss.scalar_type() == at::kFloat && loss.numel() >= M && loss.is_contiguous(), "loss fp32 [M]");
+  TORCH_CHECK(cnt.scalar_type() == at::kInt && cnt.numel() >= 4 * ((M + 127) / 128), "cnt int32 [4 * ceil(M / 128)]");
+  if (write_dz) TORCH_CHECK(D.size(0) >= M && D.size(1) >= N, "D [M, N]");
+  CeEpi c;
+  c.tgt = tgt.data_ptr(); c.tgt_i64 = tgt.scalar_type() == at::kLong; c.T = (int)T; c.tgt_ld = tgt.stride(0);
+  if (roww.has_value()) {
+    TORCH_CHECK(roww->scalar_type() == at::kFloat && roww->numel() >= M && roww->is_contiguous(), "row weights fp32 [M]");
+    c.roww = roww->data_ptr<float>();
+  }
+  c.V = (int)V; c.S = (float)S; c.part = part.data_ptr<float>(); c.yc = yc.data_ptr<float>();
+  c.cnt = cnt.data_ptr<int>(); c.loss = loss.data_ptr<float>(); c.write_dz = write_dz ? 1 : 0;
+  gemm_bf16_impl(A, false, B, false, M, N, K, D, EPI_CE, 1.0, 0.0, c10::nullopt, c10::nullopt, 0.0, 1, 256, err,
+                 c10::nullopt, 1.0, RopeEpi{}, c);
 }
 
 // Few-row GEMM (decode): out[M, N] bf16 = x[M, K] W[N, K]^T (+ R | relu^2), K split over the

@@ -385,32 +385,75 @@ class QKVRopeAttnFn(Function):
 
 
 # --------------------------------------------------------------------------- lm_head + CE
-class LMHeadSoftcapCEFn(Function):
-    """loss = CE(S tanh(x W^T / S)[:, :V], targets), forward and dlogits in one pass.
+_CE_CNT: dict[int, torch.Tensor] = {}
 
+
+def _ce_counters(dev: torch.device, M: int) -> torch.Tensor:
+    """Per-32-row-slab arrival counters of the CE GEMM epilogue: zeroed once, and every
+    launch leaves them zero again."""
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    need = 4 * ((M + 127) // 128)
+    t = _CE_CNT.get(idx)
+    if t is None or t.numel() < need:
+        t = torch.zeros(need, dtype=torch.int32, device=dev)
+        _CE_CNT[idx] = t
+    return t
+
+
+def _lm_head_ce(x2, wb, targets, softcap: float, vocab: int, row_weight, write_dz: bool):
+    """One lm_head GEMM with softcap + cross-entropy in its epilogue (``gemm_ce``): returns
+    the per-row losses and the [M, Vpad] bf16 buffer holding dz (when ``write_dz``)."""
+    M = x2.shape[0]
+    Vp = wb.shape[0]
+    tg = targets if targets.dim() == 2 else targets.view(1, -1)
+    if tg.stride(-1) != 1:
+        tg = tg.contiguous()
+    dz = torch.empty((M, Vp), dtype=BF16, device=x2.device)
+    tiles_n = (Vp + 255) // 256
+    part = torch.empty(M * 2 * tiles_n, dtype=torch.float32, device=x2.device)
+    yc = torch.empty(M, dtype=torch.float32, device=x2.device)
+    loss_rows = torch.empty(M, dtype=torch.float32, device=x2.device)
+    rw = None if row_weight is None else row_weight.reshape(-1).float().contiguous()
+    C().gemm_ce(x2, wb, dz, tg, tg.shape[1], rw, int(vocab), float(softcap), part, yc,
+                _ce_counters(x2.device, M), loss_rows, bool(write_dz), gemm.err_word(x2.device))
+    return loss_rows, dz, tg
+
+
+def _ce_fusable(x2, wb) -> bool:
+    return wb.shape[0] % 256 == 0 and x2.shape[1] % 8 == 0
+
+
+class LMHeadSoftcapCEFn(Function):
+    """loss = CE(S tanh(x W^T / S)[:, :V], targets), forward and dlogits in one GEMM.
+
+    The lm_head GEMM's epilogue computes the softcap, the per-row partial sums and the
+    target logit; the warp completing each 32-row slab writes the losses and turns the
+    slab's logits into dlogits (bf16, in place) while they are still in L2.
     ``row_weight`` (fp32 per token, or None) gives the byte-weighted mean; targets < 0
-    are ignored.  dlogits are stored (bf16) in place of the logits; the upstream
-    gradient scalar is applied on the device inside the two backward GEMMs."""
+    are ignored.  The upstream gradient scalar is applied on the device inside the two
+    backward GEMMs."""
 
     @staticmethod
     def forward(ctx, x, w, targets, softcap, vocab, row_weight, reduction):
         x2 = gemm._c2(x)
         wb = w16(w)
         M = x2.shape[0]
-        logits = gemm.linear_fwd(x2, wb)
-        loss_rows = torch.empty(M, dtype=torch.float32, device=x.device)
-        tg = targets if targets.dim() == 2 else targets.view(1, -1)
-        T = tg.shape[1]
-        if tg.stride(1) != 1:
-            tg = tg.contiguous()
-        C().softcap_ce(logits, tg, T, row_weight, vocab, float(softcap), 1.0, loss_rows, True)
+        if _ce_fusable(x2, wb):
+            loss_rows, dz, tg = _lm_head_ce(x2, wb, targets, softcap, vocab, row_weight, True)
+        else:
+            dz = gemm.linear_fwd(x2, wb)
+            loss_rows = torch.empty(M, dtype=torch.float32, device=x.device)
+            tg = targets if targets.dim() == 2 else targets.view(1, -1)
+            if tg.stride(1) != 1:
+                tg = tg.contiguous()
+            C().softcap_ce(dz, tg, tg.shape[1], row_weight, vocab, float(softcap), 1.0, loss_rows, True)
         if row_weight is not None:
-            denom = (row_weight * (tg.reshape(-1) >= 0)).sum()
+            denom = (row_weight.reshape(-1) * (tg.reshape(-1) >= 0)).sum()
         else:
             denom = (tg >= 0).sum().to(torch.float32)
         inv = 1.0 / denom.clamp_min(1.0)
         loss = loss_rows.sum() * inv
-        ctx.save_for_backward(x2, logits, inv)
+        ctx.save_for_backward(x2, dz, inv)
         ctx.w = w
         ctx.shape = x.shape
         return loss
@@ -436,9 +479,14 @@ def softcap_logits(x, w, softcap: float, vocab: int) -> torch.Tensor:
 
 
 def softcap_ce_rows(x, w, targets, softcap: float, vocab: int) -> torch.Tensor:
-    """Per-token softcapped CE (no gradient), 0 where target < 0."""
+    """Per-token softcapped CE (no gradient), 0 where target < 0: the lm_head GEMM with the
+    CE epilogue in its statistics-only form (no logits are stored)."""
     x2 = gemm._c2(x)
-    logits = gemm.linear_fwd(x2, w16(w))
+    wb = w16(w)
+    if _ce_fusable(x2, wb):
+        loss_rows, _dz, _tg = _lm_head_ce(x2, wb, targets, softcap, vocab, None, False)
+        return loss_rows.view(targets.shape)
+    logits = gemm.linear_fwd(x2, wb)
     loss_rows = torch.empty(x2.shape[0], dtype=torch.float32, device=x.device)
     tg = targets if targets.dim() == 2 else targets.view(1, -1)
     C().softcap_ce(logits, tg.contiguous(), tg.shape[1], None, vocab, float(softcap), 1.0, loss_rows, False)

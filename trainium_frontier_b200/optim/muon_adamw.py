@@ -276,6 +276,14 @@ class MuonAdamW(torch.optim.Optimizer):
             if not inplace:
                 w = torch.stack([p.detach() for p in sub])
             sl = slice(i0, i1)
+            if inplace and to_bf16 and not self.muon_lr_fp32 and torch.is_tensor(one_b2_t):
+                from ..ops.optim_kernels import muon_owner_update, muon_stack_fusable
+                mb_s = state["momentum_buffer"][sl]
+                if muon_stack_fusable(g, mb_s, mom_t, lr_t) and w.dtype == torch.float32 and w.is_contiguous():
+                    ob2 = one_b2 if torch.is_tensor(one_b2) else one_b2_t
+                    muon_owner_update(g, mb_s, state["second_momentum_buffer"][sl], mom_t, one_mom_t, ob2,
+                                      ns_steps, w=w, lr=lr_t, lrwd=lrwd_t)
+                    continue
             _muon_math(w, g, state["momentum_buffer"][sl], state["second_momentum_buffer"][sl],
                        mom_t if mom_t.dim() == 0 else mom_t[sl], one_mom_t if one_mom_t.dim() == 0 else one_mom_t[sl],
                        lr_t if lr_t.dim() == 0 else lr_t[sl], lrwd_t if lrwd_t.dim() == 0 else lrwd_t[sl],

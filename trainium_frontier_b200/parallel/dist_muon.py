@@ -49,6 +49,18 @@ class BucketPlan:
     seg_numel: int = 0                                 # padded segment size (elements)
 
 
+def unit_cost(u: Unit, steps: int = 5) -> float:
+    """Estimated owner time of a unit (seconds on one B200): Newton-Schulz FLOPs at
+    ~1 PFLOP/s plus ~40 bytes of elementwise traffic per element at ~6.5 TB/s.  An
+    r x c matrix with n = min(r, c), m = max(r, c) costs 4 n^2 m + 2 n^3 per iteration
+    (Gram product, its square, the product back), so a 1280 x 5120 matrix costs about
+    three, not four, 1280 x 1280 ones -- owners are balanced on this, not on size."""
+    r, c = u.params[0].shape[-2], u.params[0].shape[-1]
+    n, m = min(r, c), max(r, c)
+    flops = steps * (4.0 * n * n * m + 2.0 * n ** 3) * len(u.params)
+    return flops / 1.0e15 + 40.0 * u.numel / 6.5e12
+
+
 def plan_buckets(model, muon_param_ids: set[int], world: int, bucket_layers: int) -> list[BucketPlan]:
     blocks = list(model.transformer.h)
     L = len(blocks)
@@ -68,11 +80,13 @@ def plan_buckets(model, muon_param_ids: set[int], world: int, bucket_layers: int
             for p in blk.parameters():
                 if id(p) in muon_param_ids and id(p) not in taken:
                     units.append(Unit([p], p.numel()))
+        cost = [0.0] * world
         loads = [0] * world
         owners: list[list[Unit]] = [[] for _ in range(world)]
-        for u in sorted(units, key=lambda u: -u.numel):
-            r = min(range(world), key=lambda i: loads[i])
+        for u in sorted(units, key=lambda u: -unit_cost(u)):
+            r = min(range(world), key=lambda i: (cost[i], loads[i]))
             owners[r].append(u)
+            cost[r] += unit_cost(u)
             loads[r] += u.numel
         # inside a rank: group by shape so each (rank, shape) run is one contiguous stack
         for r in range(world):
@@ -297,6 +311,12 @@ class DistMuon:
                     g = g * self.clip_coef
                 w = torch.stack([p.detach() for p in params]) if not _adjacent(params) else _stack_view(params)
                 st = self._state(params, grp)
+                if to_bf16:
+                    # the fused owner kernels (clip folded into the momentum prologue)
+                    _fused_owner_direction(self, grp, seg[off:off + n].view(K, *shape), st,
+                                           None if self.clip_coef is None else self.clip_coef.reshape(1),
+                                           upd[off:off + n].view(K, *shape))
+                    continue
                 gq = muon_direction(opt, grp, w, g, st["mb"], st["second"], to_bf16)
                 upd[off:off + n].copy_(gq.reshape(-1).to(torch.bfloat16))
             out = self.gath[b]
@@ -360,38 +380,45 @@ def _apply_update(opt, grp, w, gq, params) -> None:
     w.sub_(lr_t.to(gq.dtype) * gq + lrwd_t * w * mask)
 
 
-def _fused_owner_direction(dm, grp, g, st, coef):
-    """Owner half on the GPU: fused prologue kernel, Newton-Schulz, NorMuon scaling."""
-    from ..ops import newton_schulz as ns
+def _fused_owner_direction(dm, grp, g, st, coef, out):
+    """Owner half on the GPU, written straight into this rank's update buffer ``out``:
+    clip + momentum / Nesterov prologue, Frobenius normalisation, Newton-Schulz, NorMuon
+    (``ops.optim_kernels.muon_owner_update``)."""
+    from ..ops.optim_kernels import muon_owner_update, muon_stack_fusable
+    from ..optim.muon_adamw import muon_direction
     opt = dm.opt
-    K = g.shape[0]
     shape = g.shape[1:]
-    red_dim = -1 if shape[-2] >= shape[-1] else -2
     ratio = max(1.0, shape[-2] / shape[-1]) ** 0.5
-    _lr, _lrwd, mom_t, one_mom_t, _ = opt._muon_scalars(grp, g, ratio)
-    x = torch.empty(g.shape, dtype=torch.bfloat16, device=g.device)
-    fro = torch.zeros(K, dtype=torch.float32, device=g.device)
-    dm.C.muon_pre(g, st["mb"], x, coef, mom_t.reshape(1), one_mom_t.reshape(1), fro)
-    x.mul_((1.0 / (fro.sqrt() * 1.01 + 1e-6)).to(torch.bfloat16).view(K, 1, 1))
-    gq = ns.newton_schulz(x, min(grp["ns_steps"], len(POLAR_EXPRESS_COEFFS)))
-    v_mean = gq.float().square().mean(dim=red_dim, keepdim=True)
-    red_size = gq.size(red_dim)
-    v_norm = (v_mean.sum(dim=(-2, -1), keepdim=True) * red_size).sqrt()
-    st["second"].lerp_(v_mean, 1 - grp["beta2"])
-    step_size = st["second"].clamp_min(1e-10).rsqrt()
-    scaled = (v_mean * red_size) * step_size.square()
-    v_norm_new = scaled.sum(dim=(-2, -1), keepdim=True).sqrt()
-    return gq * (step_size * (v_norm / v_norm_new.clamp_min(1e-10))).to(gq.dtype)
+    _lr, _lrwd, mom_t, one_mom_t, one_b2_t = opt._muon_scalars(grp, g, ratio)
+    if not muon_stack_fusable(g, st["mb"], mom_t, _lr):
+        # shapes the kernels do not take (e.g. a width not a multiple of 8): eager math
+        gc = g * coef if coef is not None else g
+        out.copy_(muon_direction(opt, grp, gc, gc, st["mb"], st["second"], True).to(out.dtype))
+        return
+    muon_owner_update(g, st["mb"], st["second"], mom_t, one_mom_t, one_b2_t,
+                      min(grp["ns_steps"], len(POLAR_EXPRESS_COEFFS)), coef=coef, out=out)
 
 
 def _step_fused(self, update_adamw: bool = True) -> None:
+    """Owner math bucket by bucket on the main stream; as soon as every owner has written
+    bucket b's updates (a device barrier issued on the comm stream after this rank's
+    bucket-b work), the gather + apply of bucket b runs on the comm stream while the main
+    stream goes on with the Newton-Schulz of bucket b+1."""
     opt = self.opt
     for g in opt.param_groups:
         if g["kind"] == "adamw" and update_adamw:
             opt._adamw_step(g)
         elif g["kind"] == "rmsprop" and update_adamw:
             opt._rmsprop_step(g)
+    # scalars of every group (lr*ratio, lr*ratio*wd, momentum, ...) staged once for the
+    # owner kernels and the apply kernel
+    for g in opt.param_groups:
+        if g["kind"] == "muon":
+            shape = g["params"][0].shape
+            opt._muon_scalars(g, g["params"][0], max(1.0, shape[-2] / shape[-1]) ** 0.5)
     coef = self.clip_coef.reshape(1) if self.clip_coef is not None else None
+    main = torch.cuda.current_stream(self.device)
+    side = self.comm if self.comm is not None else main
     for b in range(len(self.plans)):
         S = self.plans[b].seg_numel
         seg = self.recv[b]
@@ -401,16 +428,13 @@ def _step_fused(self, update_adamw: bool = True) -> None:
             n = K * params[0].numel()
             grp = self.group_of[id(params[0])]
             g = seg[off:off + n].view(K, *shape)
-            gq = _fused_owner_direction(self, grp, g, self._state(params, grp), coef)
-            self.upd[base + off:base + off + n].copy_(gq.reshape(-1))
-    # scalars of every group (lr*ratio, lr*ratio*wd) for the apply kernel
-    for g in opt.param_groups:
-        if g["kind"] == "muon":
-            shape = g["params"][0].shape
-            opt._muon_scalars(g, g["params"][0], max(1.0, shape[-2] / shape[-1]) ** 0.5)
-    self._barrier()  # every owner's updates are in its update buffer
-    for b in range(len(self.plans)):
-        self.C.symm_ag_apply(self.upd_peers, self._runs_table(b))
+            _fused_owner_direction(self, grp, g, self._state(params, grp), coef,
+                                   self.upd[base + off:base + off + n].view(K, *shape))
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            self._barrier()  # every owner's bucket-b updates are in its update buffer
+            self.C.symm_ag_apply(self.upd_peers, self._runs_table(b))
+    main.wait_stream(side)
     self._barrier()  # peers are done reading this rank's gradient and update buffers
 
 
