@@ -18,6 +18,11 @@ Two numbers are reported:
 Activations per micro-step are several GB, far above the 126 MB L2, so no explicit
 flush is needed between steps.
 
+``--impl library`` is a separately labelled comparator, not the reference: this
+framework's model, engine and optimizer with every op routed through its PyTorch oracle
+(bf16 cuBLAS GEMMs, SDPA attention, eager elementwise / optimizer math) -- how the same
+model fares on library kernels.
+
 ``--impl reference`` runs the unmodified reference (``baseline/_ref/train.py``,
 installed from the reference tree) through its own module API and stock code path
 (torch.compile/inductor, SDPA, its eager Muon, per-parameter all-reduce) on the same
@@ -139,6 +144,21 @@ def barrier_sync(dev):
 
 # ----------------------------------------------------------------------------- ours
 def run_ours(args) -> dict:
+    import contextlib
+
+    import torch
+    from trainium_frontier_b200 import ops
+    library = args.impl == "library"
+    with (ops.oracle_mode() if library else contextlib.nullcontext()):
+        out = _run_ours(args)
+    if library:
+        out["impl"] = "library"
+        out["dtype"] = "bf16 (this framework's model and engine with every op on its PyTorch oracle: cuBLAS GEMMs, SDPA, eager elementwise)"
+        out["gpu_launches"] = 0
+    return out
+
+
+def _run_ours(args) -> dict:
     import torch
     from trainium_frontier_b200.config import preset
     from trainium_frontier_b200.ops import _ext
@@ -397,7 +417,9 @@ def main():
     ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "library"],
+                    help="ours: the sm_100a kernels; reference: the reference's own CUDA path; library: this "
+                         "framework's model with every op on its PyTorch oracle (a bf16 library comparator)")
     ap.add_argument("--micro-rows", type=int, default=0,
                     help="sequences per micro-step per GPU (default: 32 at seq 2048, 4 for d26 at seq 4096)")
     ap.add_argument("--ref-micro-rows", type=int, default=0,

@@ -50,7 +50,15 @@ struct FaArgs {
   __nv_bfloat16* dV;
   long long lddv;
   int* err;
+  long long* trace;  // optional phase timeline (clock64) of CTA 0, see fa_trace_set
 };
+
+// Phase timeline of CTA 0 (off unless a buffer is installed): role r, step i, event e at
+// trace[(r * 64 + i) * 8 + e], i < 64.  Roles: 0 MMA issuer, 1 softmax warp (first of
+// its group), 2 dQ drain / second softmax group, 3 producer.
+__device__ __forceinline__ void fa_stamp(long long* tr, int role, int i, int e) {
+  if (tr != nullptr && blockIdx.x == 0 && i < 64) tr[(role * 64 + i) * 8 + e] = clock64();
+}
 
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -945,11 +953,12 @@ __global__ void __launch_bounds__(192, 1)
 //   * four dedicated warps drain dQ: 32-column slices are staged (scaled, 128-byte swizzle)
 //     in a double-buffered shared tile and added into the fp32 dQ accumulator by TMA bulk
 //     reduce-adds, so no per-thread global atomics remain.
-//   warp 0 TMA, warp 1 MMA, warps 2-5 softmax / dS / epilogue, warps 6-9 dQ drain.
+//   warp 0 TMA, warp 1 MMA, warps 2-9 softmax / dS / epilogue (two per TMEM lane quarter,
+//   64 columns each), warps 10-13 dQ drain.
 constexpr size_t kBwd2Need = 2 * 32768 + 2 * 32768 + 32768 + 32768 + 2 * 16384 + 4 * 512 + 32 * 8 + 32;
 constexpr size_t kBwd2Smem = 232448;
 
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(448, 1)
     fa_bwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                    const __grid_constant__ CUtensorMap tmDQ, const FaArgs a) {
@@ -1017,11 +1026,11 @@ __global__ void __launch_bounds__(320, 1)
     mbar_init(do_full, 1);
     mbar_init(do_empty, 1);
     mbar_init(s_full, 1);
-    mbar_init(s_free, 128);
+    mbar_init(s_free, 256);
     mbar_init(dp_full, 1);
-    mbar_init(p_full, 128);
+    mbar_init(p_full, 256);
     mbar_init(dv_done, 1);
-    mbar_init(ds_full, 128);
+    mbar_init(ds_full, 256);
     mbar_init(dq_full, 1);
     mbar_init(dq_free, 128);
     mbar_init(pds_free, 1);
@@ -1066,6 +1075,7 @@ __global__ void __launch_bounds__(320, 1)
           ok = false;
           break;
         }
+        fa_stamp(a.trace, 3, it, 0);
         mbar_arrive_expect_tx(&q_full[bf], TILE + 2 * 512);
         q_valid |= 1u << bf;
         q_par = (q_par & ~(1u << bf)) | ((uint32_t)((it >> 1) & 1) << bf);
@@ -1077,6 +1087,7 @@ __global__ void __launch_bounds__(320, 1)
           ok = false;
           break;
         }
+        fa_stamp(a.trace, 3, it, 1);
         mbar_arrive_expect_tx(do_full, TILE);
         do_pending = true;
         do_par = it & 1;
@@ -1120,14 +1131,19 @@ __global__ void __launch_bounds__(320, 1)
       for (int it = 0; it < n_it && ok; ++it) {
         const int bf = it & 1;
         const uint32_t q_addr = smem_u32(sQ + bf * TILE);
+        fa_stamp(a.trace, 0, it, 4);
         if (!mbar_wait(do_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
+        fa_stamp(a.trace, 0, it, 5);
         if (it >= 1 && !mbar_wait(dq_free, (it - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
+        fa_stamp(a.trace, 0, it, 6);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)  // dP^T = V dO^T
           umma_bf16(tR1, desc_kmajor(v_addr, kk), desc_kmajor(do_addr, kk), IDESC_SS, kk > 0 ? 1u : 0u);
         umma_commit(dp_full);
+        fa_stamp(a.trace, 0, it, 0);
         if (!mbar_wait(p_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
+        fa_stamp(a.trace, 0, it, 1);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)  // dV += P^T dO
@@ -1135,7 +1151,9 @@ __global__ void __launch_bounds__(320, 1)
         umma_commit(dv_done);
         umma_commit(do_empty);  // dO read by dP^T and dV
         if (it + 1 < n_it && !issue_s(it + 1)) { ok = false; break; }
+        fa_stamp(a.trace, 0, it, 2);
         if (!mbar_wait(ds_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
+        fa_stamp(a.trace, 0, it, 3);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)  // dK += dS^T Q
@@ -1157,13 +1175,17 @@ __global__ void __launch_bounds__(320, 1)
           if (globaltimer_ns() - t0 > 100000000ull) break;
       }
     }
-  } else if (warp < 6) {
+  } else if (warp < 10) {
     // ------------------------------------------------------------------ P, dS, epilogue
-    // TMEM rows are read 64 columns (two 32-column loads) per wait; LSE is turned into
-    // -LSE * log2(e) once per query tile (one element per thread) and read with the Dvec
-    // terms as 16-byte broadcasts; the math runs on packed fp32 pairs, and a quarter of
-    // the exponentials on the FMA pipe (exp2_poly2).
+    // Eight warps: two per TMEM lane quarter, each taking 64 of the row's 128 columns, so
+    // every SM sub-partition runs two of them and their TMEM-load and MUFU latencies
+    // overlap.  A thread's 64 columns are read with one wait; LSE is turned into
+    // -LSE * log2(e) once per query tile and read with the Dvec terms as 16-byte
+    // broadcasts; the math runs on packed fp32 pairs, and a quarter of the exponentials
+    // on the FMA pipe (exp2_poly2).
     const int q4 = warp & 3;
+    const int half = (warp - 2) >> 2;  // columns [64 half, 64 half + 64)
+    const int cb = half * 64;
     const int r = q4 * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     const float c = a.scale_log2;
@@ -1174,30 +1196,33 @@ __global__ void __launch_bounds__(320, 1)
       const int i = i0 + it;
       float* nlse = sLse + bf * 128;
       const float* dvec = sDv + bf * 128;
+      const bool stamp = warp == 2 && lane == 0;
+      if (stamp) fa_stamp(a.trace, 1, it, 0);
       if (!mbar_wait_warp(&q_full[bf], (it >> 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
-      nlse[r] = -nlse[r] * kLog2e;
-      named_bar_sync(1, 128);
+      if (half == 0) nlse[r] = -nlse[r] * kLog2e;
+      named_bar_sync(1, 256);
       if (!mbar_wait_warp(s_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      if (stamp) fa_stamp(a.trace, 1, it, 1);
       tc_fence_after();
       const bool diag = a.causal && (i == kt);
-      uint32_t pk[64];  // P^T row as packed bf16 pairs (kept for dS)
+      uint32_t pk[32];  // this thread's 64 columns of the P^T row, packed bf16 pairs (kept for dS)
 #pragma unroll
       for (int h2 = 0; h2 < 2; ++h2) {
-        uint32_t sv[64];
+        uint32_t sv[32];
         __syncwarp();
-        tmem_ld_32x32b_x32(tR0 + lane_off + h2 * 64, *reinterpret_cast<uint32_t(*)[32]>(sv));
-        tmem_ld_32x32b_x32(tR0 + lane_off + h2 * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+        tmem_ld_32x32b_x32(tR0 + lane_off + cb + h2 * 32, sv);
         tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 64; e += 4) {
-          const int cc = h2 * 64 + e;
+        for (int e0 = 0; e0 < 32; e0 += 4) {
+          const int e = h2 * 32 + e0;
+          const int cc = cb + e;
           const float4 n4 = *reinterpret_cast<const float4*>(nlse + cc);
-          const float2 v0 = __ffma2_rn(make_float2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), c2,
+          const float2 v0 = __ffma2_rn(make_float2(__uint_as_float(sv[e0]), __uint_as_float(sv[e0 + 1])), c2,
                                        make_float2(n4.x, n4.y));
-          const float2 v1 = __ffma2_rn(make_float2(__uint_as_float(sv[e + 2]), __uint_as_float(sv[e + 3])), c2,
+          const float2 v1 = __ffma2_rn(make_float2(__uint_as_float(sv[e0 + 2]), __uint_as_float(sv[e0 + 3])), c2,
                                        make_float2(n4.z, n4.w));
           float2 p0, p1;
-          if (cc >= 96) {
+          if (e >= 48) {
             p0 = exp2_poly2(v0);
             p1 = exp2_poly2(v1);
           } else {
@@ -1210,72 +1235,74 @@ __global__ void __launch_bounds__(320, 1)
             if (cc + 2 < r) p1.x = 0.f;
             if (cc + 3 < r) p1.y = 0.f;
           }
-          pk[cc >> 1] = pack_bf16x2(p0.x, p0.y);
-          pk[(cc >> 1) + 1] = pack_bf16x2(p1.x, p1.y);
+          pk[e >> 1] = pack_bf16x2(p0.x, p0.y);
+          pk[(e >> 1) + 1] = pack_bf16x2(p1.x, p1.y);
         }
       }
       tc_fence_before();
       mbar_arrive(s_free);
+      if (stamp) fa_stamp(a.trace, 1, it, 2);
       if (it >= 1 && !mbar_wait_warp(pds_free, (it - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      if (stamp) fa_stamp(a.trace, 1, it, 3);
 #pragma unroll
-      for (int cc = 0; cc < 16; ++cc) {
-        const uint4 u = make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
-        *reinterpret_cast<uint4*>(sPD + (cc >> 3) * kPanel + sw128_chunk_offset(r, cc & 7)) = u;
-      }
+      for (int q = 0; q < 8; ++q)
+        *reinterpret_cast<uint4*>(sPD + half * kPanel + sw128_chunk_offset(r, q)) =
+            make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
+      if (stamp) fa_stamp(a.trace, 1, it, 4);
       if (!mbar_wait_warp(dp_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
       if (!mbar_wait_warp(dv_done, it & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      if (stamp) fa_stamp(a.trace, 1, it, 5);
       tc_fence_after();
 #pragma unroll
-      for (int h2 = 0; h2 < 4; ++h2) {
+      for (int h2 = 0; h2 < 2; ++h2) {
         uint32_t dv[32];
         __syncwarp();
-        tmem_ld_32x32b_x32(tR1 + lane_off + h2 * 32, dv);
+        tmem_ld_32x32b_x32(tR1 + lane_off + cb + h2 * 32, dv);
         tmem_ld_wait();
-        uint32_t dsk[16];
 #pragma unroll
-        for (int e = 0; e < 32; e += 4) {
-          const int cc = h2 * 32 + e;
+        for (int e0 = 0; e0 < 32; e0 += 4) {
+          const int e = h2 * 32 + e0;
+          const int cc = cb + e;
           const float4 d4 = *reinterpret_cast<const float4*>(dvec + cc);
-          const float2 pa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&pk[cc >> 1]));
-          const float2 pb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&pk[(cc >> 1) + 1]));
-          const float2 da = __fadd2_rn(make_float2(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])),
+          const float2 pa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&pk[e >> 1]));
+          const float2 pb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&pk[(e >> 1) + 1]));
+          const float2 da = __fadd2_rn(make_float2(__uint_as_float(dv[e0]), __uint_as_float(dv[e0 + 1])),
                                        make_float2(-d4.x, -d4.y));
-          const float2 db = __fadd2_rn(make_float2(__uint_as_float(dv[e + 2]), __uint_as_float(dv[e + 3])),
+          const float2 db = __fadd2_rn(make_float2(__uint_as_float(dv[e0 + 2]), __uint_as_float(dv[e0 + 3])),
                                        make_float2(-d4.z, -d4.w));
           const float2 sa = __fmul2_rn(pa, da), sb = __fmul2_rn(pb, db);
-          dsk[e >> 1] = pack_bf16x2(sa.x, sa.y);
-          dsk[(e >> 1) + 1] = pack_bf16x2(sb.x, sb.y);
-        }
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int ch = h2 * 4 + q;
-          *reinterpret_cast<uint4*>(sPD + (ch >> 3) * kPanel + sw128_chunk_offset(r, ch & 7)) =
-              make_uint4(dsk[4 * q], dsk[4 * q + 1], dsk[4 * q + 2], dsk[4 * q + 3]);
+          pk[e >> 1] = pack_bf16x2(sa.x, sa.y);  // dS^T overwrites P^T in registers too
+          pk[(e >> 1) + 1] = pack_bf16x2(sb.x, sb.y);
         }
       }
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        *reinterpret_cast<uint4*>(sPD + half * kPanel + sw128_chunk_offset(r, q)) =
+            make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(ds_full);
+      if (stamp) fa_stamp(a.trace, 1, it, 6);
     }
     if (ok && mbar_wait_warp(kv_done, 0, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) {
       tc_fence_after();
-      __nv_bfloat16* dvp = a.dV + (long long)(krow0 + r) * a.lddv + h * D;
-      __nv_bfloat16* dkp = a.dK + (long long)(krow0 + r) * a.lddk + h * D;
+      __nv_bfloat16* dvp = a.dV + (long long)(krow0 + r) * a.lddv + h * D + cb;
+      __nv_bfloat16* dkp = a.dK + (long long)(krow0 + r) * a.lddk + h * D + cb;
 #pragma unroll 1
-      for (int cc = 0; cc < D / 32; ++cc) {
+      for (int cc = 0; cc < 2; ++cc) {
         uint32_t o[32];
         float f[32];
         __syncwarp();
-        tmem_ld_32x32b_x32(tDV + lane_off + cc * 32, o);
+        tmem_ld_32x32b_x32(tDV + lane_off + cb + cc * 32, o);
         tmem_ld_wait();
 #pragma unroll
         for (int v = 0; v < 32; ++v) f[v] = __uint_as_float(o[v]);
         store_row_bf16_global(dvp + cc * 32, f, 32);
         __syncwarp();
-        tmem_ld_32x32b_x32(tDK + lane_off + cc * 32, o);
+        tmem_ld_32x32b_x32(tDK + lane_off + cb + cc * 32, o);
         tmem_ld_wait();
 #pragma unroll
         for (int v = 0; v < 32; ++v) f[v] = __uint_as_float(o[v]) * a.scale;
@@ -1287,52 +1314,60 @@ __global__ void __launch_bounds__(320, 1)
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-    const bool issuer = (warp == 6 && lane == 0);
+    const bool issuer = (warp == 10 && lane == 0);
     int g = 0;          // staging slices issued so far (this CTA)
     bool ok = true;
     for (int it = 0; it < n_it && ok; ++it) {
       const int i = i0 + it;
+      if (issuer) fa_stamp(a.trace, 2, it, 0);
       if (!mbar_wait_warp(dq_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      if (issuer) fa_stamp(a.trace, 2, it, 1);
       tc_fence_after();
-      uint32_t o[4][32];
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
+      // two 64-column halves (64 registers); R1 is released once both have been read
+#pragma unroll 1
+      for (int hh = 0; hh < 2 && ok; ++hh) {
+        uint32_t o[2][32];
         __syncwarp();
-        tmem_ld_32x32b_x32(tR1 + lane_off + cc * 32, o[cc]);
-      }
-      tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(dq_free);  // R1 may take dP^T of the next tile
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc, ++g) {
-        const int sb = g & 1;
-        if (g >= 2 && !mbar_wait_warp(&stg_free[sb], ((g - 2) >> 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) {
-          ok = false;
-          break;
+        tmem_ld_32x32b_x32(tR1 + lane_off + hh * 64, o[0]);
+        tmem_ld_32x32b_x32(tR1 + lane_off + hh * 64 + 32, o[1]);
+        tmem_ld_wait();
+        if (hh == 1) {
+          tc_fence_before();
+          mbar_arrive(dq_free);  // R1 may take dP^T of the next tile
+          if (issuer) fa_stamp(a.trace, 2, it, 2);
         }
-        uint8_t* st = sDQ + sb * STG;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {  // row r: 32 fp32 = 8 x 16 B chunks, 128-byte swizzle
-          const float4 v = make_float4(__uint_as_float(o[cc][4 * q]) * a.scale, __uint_as_float(o[cc][4 * q + 1]) * a.scale,
-                                       __uint_as_float(o[cc][4 * q + 2]) * a.scale, __uint_as_float(o[cc][4 * q + 3]) * a.scale);
-          *reinterpret_cast<float4*>(st + r * 128 + ((q ^ (r & 7)) << 4)) = v;
-        }
-        fence_proxy_async_smem();
-        mbar_arrive(&stg_full[sb]);
-        if (issuer) {
-          if (!mbar_wait(&stg_full[sb], (g >> 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) {
+        for (int c2 = 0; c2 < 2; ++c2, ++g) {
+          const int cc = hh * 2 + c2;
+          const int sb = g & 1;
+          if (g >= 2 && !mbar_wait_warp(&stg_free[sb], ((g - 2) >> 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) {
             ok = false;
-          } else {
-            tma_reduce_add_3d(&tmDQ, st, h * D + cc * 32, b * a.T + i * 128, 0);
-            bulk_commit_group();
-            if (g >= 1) {
-              bulk_wait_group_read<1>();            // slice g-1 has been read from shared memory
-              mbar_arrive(&stg_free[(g - 1) & 1]);
+            break;
+          }
+          uint8_t* st = sDQ + sb * STG;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {  // row r: 32 fp32 = 8 x 16 B chunks, 128-byte swizzle
+            const float4 v = make_float4(__uint_as_float(o[c2][4 * q]) * a.scale, __uint_as_float(o[c2][4 * q + 1]) * a.scale,
+                                         __uint_as_float(o[c2][4 * q + 2]) * a.scale, __uint_as_float(o[c2][4 * q + 3]) * a.scale);
+            *reinterpret_cast<float4*>(st + r * 128 + ((q ^ (r & 7)) << 4)) = v;
+          }
+          fence_proxy_async_smem();
+          mbar_arrive(&stg_full[sb]);
+          if (issuer) {
+            if (!mbar_wait(&stg_full[sb], (g >> 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) {
+              ok = false;
+            } else {
+              tma_reduce_add_3d(&tmDQ, st, h * D + cc * 32, b * a.T + i * 128, 0);
+              bulk_commit_group();
+              if (g >= 1) {
+                bulk_wait_group_read<1>();            // slice g-1 has been read from shared memory
+                mbar_arrive(&stg_free[(g - 1) & 1]);
+              }
             }
           }
+          ok = __all_sync(0xffffffffu, ok) != 0;
+          if (!ok) break;
         }
-        ok = __all_sync(0xffffffffu, ok) != 0;
-        if (!ok) break;
       }
     }
     if (issuer) bulk_wait_group<0>();  // every reduce-add has completed before the CTA exits
@@ -1398,6 +1433,19 @@ static void check_view(const torch::Tensor& t, const char* n, int64_t rows, int6
   TORCH_CHECK((t.stride(0) * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0, n, ": 16-byte aligned rows");
 }
 
+static long long* g_fa_trace = nullptr;
+
+// Install (or with None remove) an int64 [4 * 64 * 8] buffer that the next flash-attention
+// launches fill with the phase timeline of their CTA 0 (clock64 values).
+void fa_trace_set(c10::optional<torch::Tensor> buf) {
+  if (buf.has_value()) {
+    TORCH_CHECK(buf->is_cuda() && buf->scalar_type() == at::kLong && buf->numel() >= 4 * 64 * 8, "int64 [2048]");
+    g_fa_trace = reinterpret_cast<long long*>(buf->data_ptr<int64_t>());
+  } else {
+    g_fa_trace = nullptr;
+  }
+}
+
 // q, k, v: [B*T, *] row views (head h at cols h*D); out: [B*T, >= H*D]; lse: fp32 [B*H*T]
 void fa_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, int64_t B, int64_t T, int64_t H, int64_t D,
             double scale, bool causal, torch::Tensor out, torch::Tensor lse, torch::Tensor err) {
@@ -1419,6 +1467,7 @@ void fa_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, int64_t B, int64_
   a.O = reinterpret_cast<__nv_bfloat16*>(out.data_ptr()); a.ldo = out.stride(0);
   a.lse = lse.data_ptr<float>();
   a.err = err.data_ptr<int>();
+  a.trace = g_fa_trace;
   const unsigned grid = (unsigned)(B * H * (T / 128));
   auto s = at::cuda::getCurrentCUDAStream();
   static const bool one_tile = getenv("TFB_FA_FWD_ONE_TILE") != nullptr;
@@ -1481,13 +1530,14 @@ void fa_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, 
   a.dK = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr()); a.lddk = dk.stride(0);
   a.dV = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr()); a.lddv = dv.stride(0);
   a.err = err.data_ptr<int>();
+  a.trace = g_fa_trace;
   const unsigned grid = (unsigned)(B * H * (T / 128));
   static const bool serial_bwd = getenv("TFB_FA_BWD_SERIAL") != nullptr;
   if (D == 128 && !serial_bwd) {
     static bool init = false;
     if (!init) { set_smem(fa_bwd2_kernel, kBwd2Smem); init = true; }
     CUtensorMap tdq = make_tmap_f32(dq_acc.data_ptr(), cols, rows, dq_acc.stride(0), 32, 128);
-    fa_bwd2_kernel<<<grid, 320, kBwd2Smem, s>>>(tq, tk, tv, tdo, tdq, a);
+    fa_bwd2_kernel<<<grid, 448, kBwd2Smem, s>>>(tq, tk, tv, tdo, tdq, a);
   } else if (D == 128) {
     static bool init = false;
     if (!init) { set_smem(fa_bwd_kernel<128>, FaCfg<128>::BWD_SMEM); init = true; }

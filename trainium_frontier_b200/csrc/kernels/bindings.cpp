@@ -16,7 +16,7 @@ void gemm_rope(torch::Tensor A, torch::Tensor B, torch::Tensor D, torch::Tensor 
                int64_t rope_cols, c10::optional<torch::Tensor> rstd, torch::Tensor err);
 void gemm_ce(torch::Tensor A, torch::Tensor B, torch::Tensor D, torch::Tensor tgt, int64_t T,
              c10::optional<torch::Tensor> roww, int64_t V, double S, torch::Tensor part, torch::Tensor yc,
-             torch::Tensor cnt, torch::Tensor loss, bool write_dz, torch::Tensor err);
+             torch::Tensor loss, bool write_dz, torch::Tensor err);
 void gemm_splitk_fin(torch::Tensor A, torch::Tensor B, torch::Tensor ws, torch::Tensor cnt, torch::Tensor out,
                      c10::optional<torch::Tensor> R, bool relu2, double tau, int64_t split, torch::Tensor err);
 void rmsnorm_fwd(torch::Tensor x, torch::Tensor y, c10::optional<torch::Tensor> rstd);
@@ -39,6 +39,9 @@ void ngram_scatter(torch::Tensor rows, torch::Tensor dout, torch::Tensor grad);
 void muon_fro_scale(torch::Tensor x, torch::Tensor fro);
 void normuon_tail(torch::Tensor gq, torch::Tensor second, torch::Tensor one_b2, c10::optional<torch::Tensor> out,
                   c10::optional<torch::Tensor> w, c10::optional<torch::Tensor> lr, c10::optional<torch::Tensor> lrwd);
+void fa_trace_set(c10::optional<torch::Tensor> buf);
+void embed_grad_det(torch::Tensor idx, torch::Tensor wte, torch::Tensor rstd, c10::optional<torch::Tensor> gacc,
+                    c10::optional<torch::Tensor> gb, torch::Tensor dwte);
 void rope_norm_fwd(torch::Tensor buf, int64_t head0, int64_t nheads, int64_t D, torch::Tensor cos,
                    torch::Tensor sin, int64_t T, int64_t pos_offset, c10::optional<torch::Tensor> rstd,
                    c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> pos_t);
@@ -88,6 +91,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mix_norm_bwd", &tfb::mix_norm_bwd);
   m.def("embed_norm_fwd", &tfb::embed_norm_fwd);
   m.def("embed_norm_bwd", &tfb::embed_norm_bwd);
+  m.def("embed_grad_det", &tfb::embed_grad_det, "deterministic embedding gradient (sorted segmented sums)");
   m.def("rope_norm_fwd", &tfb::rope_norm_fwd, py::arg("buf"), py::arg("head0"), py::arg("nheads"), py::arg("D"),
         py::arg("cos"), py::arg("sin"), py::arg("T"), py::arg("pos_offset"), py::arg("rstd"), py::arg("out"),
         py::arg("pos_t") = py::none());
@@ -110,6 +114,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ngram_scatter", &tfb::ngram_scatter, "n-gram table gradient scatter-add (fp32)");
   m.def("muon_fro_scale", &tfb::muon_fro_scale, "Muon Frobenius normalisation (reference bf16 op order)");
   m.def("normuon_tail", &tfb::normuon_tail, "NorMuon second moment + scaled update (or its apply)");
+  m.def("fa_trace_set", &tfb::fa_trace_set, "install / remove the flash-attention phase timeline buffer");
   m.def("fa_fwd", &tfb::fa_fwd, "tcgen05 causal flash attention forward");
   m.def("fa_bwd", &tfb::fa_bwd, "tcgen05 causal flash attention backward");
 }

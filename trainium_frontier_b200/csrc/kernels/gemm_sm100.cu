@@ -25,13 +25,12 @@
 //   EPI_RELU2_BWD D = bf16(bf16(alpha * acc) * 2 relu(R - tau))   (R = h)
 //   EPI_F32       D(f32) = alpha * acc (+ D if beta)        weight gradients (fp32, split-K via
 //                                                          vector atomics into the gradient)
-//   EPI_CE        lm_head + logit softcap + cross-entropy: z = bf16(acc) (stored only when
-//                 the gradient is wanted), y = S tanh(z / S); each tile adds its rows'
-//                 partial sum of exp(y - S) and the target's y to small per-row buffers, and
-//                 the warp that completes a 32-row slab (an arrival counter per slab)
-//                 writes the rows' losses and turns the slab's stored z into
-//                 dz = w (softmax(y) - onehot)(1 - t^2) in place, while it is still in L2 --
-//                 no separate pass over the [tokens, vocab] logits.
+//   EPI_CE        lm_head + logit softcap + cross-entropy statistics: z = bf16(acc) (stored
+//                 only when the gradient is wanted), y = S tanh(z / S); each tile writes its
+//                 rows' partial sums of exp(y - S) (one per tile column half) and the
+//                 target's y to small per-row buffers, so no pass over the [tokens, vocab]
+//                 logits is needed for the loss; ce_finish_kernel then adds the partials,
+//                 writes the losses and (with the gradient) turns z into dz in one pass.
 // Modes (the tensor-parallel collectives fused into the GEMM, over NVLink peer memory):
 //   MODE_PLAIN    the GEMM above.
 //   MODE_AG       all-gather -> GEMM.  A is the [M, K] gather buffer of which every rank
@@ -120,7 +119,6 @@ struct GemmArgs {
   float ce_S;              // softcap
   float* ce_part;          // [M][2 * tiles_n] partial sums of exp(y - S)
   float* ce_yc;            // [M] target's capped logit
-  int* ce_cnt;             // [ceil(M / 32)] arrival counters per 32-row slab, zero between launches
   float* ce_loss;          // [M] w * (S + log(sum) - y_c), 0 for ignored targets
   int ce_write_dz;         // store z and rewrite it as dz
   TpArgs tp;
@@ -292,57 +290,6 @@ __device__ __noinline__ void split_finish(const GemmArgs& a, int mb, int nb, int
   }
   __syncwarp();
   if (lane == 0) a.fin_cnt[slot] = 0;
-}
-
-// The warp that completes a 32-row slab of the lm_head GEMM (EPI_CE): every tile of the
-// slab has added its partial sums and (if the gradient is wanted) stored z.  One row at a
-// time: total, loss, and dz over the row's stored z (L2-resident reads, 16-byte vectors).
-__device__ __noinline__ void ce_finish(const GemmArgs& a, int slab, int lane) {
-  const int parts = 2 * a.tiles_n;
-  const float S = a.ce_S, invS = 1.f / S;
-#pragma unroll 1
-  for (int rr = 0; rr < 32; ++rr) {
-    const int row = slab * 32 + rr;
-    if (row >= a.M) break;
-    float tot = 0.f;
-    for (int k = lane; k < parts; k += 32) tot += __ldcg(a.ce_part + (long long)row * parts + k);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
-    const long long ti = (long long)(row / a.ce_T) * a.ce_tgt_ld + row % a.ce_T;
-    const long long cls = a.ce_tgt_i64 ? reinterpret_cast<const long long*>(a.ce_tgt)[ti]
-                                       : (long long)reinterpret_cast<const int*>(a.ce_tgt)[ti];
-    const bool valid = cls >= 0 && cls < a.ce_V;
-    const float wgt = valid ? (a.ce_roww ? a.ce_roww[row] : 1.f) : 0.f;
-    if (lane == 0) a.ce_loss[row] = valid ? wgt * (S + logf(tot) - __ldcg(a.ce_yc + row)) : 0.f;
-    if (!a.ce_write_dz) continue;
-    const float inv_tot = 1.f / tot;
-    __nv_bfloat16* zrow = reinterpret_cast<__nv_bfloat16*>(a.D) + (long long)row * a.ldd;
-    for (int j0 = lane * 8; j0 < a.N; j0 += 256) {
-      uint4 u = __ldcg(reinterpret_cast<const uint4*>(zrow + j0));
-      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float2 z = __bfloat1622float2(h[q]);
-        float o[2];
-        const float zz[2] = {z.x, z.y};
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int j = j0 + 2 * q + e;
-          if (j < a.ce_V && wgt != 0.f) {
-            const float th = tanhf(zz[e] * invS);
-            const float p = __expf(S * th - S) * inv_tot;
-            o[e] = wgt * (p - (j == cls ? 1.f : 0.f)) * (1.f - th * th);
-          } else {
-            o[e] = 0.f;
-          }
-        }
-        h[q] = __floats2bfloat162_rn(o[0], o[1]);
-      }
-      *reinterpret_cast<uint4*>(zrow + j0) = u;
-    }
-  }
-  __syncwarp();
-  if (lane == 0) a.ce_cnt[slab] = 0;  // clean for the next launch
 }
 
 template <int MODE>
@@ -1017,25 +964,7 @@ __global__ void __launch_bounds__(ModeThreads<MODE>::value, 1)
         __syncwarp();
         tc_fence_before();
         release_acc(acc);
-        if constexpr (EPI == EPI_CE) {
-          // Publish this warp's stores (TMA, async proxy; complete after the wait above) and
-          // partials, count them for its 32-row slab (two column halves per tile), and the
-          // warp that completes the slab finishes its rows.  No wait on any other warp.
-          if (lane == 0) fence_proxy_async_global();
-          __threadfence();
-          __syncwarp();
-          const int slab = mb * 4 + q;
-          int last = 0;
-          if (lane == 0) {
-            __threadfence();
-            last = atomicAdd(args.ce_cnt + slab, 1) == 2 * args.tiles_n - 1;
-          }
-          last = __shfl_sync(0xffffffffu, last, 0);
-          if (last) {
-            __threadfence();
-            ce_finish(args, slab, lane);
-          }
-        }
+
       } else {
         const bool row_ok = row < args.M;
 #pragma unroll 1
@@ -1456,7 +1385,6 @@ struct CeEpi {
   float S = 15.f;
   float* part = nullptr;
   float* yc = nullptr;
-  int* cnt = nullptr;
   float* loss = nullptr;
   int write_dz = 1;
 };
@@ -1555,7 +1483,7 @@ static void gemm_bf16_impl(torch::Tensor A, bool a_mn, torch::Tensor B, bool b_m
     TORCH_CHECK(a.tma_store && bn == 256 && !a_mn && !b_mn && nb == 1 && a.R == nullptr && ce.tgt != nullptr,
                 "CE epilogue: 2-D K-major operands, bf16 TMA-store output, 256-wide tiles");
     a.ce_tgt = ce.tgt; a.ce_tgt_i64 = ce.tgt_i64; a.ce_T = ce.T; a.ce_tgt_ld = ce.tgt_ld; a.ce_roww = ce.roww;
-    a.ce_V = ce.V; a.ce_S = ce.S; a.ce_part = ce.part; a.ce_yc = ce.yc; a.ce_cnt = ce.cnt; a.ce_loss = ce.loss;
+    a.ce_V = ce.V; a.ce_S = ce.S; a.ce_part = ce.part; a.ce_yc = ce.yc; a.ce_loss = ce.loss;
     a.ce_write_dz = ce.write_dz;
   }
   a.rope_cos = rope.cos; a.rope_sin = rope.sin; a.rope_T = rope.T; a.rope_cols = rope.cols;
@@ -1610,17 +1538,67 @@ void gemm_rope(torch::Tensor A, torch::Tensor B, torch::Tensor D, torch::Tensor 
                  c10::nullopt, 1.0, r);
 }
 
+// Row pass after the EPI_CE GEMM: one warp per row adds the row's partial sums, writes
+// its loss w (S + log sum - y_c) and, with the gradient, rewrites the stored z as
+// dz = w (exp(y - S) / sum - [j == c]) (1 - tanh(z / S)^2), 16-byte vectors.
+__global__ void ce_finish_kernel(const __nv_bfloat16* __restrict__ zin, __nv_bfloat16* __restrict__ zout, long long ldz,
+                                 int M, int N, int V, float S, const float* __restrict__ part, int parts,
+                                 const float* __restrict__ yc, const void* __restrict__ tgt, int tgt_i64, int T,
+                                 long long tgt_ld, const float* __restrict__ roww, float* __restrict__ loss,
+                                 int write_dz) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const float invS = 1.f / S;
+  float tot = 0.f;
+  for (int k = lane; k < parts; k += 32) tot += part[(long long)row * parts + k];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+  const long long ti = (long long)(row / T) * tgt_ld + row % T;
+  const long long cls = tgt_i64 ? reinterpret_cast<const long long*>(tgt)[ti] : (long long)reinterpret_cast<const int*>(tgt)[ti];
+  const bool valid = cls >= 0 && cls < V;
+  const float wgt = valid ? (roww ? roww[row] : 1.f) : 0.f;
+  if (lane == 0) loss[row] = valid ? wgt * (S + logf(tot) - yc[row]) : 0.f;
+  if (!write_dz) return;
+  const float inv_tot = 1.f / tot;
+  const __nv_bfloat16* zr = zin + (long long)row * ldz;
+  __nv_bfloat16* zw = zout + (long long)row * ldz;
+  for (int j0 = lane * 8; j0 < N; j0 += 256) {
+    uint4 u = *reinterpret_cast<const uint4*>(zr + j0);
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 z = __bfloat1622float2(h[q]);
+      const float zz[2] = {z.x, z.y};
+      float o[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int j = j0 + 2 * q + e;
+        if (j < V && wgt != 0.f) {
+          const float th = tanhf(zz[e] * invS);
+          const float p = __expf(S * th - S) * inv_tot;
+          o[e] = wgt * (p - (j == cls ? 1.f : 0.f)) * (1.f - th * th);
+        } else {
+          o[e] = 0.f;
+        }
+      }
+      h[q] = __floats2bfloat162_rn(o[0], o[1]);
+    }
+    *reinterpret_cast<uint4*>(zw + j0) = u;
+  }
+}
+
 // lm_head GEMM with the softcapped cross-entropy in the epilogue (EPI_CE).
 //   A = x [M, K] bf16, B = W [N, K] bf16 (N = padded vocab, a multiple of 256, >= V);
 //   tgt [B, T] int64 / int32 (row m = b * T + t; < 0 or >= V ignored); roww fp32 [M] or none;
-//   part fp32 [M * 2 * ceil(N / 256)], yc fp32 [M], cnt int32 [ceil(M / 32)] zeroed once
-//   (left zeroed), loss fp32 [M] <- w * (S + log sum_j exp(y_j - S) - y_c).
+//   part fp32 [M * 2 * ceil(N / 256)], yc fp32 [M] (scratch); loss fp32 [M] <-
+//   w * (S + log sum_j exp(y_j - S) - y_c).
 //   With write_dz, D [M, N] bf16 receives dz = w (softmax(y) - onehot)(1 - tanh^2) (scale 1;
 //   the mean's 1 / denominator goes into the backward GEMMs' alpha); without, D is not
 //   touched and may be any bf16 tensor.
 void gemm_ce(torch::Tensor A, torch::Tensor B, torch::Tensor D, torch::Tensor tgt, int64_t T,
              c10::optional<torch::Tensor> roww, int64_t V, double S, torch::Tensor part, torch::Tensor yc,
-             torch::Tensor cnt, torch::Tensor loss, bool write_dz, torch::Tensor err) {
+             torch::Tensor loss, bool write_dz, torch::Tensor err) {
   TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && D.dim() == 2, "2-D operands");
   const int64_t M = A.size(0), K = A.size(1), N = B.size(0);
   TORCH_CHECK(B.size(1) == K && N % 256 == 0 && V > 0 && V <= N, "N: padded vocab (multiple of 256) >= V");
@@ -1631,7 +1609,6 @@ void gemm_ce(torch::Tensor A, torch::Tensor B, torch::Tensor D, torch::Tensor tg
   TORCH_CHECK(part.scalar_type() == at::kFloat && part.numel() >= M * 2 * tiles_n, "part fp32 [M * 2 * tiles_n]");
   TORCH_CHECK(yc.scalar_type() == at::kFloat && yc.numel() >= M, "yc fp32 [M]");
   TORCH_CHECK(loss.scalar_type() == at::kFloat && loss.numel() >= M && loss.is_contiguous(), "loss fp32 [M]");
-  TORCH_CHECK(cnt.scalar_type() == at::kInt && cnt.numel() >= 4 * ((M + 127) / 128), "cnt int32 [4 * ceil(M / 128)]");
   if (write_dz) TORCH_CHECK(D.size(0) >= M && D.size(1) >= N, "D [M, N]");
   CeEpi c;
   c.tgt = tgt.data_ptr(); c.tgt_i64 = tgt.scalar_type() == at::kLong; c.T = (int)T; c.tgt_ld = tgt.stride(0);
@@ -1640,9 +1617,14 @@ void gemm_ce(torch::Tensor A, torch::Tensor B, torch::Tensor D, torch::Tensor tg
     c.roww = roww->data_ptr<float>();
   }
   c.V = (int)V; c.S = (float)S; c.part = part.data_ptr<float>(); c.yc = yc.data_ptr<float>();
-  c.cnt = cnt.data_ptr<int>(); c.loss = loss.data_ptr<float>(); c.write_dz = write_dz ? 1 : 0;
+  c.loss = loss.data_ptr<float>(); c.write_dz = write_dz ? 1 : 0;
   gemm_bf16_impl(A, false, B, false, M, N, K, D, EPI_CE, 1.0, 0.0, c10::nullopt, c10::nullopt, 0.0, 1, 256, err,
                  c10::nullopt, 1.0, RopeEpi{}, c);
+  auto* z = reinterpret_cast<__nv_bfloat16*>(D.data_ptr());
+  ce_finish_kernel<<<(unsigned)((M + 7) / 8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      z, z, D.stride(0), (int)M, (int)N, (int)V, (float)S, c.part, (int)(2 * tiles_n), c.yc, c.tgt, c.tgt_i64, c.T,
+      c.tgt_ld, c.roww, c.loss, c.write_dz);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 // Few-row GEMM (decode): out[M, N] bf16 = x[M, K] W[N, K]^T (+ R | relu^2), K split over the

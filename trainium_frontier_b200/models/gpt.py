@@ -568,7 +568,7 @@ class GPT(nn.Module):
     def _ngram_lookup(self, key: str, ids: torch.Tensor, dtype: torch.dtype, raw: dict | None = None,
                       idx: torch.Tensor | None = None) -> torch.Tensor:
         table = self.ngram_embeds[key].weight
-        if idx is not None and table.is_cuda:
+        if idx is not None and table.is_cuda and not ops.oracle_active():
             # hash + gather in one kernel (the ids computed above are the same rows)
             order = 2 if key[0] == "b" else 3
             p = _ngram_primes(int(key[1:]))

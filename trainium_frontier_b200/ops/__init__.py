@@ -5,18 +5,42 @@ Every op has two implementations selected by the device of its inputs:
   extension is required there and its absence raises.
 * CPU tensors  -> the fp32 PyTorch oracle in ``ops.reference`` (reference op order),
   which is also what the GPU numerics tests compare against.
+
+``oracle_mode()`` routes CUDA tensors through the oracle as well (library GEMMs, SDPA,
+eager elementwise ops in the compute dtype): the bf16 library comparator of the
+benchmark runs the same model and engine that way.  It is a measurement switch, never
+the training path.
 """
 from __future__ import annotations
 
+import contextlib
 import os
 
 import torch
 
 from . import reference as ref
 
+_ORACLE = [False]
+
+
+@contextlib.contextmanager
+def oracle_mode(on: bool = True):
+    """Within the block, every op (and the optimizer's kernel paths) uses the PyTorch
+    oracle on any device."""
+    prev = _ORACLE[0]
+    _ORACLE[0] = bool(on)
+    try:
+        yield
+    finally:
+        _ORACLE[0] = prev
+
+
+def oracle_active() -> bool:
+    return _ORACLE[0]
+
 
 def _cuda(t: torch.Tensor) -> bool:
-    return t.is_cuda
+    return t.is_cuda and not _ORACLE[0]
 
 
 def norm(x: torch.Tensor) -> torch.Tensor:

@@ -28,6 +28,7 @@ from . import gemm
 from ._ext import C
 
 BF16 = torch.bfloat16
+_EMBED_DETERMINISTIC = __import__("os").environ.get("TFB_EMBED_GRAD_ATOMIC", "0") != "1"
 
 
 # --------------------------------------------------------------------------- helpers
@@ -136,7 +137,12 @@ class EmbedNormFn(Function):
         gb = _2d(dout.contiguous()) if dout is not None else None
         if gacc is None and gb is None:
             return None, None
-        C().embed_norm_bwd(idx32, wte.detach(), rstd, gacc, gb, grad_buf(wte))
+        if _EMBED_DETERMINISTIC and wte.shape[0] <= 8192 and wte.shape[1] <= 2048:
+            # sorted segmented sums: the same bits every run (TFB_EMBED_GRAD_ATOMIC=1: the
+            # one-pass scatter with fp32 atomics)
+            C().embed_grad_det(idx32, wte.detach(), rstd, gacc, gb, grad_buf(wte))
+        else:
+            C().embed_norm_bwd(idx32, wte.detach(), rstd, gacc, gb, grad_buf(wte))
         holder.buf = None
         return None, None
 
@@ -385,24 +391,10 @@ class QKVRopeAttnFn(Function):
 
 
 # --------------------------------------------------------------------------- lm_head + CE
-_CE_CNT: dict[int, torch.Tensor] = {}
-
-
-def _ce_counters(dev: torch.device, M: int) -> torch.Tensor:
-    """Per-32-row-slab arrival counters of the CE GEMM epilogue: zeroed once, and every
-    launch leaves them zero again."""
-    idx = dev.index if dev.index is not None else torch.cuda.current_device()
-    need = 4 * ((M + 127) // 128)
-    t = _CE_CNT.get(idx)
-    if t is None or t.numel() < need:
-        t = torch.zeros(need, dtype=torch.int32, device=dev)
-        _CE_CNT[idx] = t
-    return t
-
-
 def _lm_head_ce(x2, wb, targets, softcap: float, vocab: int, row_weight, write_dz: bool):
-    """One lm_head GEMM with softcap + cross-entropy in its epilogue (``gemm_ce``): returns
-    the per-row losses and the [M, Vpad] bf16 buffer holding dz (when ``write_dz``)."""
+    """The lm_head GEMM with the softcap + cross-entropy statistics in its epilogue and one
+    row pass after it (``gemm_ce``): returns the per-row losses and the [M, Vpad] bf16
+    buffer holding dz (when ``write_dz``)."""
     M = x2.shape[0]
     Vp = wb.shape[0]
     tg = targets if targets.dim() == 2 else targets.view(1, -1)
@@ -414,21 +406,25 @@ def _lm_head_ce(x2, wb, targets, softcap: float, vocab: int, row_weight, write_d
     yc = torch.empty(M, dtype=torch.float32, device=x2.device)
     loss_rows = torch.empty(M, dtype=torch.float32, device=x2.device)
     rw = None if row_weight is None else row_weight.reshape(-1).float().contiguous()
-    C().gemm_ce(x2, wb, dz, tg, tg.shape[1], rw, int(vocab), float(softcap), part, yc,
-                _ce_counters(x2.device, M), loss_rows, bool(write_dz), gemm.err_word(x2.device))
+    C().gemm_ce(x2, wb, dz, tg, tg.shape[1], rw, int(vocab), float(softcap), part, yc, loss_rows,
+                bool(write_dz), gemm.err_word(x2.device))
     return loss_rows, dz, tg
 
 
 def _ce_fusable(x2, wb) -> bool:
-    return wb.shape[0] % 256 == 0 and x2.shape[1] % 8 == 0
+    """The CE statistics ride in the lm_head GEMM's epilogue (TFB_CE_FUSED=0: the GEMM
+    stores logits and the two-pass row kernel computes the loss and dlogits)."""
+    import os
+    return wb.shape[0] % 256 == 0 and x2.shape[1] % 8 == 0 and os.environ.get("TFB_CE_FUSED", "1") != "0"
 
 
 class LMHeadSoftcapCEFn(Function):
     """loss = CE(S tanh(x W^T / S)[:, :V], targets), forward and dlogits in one GEMM.
 
-    The lm_head GEMM's epilogue computes the softcap, the per-row partial sums and the
-    target logit; the warp completing each 32-row slab writes the losses and turns the
-    slab's logits into dlogits (bf16, in place) while they are still in L2.
+    The lm_head GEMM's epilogue computes the softcap, the per-row partial sums of the
+    softmax denominator and the target logit while it stores the bf16 logits; one row
+    pass then writes the losses and turns the logits into dlogits in place (one read and
+    one write of the [tokens, vocab] buffer instead of the former two reads and a write).
     ``row_weight`` (fp32 per token, or None) gives the byte-weighted mean; targets < 0
     are ignored.  The upstream gradient scalar is applied on the device inside the two
     backward GEMMs."""

@@ -54,6 +54,7 @@ def newton_schulz_gpu(x: torch.Tensor, steps: int) -> torch.Tensor:
 
 
 def newton_schulz(x: torch.Tensor, steps: int) -> torch.Tensor:
-    if x.is_cuda and x.dtype == torch.bfloat16:
+    from . import oracle_active
+    if x.is_cuda and x.dtype == torch.bfloat16 and not oracle_active():
         return newton_schulz_gpu(x, steps)
     return newton_schulz_reference(x, steps)

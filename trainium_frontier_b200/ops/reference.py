@@ -33,6 +33,11 @@ def embed_norm(idx: torch.Tensor, wte: torch.Tensor, dtype: torch.dtype) -> torc
 
 
 def mix_norm(x, x0, resid_lambda, x0_lambda):
+    """xm = resid_lambda x + x0_lambda x0 in x's dtype (the shape-[1] fp32 lambdas are cast
+    first, so a bf16 residual stream stays bf16 as in the fused kernel; for fp32 inputs this
+    is the reference's expression unchanged)."""
+    if resid_lambda.dtype != x.dtype:
+        resid_lambda, x0_lambda = resid_lambda.to(x.dtype), x0_lambda.to(x.dtype)
     xm = resid_lambda * x + x0_lambda * x0
     return xm, norm(xm)
 

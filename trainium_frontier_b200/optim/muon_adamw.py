@@ -166,7 +166,8 @@ class MuonAdamW(torch.optim.Optimizer):
         lr = self._device_scalar(group, "lr", group["lr"], params[0])
         beta1, beta2 = group["betas"]
         wd = group["weight_decay"]
-        if params[0].is_cuda and all(p.dtype == torch.float32 for p in params):
+        from ..ops import oracle_active
+        if params[0].is_cuda and all(p.dtype == torch.float32 for p in params) and not oracle_active():
             from ..ops.optim_kernels import adamw_multi
             adamw_multi(params, grads, exp_avgs, exp_avg_sqs, lr, beta1, beta2, group["eps"], wd,
                         bias1, bias2, cautious=group.get("cautious_wd", False))
@@ -276,7 +277,8 @@ class MuonAdamW(torch.optim.Optimizer):
             if not inplace:
                 w = torch.stack([p.detach() for p in sub])
             sl = slice(i0, i1)
-            if inplace and to_bf16 and not self.muon_lr_fp32 and torch.is_tensor(one_b2_t):
+            from ..ops import oracle_active
+            if inplace and to_bf16 and not self.muon_lr_fp32 and torch.is_tensor(one_b2_t) and not oracle_active():
                 from ..ops.optim_kernels import muon_owner_update, muon_stack_fusable
                 mb_s = state["momentum_buffer"][sl]
                 if muon_stack_fusable(g, mb_s, mom_t, lr_t) and w.dtype == torch.float32 and w.is_contiguous():

@@ -132,6 +132,9 @@ class DistMuon:
         self.state: dict[int, dict] = {}
         self.clip_coef = None
         self.sumsq = torch.zeros(1, dtype=torch.float32, device=dev)
+        # optional phase timeline: a list that receives (name, CUDA event) pairs recorded on
+        # the main stream at the phase boundaries of finish_grad_sync and step
+        self.timeline = None
         self.goff = []
         off = 0
         for p in self.plans:
@@ -174,6 +177,12 @@ class DistMuon:
     def begin_step(self) -> None:
         self.sumsq.zero_()
 
+    def mark(self, name: str) -> None:
+        if self.timeline is not None:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self.timeline.append((name, e))
+
     # ------------------------------------------------------------------ grads
     def _bucket_view(self, b: int) -> torch.Tensor:
         s, e = self.engine.layout.dist_bucket_range[b]
@@ -209,6 +218,7 @@ class DistMuon:
 
     def finish_grad_sync(self) -> None:
         lay = self.engine.layout
+        self.mark("sync:start")
         for b in range(len(self.plans)):
             self._launch_rs(b)
         rs, re_ = lay.rest_range
@@ -227,6 +237,7 @@ class DistMuon:
         self.rest_work = None
         if self.comm is not None:
             torch.cuda.current_stream(self.device).wait_stream(self.comm)
+        self.mark("sync:reduce-scatter tail + rest all-reduce")
         # global norm of the averaged gradient
         clip = self.engine.cfg.grad_clip
         self.clip_coef = None
@@ -243,6 +254,7 @@ class DistMuon:
             coef = torch.clamp(clip / (total + 1e-6), max=1.0)
             rest.mul_(coef)
             self.clip_coef = coef
+        self.mark("sync:clip (norm all-reduce)")
 
     # ------------------------------------------------------------------ step
     def _owned_runs(self, b: int):
@@ -405,11 +417,13 @@ def _step_fused(self, update_adamw: bool = True) -> None:
     bucket-b work), the gather + apply of bucket b runs on the comm stream while the main
     stream goes on with the Newton-Schulz of bucket b+1."""
     opt = self.opt
+    self.mark("opt:start")
     for g in opt.param_groups:
         if g["kind"] == "adamw" and update_adamw:
             opt._adamw_step(g)
         elif g["kind"] == "rmsprop" and update_adamw:
             opt._rmsprop_step(g)
+    self.mark("opt:adamw")
     # scalars of every group (lr*ratio, lr*ratio*wd, momentum, ...) staged once for the
     # owner kernels and the apply kernel
     for g in opt.param_groups:
@@ -434,8 +448,11 @@ def _step_fused(self, update_adamw: bool = True) -> None:
         with torch.cuda.stream(side):
             self._barrier()  # every owner's bucket-b updates are in its update buffer
             self.C.symm_ag_apply(self.upd_peers, self._runs_table(b))
+    self.mark("opt:owner Newton-Schulz + NorMuon (gather-apply overlapped)")
     main.wait_stream(side)
+    self.mark("opt:gather-apply tail")
     self._barrier()  # peers are done reading this rank's gradient and update buffers
+    self.mark("opt:final barrier")
 
 
 def _runs_table(self, b: int) -> torch.Tensor:

@@ -19,7 +19,8 @@ Times, with CUDA events on the launching stream and the max over ranks:
 
 Roofline per path = max(bytes crossing NVLink into this GPU / link bandwidth, local HBM
 bytes / HBM bandwidth), with the link bandwidth the measured 770 GB/s per direction peer
-copy (nominal 900) and the HBM bandwidth from the measured peaks file when present.
+copy and the HBM bandwidth from the measured peaks file when present; the fraction
+against NVLink 5's nominal 900 GB/s per direction is reported beside it.
 The default size is the d20 model's Muon matrices (20 x (4 x 1280^2 + 2 x 1280 x 5120)).
 
 Reference counterparts: its only gradient collectives, the per-parameter and flat-buffer
@@ -34,7 +35,8 @@ import os
 import torch
 import torch.distributed as dist
 
-LINK_GBS = 770.0
+LINK_GBS = 770.0          # measured peer-copy bandwidth per direction on this B200 pool
+LINK_GBS_NOMINAL = 900.0  # NVLink 5 per direction per GPU (context: fraction also reported against it)
 
 
 def _peaks() -> dict:
@@ -157,8 +159,10 @@ def bench_tp(args) -> None:
     }
     for k, (t, tn, fl, link) in rows.items():
         roof = max(fl / (peak * 1e9), link / (LINK_GBS * 1e6))
+        roof_nom = max(fl / (peak * 1e9), link / (LINK_GBS_NOMINAL * 1e6))
         out[k] = {"ms": t, "nccl_plus_gemm_ms": tn, "tflops": fl / t / 1e9, "roofline_ms": roof,
-                  "frac_of_roofline": roof / t, "nvlink_bytes_in": link}
+                  "frac_of_roofline": roof / t, "frac_of_roofline_nominal_900": roof_nom / t,
+                  "nvlink_bytes_in": link}
     if rank == 0:
         print(json.dumps(out))
         if args.json:
@@ -239,7 +243,9 @@ def main() -> None:
     ag_hbm = n * (4 + 4 + 2) + seg * 2            # master read+write, bf16 cache write, own update
     for name, t, link, hbm in (("fused_rs", t_rs, rs_link, rs_hbm), ("fused_ag_apply", t_ag, ag_link, ag_hbm)):
         roof_ms = max(link / (LINK_GBS * 1e9), hbm / (peaks["hbm_gbs"] * 1e9)) * 1e3
+        roof_nom = max(link / (LINK_GBS_NOMINAL * 1e9), hbm / (peaks["hbm_gbs"] * 1e9)) * 1e3
         res[name] = {"ms": t, "roofline_ms": roof_ms, "frac_of_roofline": roof_ms / t,
+                     "frac_of_roofline_nominal_900": roof_nom / t,
                      "nvlink_bytes_in": link, "hbm_bytes": hbm, "link_gbs_achieved": link / t / 1e6}
     res["nccl_reduce_scatter"] = {"ms": t_rs_nccl, "frac_of_roofline": res["fused_rs"]["roofline_ms"] / t_rs_nccl}
     res["nccl_all_gather_no_apply"] = {"ms": t_ag_nccl}

@@ -154,17 +154,62 @@ def one_kernel(case: str, dev):
     torch.cuda.synchronize(dev)
 
 
+def trace_fa_bwd(dev, B: int = 16, T: int = 2048, H: int = 10, D: int = 128) -> dict:
+    """Phase timeline (SM clock cycles) of CTA 0 of the pipelined flash-attention backward:
+    per query tile, when each role reached each phase (see ``fa_stamp`` in
+    csrc/kernels/attention_sm100.cu).  For reading where the pipeline waits."""
+    from ..ops._ext import C
+    from ..ops.flash_attention import flash_bwd, flash_fwd
+    M = B * T
+    q, k, v, do = (torch.randn(M, H * D, device=dev, dtype=torch.bfloat16) for _ in range(4))
+    o, lse = flash_fwd(q, k, v, B, T, H, D, D ** -0.5, True)
+    for _ in range(3):
+        flash_bwd(q, k, v, o, do, lse, B, T, H, D, D ** -0.5, True)
+    buf = torch.zeros(4 * 64 * 8, dtype=torch.int64, device=dev)
+    C().fa_trace_set(buf)
+    flash_bwd(q, k, v, o, do, lse, B, T, H, D, D ** -0.5, True)
+    torch.cuda.synchronize(dev)
+    C().fa_trace_set(None)
+    t = buf.view(4, 64, 8).cpu()
+    t0 = int(t[t > 0].min())
+    names = {0: ["dP issued", "P ready", "S(i+1) issued", "dS ready", "loop top", "dO landed", "dQ drained"],
+             1: ["loop top", "S ready", "P computed", "P/dS tile free", "P stored", "dP+dV done", "dS stored"],
+             2: ["loop top", "dQ ready", "dQ read"], 3: ["Q issued", "dO issued"]}
+    roles = ["mma", "softmax", "drain", "producer"]
+    out = {}
+    for r, role in enumerate(roles):
+        rows = []
+        for i in range(64):
+            ev = [int(x) for x in t[r, i, :len(names[r])]]
+            if not any(ev):
+                continue
+            rows.append({n: (e - t0 if e else None) for n, e in zip(names[r], ev)})
+        out[role] = rows
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("what", nargs="?", default="gemm")
     ap.add_argument("--one", default="", help="run one small case: gemm | gemm_relu2 | gemm_dw | fa_fwd | fa_bwd")
     ap.add_argument("--json", default="")
+    ap.add_argument("--trace", action="store_true", help="print the flash backward phase timeline of CTA 0")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     peaks = measured_peaks()
     if args.one:
         one_kernel(args.one, dev)
+        return
+    if args.trace:
+        tl = trace_fa_bwd(dev)
+        for role, rows in tl.items():
+            print(f"== {role}")
+            for i, r in enumerate(rows):
+                print(f"  {i:3d} " + "  ".join(f"{k}={v}" for k, v in r.items()))
+        if args.json:
+            with open(args.json, "w") as f:
+                json.dump(tl, f, indent=1)
         return
     out = {"peaks": peaks}
     if args.what in ("gemm", "all"):
