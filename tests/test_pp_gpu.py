@@ -9,10 +9,7 @@ import pytest
 import torch
 
 pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs"),
-              pytest.mark.skipif(os.environ.get("TFB_PP_CUDA", "0") != "1",
-                                 reason="pipeline parallelism on GPUs is gated off (TFB_PP_CUDA=1 runs it): "
-                                        "its first stage crashed on the host in its first backward GEMM")]
+              pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")]
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 

@@ -538,13 +538,18 @@ __global__ void __launch_bounds__(320, 1)
       if (ok) ok = issue_s(0, 0) && issue_s(1, 0);
       if (ok) umma_commit(&kv_empty[0]);  // K_0 read by both tiles
       for (int j = 0; j < n1 && ok; ++j) {
+        fa_stamp(a.trace, 0, j, 0);
         if (j + 1 < n0 && !issue_s(0, j + 1)) { ok = false; break; }
+        fa_stamp(a.trace, 0, j, 1);
         if (j < n0 && !issue_pv(0, j)) { ok = false; break; }
+        fa_stamp(a.trace, 0, j, 2);
         if (j + 1 < n1) {
           if (!issue_s(1, j + 1)) { ok = false; break; }
           umma_commit(&kv_empty[(2 * (j + 1)) % NS]);  // K_{j+1} done
         }
+        fa_stamp(a.trace, 0, j, 3);
         if (!issue_pv(1, j)) { ok = false; break; }
+        fa_stamp(a.trace, 0, j, 4);
         umma_commit(&kv_empty[(2 * j + 1) % NS]);      // V_j done
       }
       if (!ok) {
@@ -567,8 +572,11 @@ __global__ void __launch_bounds__(320, 1)
     const float c = a.scale_log2;
     float m_run = -INFINITY, l = 0.f;
     bool ok = true;
+    const bool stamp = (warp == 2 || warp == 6) && lane == 0;
     for (int j = 0; j < n_t; ++j) {
+      if (stamp) fa_stamp(a.trace, 1 + t, j, 0);
       if (!mbar_wait_warp(&s_full[t], j & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      if (stamp) fa_stamp(a.trace, 1 + t, j, 1);
       tc_fence_after();
       float x[128];
       {
@@ -615,6 +623,7 @@ __global__ void __launch_bounds__(320, 1)
       }
       const float2 s01 = __fadd2_rn(__fadd2_rn(sm4[0], sm4[1]), __fadd2_rn(sm4[2], sm4[3]));
       l = l * alpha + (s01.x + s01.y);
+      if (stamp) fa_stamp(a.trace, 1 + t, j, 2);
       // The shared P tile is free once the P V MMA of the other tile's previous turn has
       // completed (P0(j) follows P1(j-1), P1(j) follows P0(j)); by then this tile's own
       // previous P V has completed too (issued earlier), so O_t can be rescaled.
@@ -623,6 +632,7 @@ __global__ void __launch_bounds__(320, 1)
         const int oj = t == 0 ? j - 1 : (j < n0 ? j : j - 1);
         if (oj >= 0 && !mbar_wait_warp(&pv_done[ot], oj & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
       }
+      if (stamp) fa_stamp(a.trace, 1 + t, j, 3);
       if (j >= 1) {
         tc_fence_after();
         if (__any_sync(0xffffffffu, grow)) {
@@ -646,6 +656,7 @@ __global__ void __launch_bounds__(320, 1)
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full[t]);
+      if (stamp) fa_stamp(a.trace, 1 + t, j, 4);
     }
     if (ok && mbar_wait_warp(&pv_done[t], (n_t - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) {
       tc_fence_after();
@@ -1110,9 +1121,10 @@ __global__ void __launch_bounds__(448, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    // Order per query tile i: dP^T(i), dV(i), S^T(i+1), dK(i), dQ(i) -- S^T(i+1) goes out
+    // Order per query tile i: dP^T(i), dV(i), S^T(i+1), dQ(i), dK(i) -- S^T(i+1) goes out
     // before the wait for dS(i), so the softmax warps find it done when they move on and
-    // compute P(i+1) while the tensor core runs dK(i) and dQ(i).
+    // compute P(i+1) while the tensor core runs dQ(i) and dK(i); dQ(i) goes first so that
+    // its drain frees R1 for dP^T(i+1) while dK(i) still runs.
     if (lane == 0) {
       bool ok = mbar_wait(bar_kv, 0, abort_flag, a.err, ERR_TIMEOUT_MMA);
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), pd_addr = smem_u32(sPD), do_addr = smem_u32(sDO);
@@ -1155,13 +1167,14 @@ __global__ void __launch_bounds__(448, 1)
         if (!mbar_wait(ds_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
         fa_stamp(a.trace, 0, it, 3);
         tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)  // dK += dS^T Q
-          umma_bf16(tDK, desc_kmajor(pd_addr, kk), desc_mnmajor(q_addr, kk), IDESC_KV, (it > 0 || kk > 0) ? 1u : 0u);
+        // dQ first: its drain (and so the next dP^T, which reuses R1) starts while dK runs
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)  // dQ = dS K  (into R1: dP^T has been read)
           umma_bf16(tR1, desc_mnmajor(pd_addr, kk), desc_mnmajor(k_addr, kk), IDESC_Q, kk > 0 ? 1u : 0u);
         umma_commit(dq_full);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // dK += dS^T Q
+          umma_bf16(tDK, desc_kmajor(pd_addr, kk), desc_mnmajor(q_addr, kk), IDESC_KV, (it > 0 || kk > 0) ? 1u : 0u);
         umma_commit(pds_free);
         umma_commit(&q_empty[bf]);
       }

@@ -119,25 +119,50 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_split_kernel(
   const __nv_bfloat16* kb = kc + (long long)b * cache_bstride + h * D + 4 * lane;
   const __nv_bfloat16* vb = vc + (long long)b * cache_bstride + h * D + 4 * lane;
   float m = -INFINITY, l = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int k = k0 + warp; k < k1; k += NW) {
-    const uint2 ku = *reinterpret_cast<const uint2*>(kb + (long long)k * cache_ld);
-    const uint2 vu = *reinterpret_cast<const uint2*>(vb + (long long)k * cache_ld);
-    const float2 k01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ku.x));
-    const float2 k23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ku.y));
-    float sdot = qs[0] * k01.x + qs[1] * k01.y + qs[2] * k23.x + qs[3] * k23.y;
+  // Eight keys per warp iteration, every K and V load of the eight issued before any
+  // math, so each warp keeps 4 KB in flight (one key at a time left HBM latency-bound).
+  constexpr int KPI = 8;
+  for (int kb0 = k0 + warp * KPI; kb0 < k1; kb0 += NW * KPI) {
+    uint2 ku[KPI], vu[KPI];
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) sdot += __shfl_xor_sync(0xffffffffu, sdot, off);
-    const float m_new = fmaxf(m, sdot);
-    const float corr = __expf(m - m_new);
-    const float p = __expf(sdot - m_new);
-    const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vu.x));
-    const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vu.y));
-    l = l * corr + p;
-    o[0] = o[0] * corr + p * v01.x;
-    o[1] = o[1] * corr + p * v01.y;
-    o[2] = o[2] * corr + p * v23.x;
-    o[3] = o[3] * corr + p * v23.y;
-    m = m_new;
+    for (int j = 0; j < KPI; ++j) {
+      const int k = min(kb0 + j, k1 - 1);  // clamped: past-the-end keys are masked below
+      ku[j] = *reinterpret_cast<const uint2*>(kb + (long long)k * cache_ld);
+      vu[j] = *reinterpret_cast<const uint2*>(vb + (long long)k * cache_ld);
+    }
+    float sd[KPI];
+#pragma unroll
+    for (int j = 0; j < KPI; ++j) {
+      const float2 k01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ku[j].x));
+      const float2 k23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ku[j].y));
+      sd[j] = qs[0] * k01.x + qs[1] * k01.y + qs[2] * k23.x + qs[3] * k23.y;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+      for (int j = 0; j < KPI; ++j) sd[j] += __shfl_xor_sync(0xffffffffu, sd[j], off);
+    float mx = m;
+#pragma unroll
+    for (int j = 0; j < KPI; ++j) {
+      if (kb0 + j >= k1) sd[j] = -INFINITY;
+      mx = fmaxf(mx, sd[j]);
+    }
+    const float corr = __expf(m - mx);
+    l *= corr;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] *= corr;
+#pragma unroll
+    for (int j = 0; j < KPI; ++j) {
+      const float p = __expf(sd[j] - mx);
+      const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vu[j].x));
+      const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vu[j].y));
+      l += p;
+      o[0] += p * v01.x;
+      o[1] += p * v01.y;
+      o[2] += p * v23.x;
+      o[3] += p * v23.y;
+    }
+    m = mx;
   }
   // combine the warps of this CTA
   if (lane == 0) {

@@ -186,6 +186,7 @@ class Generator:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 self._decode_step()
+            self.graph = g
             self._rewind(T)
             for _ in range(n):
                 g.replay()
@@ -193,6 +194,15 @@ class Generator:
             for _ in range(n):
                 self._decode_step()
         return self.tokens
+
+    @torch.no_grad()
+    def replay_steps(self, n: int, T: int) -> None:
+        """Replays the captured decode step n times from position T (after ``generate``),
+        for timing and profiling one step in isolation."""
+        assert self.graph is not None, "generate(..., use_graph=True) captures the step first"
+        self._rewind(T)
+        for _ in range(n):
+            self.graph.replay()
 
     def _rewind(self, T):
         self.counters.copy_(torch.tensor([T, T + 1], dtype=torch.int32, device=self.dev))

@@ -23,7 +23,6 @@ pipeline strategy of the build plan.
 """
 from __future__ import annotations
 
-import os
 
 import torch
 import torch.distributed as dist
@@ -76,12 +75,6 @@ def pipeline_forward_backward(model, ppc: PipelineContext, batches, loss_scale: 
     (zero elsewhere).  Gradients accumulate into the parameters' ``.grad``."""
     from .. import ops
     dev = model.get_device()
-    if dev.type == "cuda" and os.environ.get("TFB_PP_CUDA", "0") != "1":
-        raise RuntimeError(
-            "pipeline parallelism runs on CPU (gloo) ranks only for now: on two B200s the first "
-            "stage's process died with SIGSEGV (host side) in its first backward GEMM call, and "
-            "the fix (binding the device context before tensor-map encodes) has not yet run on "
-            "GPUs; set TFB_PP_CUDA=1 to run it on GPUs anyway")
     dt = model.compute_dtype
     n = len(batches)
     inv = 1.0 / n

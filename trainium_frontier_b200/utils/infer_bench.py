@@ -199,3 +199,44 @@ def _decode(model, dev, rank: int, world: int) -> dict:
             "ms_per_token_step": ms / DEC_NEW, "batch": DEC_BATCH, "prompt": DEC_PROMPT, "new_tokens": DEC_NEW,
             "e2e_tokens_per_s": DEC_BATCH * DEC_NEW / wall, "generated_shape": list(host.shape),
             "note": "device time covers prefill + 256 greedy steps (graph replays); e2e adds the prompt H2D and the token D2H"}
+
+
+def profile_decode(steps: int = 3) -> dict:
+    """KV-cache decode of a random-init d20 model (batch 32, 512-token prompts): after a
+    warm-up generate (which captures the step's CUDA graph), ``steps`` graph replays are
+    bracketed by cudaProfilerStart / Stop (``ncu --profile-from-start off`` sees only them)
+    and timed with CUDA events."""
+    from ..config import preset
+    from ..inference.generate import Generator
+    from ..models.gpt import GPT
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = preset("d20", seed=1234)
+    torch.manual_seed(cfg.seed)
+    m = GPT(cfg.model_config(), cfg)
+    m.init_weights()
+    m = m.to(dev)
+    m.set_compute_dtype(torch.bfloat16)
+    m.eval()
+    g = torch.Generator().manual_seed(5)
+    prompts = torch.randint(1, 8192, (DEC_BATCH, DEC_PROMPT), generator=g).to(dev)
+    gen = Generator(m, DEC_BATCH, DEC_PROMPT + DEC_NEW + 128)
+    gen.generate(prompts, 8)
+    gen.replay_steps(8, DEC_PROMPT + 64)   # warm replays at a mid-run cache length
+    torch.cuda.synchronize(dev)
+    a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.cudart().cudaProfilerStart()
+    a.record()
+    gen.replay_steps(steps, DEC_PROMPT + 64)
+    e.record()
+    torch.cuda.synchronize(dev)
+    torch.cuda.cudart().cudaProfilerStop()
+    ms = a.elapsed_time(e) / steps
+    return {"ms_per_step": ms, "batch": DEC_BATCH, "cache_len": DEC_PROMPT + 64, "steps": steps}
+
+
+if __name__ == "__main__":
+    import json
+    import sys
+    if "--decode-profile" in sys.argv:
+        print(json.dumps(profile_decode()))

@@ -154,6 +154,35 @@ def one_kernel(case: str, dev):
     torch.cuda.synchronize(dev)
 
 
+def trace_fa_fwd(dev, B: int = 16, T: int = 2048, H: int = 10, D: int = 128) -> dict:
+    """Phase timeline (SM clock cycles) of CTA 0 of the two-tile flash-attention forward."""
+    from ..ops._ext import C
+    from ..ops.flash_attention import flash_fwd
+    M = B * T
+    q, k, v = (torch.randn(M, H * D, device=dev, dtype=torch.bfloat16) for _ in range(3))
+    for _ in range(3):
+        flash_fwd(q, k, v, B, T, H, D, D ** -0.5, True)
+    buf = torch.zeros(4 * 64 * 8, dtype=torch.int64, device=dev)
+    C().fa_trace_set(buf)
+    flash_fwd(q, k, v, B, T, H, D, D ** -0.5, True)
+    torch.cuda.synchronize(dev)
+    C().fa_trace_set(None)
+    t = buf.view(4, 64, 8).cpu()
+    t0 = int(t[t > 0].min())
+    names = {0: ["step top", "S0(j+1) issued", "PV0(j) issued", "S1(j+1) issued", "PV1(j) issued"],
+             1: ["loop top", "S ready", "P computed", "P tile free", "P stored"],
+             2: ["loop top", "S ready", "P computed", "P tile free", "P stored"]}
+    out = {}
+    for r, role in enumerate(["mma", "softmax0", "softmax1"]):
+        rows = []
+        for i in range(64):
+            ev = [int(x) for x in t[r, i, :len(names[r])]]
+            if any(ev):
+                rows.append({n: (e - t0 if e else None) for n, e in zip(names[r], ev)})
+        out[role] = rows
+    return out
+
+
 def trace_fa_bwd(dev, B: int = 16, T: int = 2048, H: int = 10, D: int = 128) -> dict:
     """Phase timeline (SM clock cycles) of CTA 0 of the pipelined flash-attention backward:
     per query tile, when each role reached each phase (see ``fa_stamp`` in
@@ -202,11 +231,12 @@ def main():
         one_kernel(args.one, dev)
         return
     if args.trace:
-        tl = trace_fa_bwd(dev)
-        for role, rows in tl.items():
-            print(f"== {role}")
-            for i, r in enumerate(rows):
-                print(f"  {i:3d} " + "  ".join(f"{k}={v}" for k, v in r.items()))
+        tl = {"backward": trace_fa_bwd(dev), "forward": trace_fa_fwd(dev)}
+        for kern, roles in tl.items():
+            for role, rows in roles.items():
+                print(f"== {kern} {role}")
+                for i, r in enumerate(rows):
+                    print(f"  {i:3d} " + "  ".join(f"{k}={v}" for k, v in r.items()))
         if args.json:
             with open(args.json, "w") as f:
                 json.dump(tl, f, indent=1)
