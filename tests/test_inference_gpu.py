@@ -55,21 +55,28 @@ def test_decode_attention_kernel(cuda_device):
     assert (out.float().view(B, H, D) - ref.squeeze(2)).abs().max().item() < 2e-2
 
 
-def test_split_decode_attention_kernel(cuda_device):
+@pytest.mark.parametrize("layout", ["token", "head"])
+def test_split_decode_attention_kernel(cuda_device, layout):
     """Cache length split over CTAs per (batch, head), partials combined by the last CTA;
-    repeated calls check that the arrival counters are left zeroed."""
+    repeated calls check that the arrival counters are left zeroed.  Token-major
+    [B, T, H*D] and head-major [B, H, T, D] caches."""
     from trainium_frontier_b200.ops._ext import C
     torch.manual_seed(1)
     B, Tm, H, D, splits = 3, 640, 4, 128, 5
     q = torch.randn(B, H * D, device=cuda_device).to(torch.bfloat16)
     kc = torch.randn(B, Tm, H * D, device=cuda_device).to(torch.bfloat16)
     vc = torch.randn(B, Tm, H * D, device=cuda_device).to(torch.bfloat16)
+    if layout == "head":
+        kcs = kc.view(B, Tm, H, D).transpose(1, 2).contiguous()
+        vcs = vc.view(B, Tm, H, D).transpose(1, 2).contiguous()
+    else:
+        kcs, vcs = kc, vc
     ws = torch.zeros(B * H * splits * (D + 4), device=cuda_device)
     cnt = torch.zeros(B * H, dtype=torch.int32, device=cuda_device)
-    for L in (1, 77, 513, 640):
+    for L, pdl in ((1, False), (77, True), (513, False), (640, True)):
         ln = torch.tensor([L], dtype=torch.int32, device=cuda_device)
         out = torch.empty(B, H * D, dtype=torch.bfloat16, device=cuda_device)
-        C().decode_attn_split(q, kc, vc, ln, H, D, D ** -0.5, out, ws, cnt, splits)
+        C().decode_attn_split(q, kcs, vcs, ln, H, D, D ** -0.5, out, ws, cnt, splits, pdl)
         qf = q.float().view(B, H, 1, D)
         kf = kc[:, :L].float().view(B, L, H, D).transpose(1, 2)
         vf = vc[:, :L].float().view(B, L, H, D).transpose(1, 2)

@@ -48,7 +48,13 @@ void rope_norm_fwd(torch::Tensor buf, int64_t head0, int64_t nheads, int64_t D, 
 void decode_attn(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache, torch::Tensor len, int64_t H,
                  int64_t D, double scale, torch::Tensor out);
 void decode_attn_split(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache, torch::Tensor len, int64_t H,
-                       int64_t D, double scale, torch::Tensor out, torch::Tensor ws, torch::Tensor cnt, int64_t splits);
+                       int64_t D, double scale, torch::Tensor out, torch::Tensor ws, torch::Tensor cnt, int64_t splits,
+                       bool pdl);
+void decode_gemm(torch::Tensor X, torch::Tensor W, torch::Tensor out, int64_t epi, bool row_norm,
+                 c10::optional<torch::Tensor> R, c10::optional<torch::Tensor> X0, c10::optional<torch::Tensor> lam_r,
+                 c10::optional<torch::Tensor> lam_0, double tau, c10::optional<torch::Tensor> cos,
+                 c10::optional<torch::Tensor> sin, c10::optional<torch::Tensor> pos, c10::optional<torch::Tensor> kc,
+                 c10::optional<torch::Tensor> vc, int64_t H, int64_t split, bool pdl, torch::Tensor err);
 void kv_append(torch::Tensor k, torch::Tensor v, torch::Tensor kcache, torch::Tensor vcache, torch::Tensor pos);
 void step_advance(torch::Tensor counters);
 void argmax_rows(torch::Tensor logits, int64_t V, torch::Tensor idx_out, c10::optional<torch::Tensor> tokens,
@@ -97,6 +103,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("pos_t") = py::none());
   m.def("decode_attn", &tfb::decode_attn);
   m.def("decode_attn_split", &tfb::decode_attn_split);
+  m.def("decode_gemm", &tfb::decode_gemm);
   m.def("kv_append", &tfb::kv_append);
   m.def("step_advance", &tfb::step_advance);
   m.def("argmax_rows", &tfb::argmax_rows);

@@ -85,91 +85,124 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
 }
 
 // decode_attn_split: the same attention with the cache length split over `splits` CTAs per
-// (batch, head) so the KV stream is read by many SMs at once.  Each CTA scores a chunk of
-// keys (one key per warp at a time, lanes over the head dimension, 256-byte rows),
-// keeps an unnormalised partial output plus (max, sum) in a workspace, and the last CTA
-// of its (batch, head) -- an arrival counter -- combines the partials, writes the row and
-// re-zeroes the counter (no memset between graph replays).
+// (batch, head) so the KV stream is read by many SMs at once.  The cache is addressed by
+// strides (batch, head, token), so it may be stored token-major ([B, T_max, H*D], the
+// projection buffer's layout) or head-major ([B, H, T_max, D], each (batch, head) one
+// contiguous stream).  Each warp scores two keys per load (a half-warp per key, 16 bytes
+// per lane: dims 8l .. 8l+7), eight keys per iteration with every K and V load of the
+// eight issued before any math; a CTA keeps an unnormalised partial output plus (max, sum)
+// in a workspace, and the last CTA of its (batch, head) -- an arrival counter -- combines
+// the partials in split order, writes the row and re-zeroes the counter (no memset
+// between graph replays).
 template <int D>
 __global__ void __launch_bounds__(kDecThreads) decode_attn_split_kernel(
     const __nv_bfloat16* __restrict__ q, long long ldq, const __nv_bfloat16* __restrict__ kc,
-    const __nv_bfloat16* __restrict__ vc, long long cache_ld, long long cache_bstride, const int* __restrict__ len_ptr,
-    int len_max, __nv_bfloat16* __restrict__ out, long long ldo, int H, float scale, int splits,
-    float* __restrict__ ws, int* __restrict__ cnt) {
-  static_assert(D == 128, "lanes cover 4 dims each");
+    const __nv_bfloat16* __restrict__ vc, long long cs_b, long long cs_h, long long cs_t,
+    const int* __restrict__ len_ptr, int len_max, __nv_bfloat16* __restrict__ out, long long ldo, int H, float scale,
+    int splits, float* __restrict__ ws, int* __restrict__ cnt) {
+  static_assert(D == 128, "a half-warp covers the 128 dims, 8 per lane");
   // partial record = D outputs + (max, sum), padded to a multiple of 4 floats so every
   // record starts on a 16-byte boundary (float4 stores / loads)
   constexpr int kPartStride = D + 4;
   constexpr int NW = kDecThreads / 32;
+  constexpr int KPH = 4;            // keys per half-warp per iteration
+  constexpr int KPW = 2 * KPH;      // keys per warp per iteration
   __shared__ float s_m[NW], s_l[NW];
   __shared__ __align__(16) float s_o[NW][D];
   __shared__ int s_last;
   const int bh = blockIdx.x / splits, sp = blockIdx.x % splits;
   const int b = bh / H, h = bh % H;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int half = lane >> 4, hl = lane & 15;
+  // launched as a programmatic dependent of the QKV projection: wait for its q / cache
+  // writes, and let the next projection start streaming its weights meanwhile
+  griddep_wait();
+  griddep_launch_dependents();
   int L = *len_ptr;
   L = L < 1 ? 1 : (L > len_max ? len_max : L);
   const int chunk = (L + splits - 1) / splits;
   const int k0 = sp * chunk, k1 = min(L, k0 + chunk);
-  // q slice of this lane (dims 4*lane .. 4*lane+3), pre-scaled
-  const uint2 qu = *reinterpret_cast<const uint2*>(q + (long long)b * ldq + h * D + 4 * lane);
-  const float2 q01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qu.x));
-  const float2 q23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qu.y));
-  const float qs[4] = {q01.x * scale, q01.y * scale, q23.x * scale, q23.y * scale};
-  const __nv_bfloat16* kb = kc + (long long)b * cache_bstride + h * D + 4 * lane;
-  const __nv_bfloat16* vb = vc + (long long)b * cache_bstride + h * D + 4 * lane;
-  float m = -INFINITY, l = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
-  // Eight keys per warp iteration, every K and V load of the eight issued before any
-  // math, so each warp keeps 4 KB in flight (one key at a time left HBM latency-bound).
-  constexpr int KPI = 8;
-  for (int kb0 = k0 + warp * KPI; kb0 < k1; kb0 += NW * KPI) {
-    uint2 ku[KPI], vu[KPI];
+  // q slice of this lane (dims 8*hl .. 8*hl+7), pre-scaled
+  float qs[8];
+  {
+    const uint4 qu = *reinterpret_cast<const uint4*>(q + (long long)b * ldq + h * D + 8 * hl);
+    const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&qu);
 #pragma unroll
-    for (int j = 0; j < KPI; ++j) {
-      const int k = min(kb0 + j, k1 - 1);  // clamped: past-the-end keys are masked below
-      ku[j] = *reinterpret_cast<const uint2*>(kb + (long long)k * cache_ld);
-      vu[j] = *reinterpret_cast<const uint2*>(vb + (long long)k * cache_ld);
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(q2[i]);
+      qs[2 * i] = f.x * scale;
+      qs[2 * i + 1] = f.y * scale;
     }
-    float sd[KPI];
+  }
+  const __nv_bfloat16* kb = kc + (long long)b * cs_b + (long long)h * cs_h + 8 * hl;
+  const __nv_bfloat16* vb = vc + (long long)b * cs_b + (long long)h * cs_h + 8 * hl;
+  float m = -INFINITY, l = 0.f, o[8];
 #pragma unroll
-    for (int j = 0; j < KPI; ++j) {
-      const float2 k01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ku[j].x));
-      const float2 k23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ku[j].y));
-      sd[j] = qs[0] * k01.x + qs[1] * k01.y + qs[2] * k23.x + qs[3] * k23.y;
+  for (int i = 0; i < 8; ++i) o[i] = 0.f;
+  for (int kw = k0 + warp * KPW; kw < k1; kw += NW * KPW) {
+    // this half-warp's keys: kw + half + 2 * j
+    uint4 ku[KPH], vu[KPH];
+#pragma unroll
+    for (int j = 0; j < KPH; ++j) {
+      const int k = min(kw + half + 2 * j, k1 - 1);  // clamped: past-the-end keys are masked below
+      ku[j] = *reinterpret_cast<const uint4*>(kb + (long long)k * cs_t);
+      vu[j] = *reinterpret_cast<const uint4*>(vb + (long long)k * cs_t);
+    }
+    float sd[KPH];
+#pragma unroll
+    for (int j = 0; j < KPH; ++j) {
+      const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&ku[j]);
+      float acc = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(k2[i]);
+        acc += qs[2 * i] * f.x + qs[2 * i + 1] * f.y;
+      }
+      sd[j] = acc;
     }
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1)
+    for (int off = 8; off > 0; off >>= 1)
 #pragma unroll
-      for (int j = 0; j < KPI; ++j) sd[j] += __shfl_xor_sync(0xffffffffu, sd[j], off);
-    float mx = m;
+      for (int j = 0; j < KPH; ++j) sd[j] += __shfl_xor_sync(0xffffffffu, sd[j], off);
+    float mx = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < KPI; ++j) {
-      if (kb0 + j >= k1) sd[j] = -INFINITY;
+    for (int j = 0; j < KPH; ++j) {
+      if (kw + half + 2 * j >= k1) sd[j] = -INFINITY;
       mx = fmaxf(mx, sd[j]);
     }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));  // one running max per warp
+    mx = fmaxf(mx, m);
     const float corr = __expf(m - mx);
     l *= corr;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) o[i] *= corr;
+    for (int i = 0; i < 8; ++i) o[i] *= corr;
 #pragma unroll
-    for (int j = 0; j < KPI; ++j) {
+    for (int j = 0; j < KPH; ++j) {
       const float p = __expf(sd[j] - mx);
-      const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vu[j].x));
-      const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vu[j].y));
+      const __nv_bfloat162* v2 = reinterpret_cast<const __nv_bfloat162*>(&vu[j]);
       l += p;
-      o[0] += p * v01.x;
-      o[1] += p * v01.y;
-      o[2] += p * v23.x;
-      o[3] += p * v23.y;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(v2[i]);
+        o[2 * i] += p * f.x;
+        o[2 * i + 1] += p * f.y;
+      }
     }
     m = mx;
   }
+  // the two half-warps share the running max: add their sums and outputs
+  l += __shfl_xor_sync(0xffffffffu, l, 16);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] += __shfl_xor_sync(0xffffffffu, o[i], 16);
   // combine the warps of this CTA
   if (lane == 0) {
     s_m[warp] = m;
     s_l[warp] = l;
   }
-  *reinterpret_cast<float4*>(&s_o[warp][4 * lane]) = make_float4(o[0], o[1], o[2], o[3]);
+  if (half == 0) {
+    *reinterpret_cast<float4*>(&s_o[warp][8 * hl]) = make_float4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<float4*>(&s_o[warp][8 * hl + 4]) = make_float4(o[4], o[5], o[6], o[7]);
+  }
   __syncthreads();
   float* part = ws + ((long long)bh * splits + sp) * kPartStride;
   if (warp == 0) {
@@ -250,9 +283,32 @@ __global__ void argmax_rows_kernel(const __nv_bfloat16* __restrict__ logits, lon
   const __nv_bfloat16* row = logits + (long long)b * ld;
   float best = -INFINITY;
   int arg = 0;
-  for (int j = threadIdx.x; j < V; j += blockDim.x) {
-    const float v = __bfloat162float(row[j]);
-    if (v > best) { best = v; arg = j; }
+  const bool vec = (V % 8) == 0 && (ld % 8) == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0;
+  if (vec) {  // 16-byte loads, all of a thread's loads issued before the compares
+    constexpr int U = 4;
+    for (int base = threadIdx.x * 8; base < V; base += blockDim.x * 8 * U) {
+      uint4 u[U];
+#pragma unroll
+      for (int k = 0; k < U; ++k) {
+        const int j = base + k * blockDim.x * 8;
+        u[k] = j < V ? *reinterpret_cast<const uint4*>(row + j) : make_uint4(0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u);
+      }
+#pragma unroll
+      for (int k = 0; k < U; ++k) {
+        const int j = base + k * blockDim.x * 8;
+        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u[k]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float v = __bfloat162float(e[i]);
+          if (v > best) { best = v; arg = j + i; }
+        }
+      }
+    }
+  } else {
+    for (int j = threadIdx.x; j < V; j += blockDim.x) {
+      const float v = __bfloat162float(row[j]);
+      if (v > best) { best = v; arg = j; }
+    }
   }
   __shared__ float sv[32];
   __shared__ int si[32];
@@ -327,32 +383,62 @@ void argmax_rows(torch::Tensor logits, int64_t V, torch::Tensor idx_out, c10::op
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// Strides (batch, head, token) of a KV cache stored token-major [B, T_max, H*D] or
+// head-major [B, H, T_max, D]; `tmax` receives T_max.
+void cache_strides(const torch::Tensor& c, int64_t H, int64_t D, long long& sb, long long& sh, long long& st,
+                          int& tmax) {
+  if (c.dim() == 3) {
+    TORCH_CHECK(c.size(2) == H * D && c.stride(2) == 1, "token-major cache [B, T_max, H*D]");
+    sb = c.stride(0); st = c.stride(1); sh = D; tmax = (int)c.size(1);
+  } else {
+    TORCH_CHECK(c.dim() == 4 && c.size(1) == H && c.size(3) == D && c.stride(3) == 1,
+                "head-major cache [B, H, T_max, D]");
+    sb = c.stride(0); sh = c.stride(1); st = c.stride(2); tmax = (int)c.size(2);
+  }
+}
+
 // ws: fp32 >= B*H*splits*(D+4), 16-byte aligned; cnt: int32 >= B*H, zero before the
 // first call (left zeroed).
 void decode_attn_split(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache, torch::Tensor len, int64_t H,
                        int64_t D, double scale, torch::Tensor out, torch::Tensor ws, torch::Tensor cnt,
-                       int64_t splits) {
+                       int64_t splits, bool pdl) {
   TORCH_CHECK(D == 128, "split decode attention supports head_dim 128");
-  TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kBFloat16 && kcache.dim() == 3 && vcache.dim() == 3, "inputs");
-  TORCH_CHECK(kcache.stride(2) == 1 && vcache.stride(2) == 1 && kcache.strides() == vcache.strides(), "cache layout");
-  auto a8 = [](const torch::Tensor& t) { return (reinterpret_cast<uintptr_t>(t.data_ptr()) & 7) == 0; };
-  TORCH_CHECK((q.stride(0) * 2) % 8 == 0 && (kcache.stride(1) * 2) % 8 == 0 && (kcache.stride(0) * 2) % 8 == 0 &&
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kBFloat16 && kcache.scalar_type() == at::kBFloat16 &&
+                  vcache.scalar_type() == at::kBFloat16, "bf16 inputs");
+  TORCH_CHECK(kcache.sizes() == vcache.sizes() && kcache.strides() == vcache.strides(), "k / v caches alike");
+  long long sb, sh, st;
+  int tmax;
+  cache_strides(kcache, H, D, sb, sh, st, tmax);
+  auto a16 = [](const torch::Tensor& t) { return (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0; };
+  TORCH_CHECK((q.stride(0) * 2) % 16 == 0 && (sb * 2) % 16 == 0 && (sh * 2) % 16 == 0 && (st * 2) % 16 == 0 &&
                   (out.stride(0) * 2) % 8 == 0 && out.stride(1) == 1 && q.stride(1) == 1,
-              "8-byte aligned rows (4 bf16 per lane)");
-  TORCH_CHECK(a8(q) && a8(kcache) && a8(vcache) && a8(out), "8-byte aligned bases");
+              "16-byte aligned q / cache rows (8 bf16 per lane), 8-byte aligned output rows");
+  TORCH_CHECK(a16(q) && a16(kcache) && a16(vcache) && (reinterpret_cast<uintptr_t>(out.data_ptr()) & 7) == 0,
+              "aligned bases");
   const int64_t B = q.size(0);
+  TORCH_CHECK(kcache.size(0) >= B, "cache batch");
   TORCH_CHECK(splits >= 1 && splits <= 64, "splits 1..64");
   TORCH_CHECK(ws.scalar_type() == at::kFloat && ws.numel() >= B * H * splits * (D + 4), "workspace size");
   TORCH_CHECK((reinterpret_cast<uintptr_t>(ws.data_ptr()) & 15) == 0, "workspace must be 16-byte aligned");
   TORCH_CHECK(cnt.scalar_type() == at::kInt && cnt.numel() >= B * H, "counter size");
   c10::cuda::CUDAGuard guard(q.device());
-  decode_attn_split_kernel<128><<<(unsigned)(B * H * splits), kDecThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0),
-      reinterpret_cast<const __nv_bfloat16*>(kcache.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(vcache.data_ptr()),
-      kcache.stride(1), kcache.stride(0), len.data_ptr<int>(), (int)kcache.size(1),
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), (int)H, (float)scale, (int)splits,
-      ws.data_ptr<float>(), cnt.data_ptr<int>());
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3((unsigned)(B * H * splits), 1, 1);
+  cfg.blockDim = dim3(kDecThreads, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = at::cuda::getCurrentCUDAStream();
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, decode_attn_split_kernel<128>,
+                                    reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), (long long)q.stride(0),
+                                    reinterpret_cast<const __nv_bfloat16*>(kcache.data_ptr()),
+                                    reinterpret_cast<const __nv_bfloat16*>(vcache.data_ptr()), sb, sh, st,
+                                    (const int*)len.data_ptr<int>(), tmax,
+                                    reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (long long)out.stride(0), (int)H,
+                                    (float)scale, (int)splits, ws.data_ptr<float>(), cnt.data_ptr<int>()));
 }
 
 }  // namespace tfb

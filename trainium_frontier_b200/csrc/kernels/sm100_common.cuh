@@ -277,6 +277,18 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start before the previous
+// kernel of its stream has finished; griddepcontrol.wait blocks the calling thread until
+// that kernel has completed and its memory is visible, so every thread that reads (or
+// overwrites) an earlier kernel's data calls it first.  launch_dependents lets the next
+// such kernel start launching once every CTA of this grid has signalled (or exited).
+// Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- CTA pairs (cta_group::2)
 // Two CTAs of a 2-CTA cluster share one tcgen05 tile: each holds half of A (its 128 rows)
 // and half of B in its own shared memory and its 128 accumulator lanes in its own TMEM;
@@ -317,6 +329,12 @@ __device__ __forceinline__ void tma_load_3d_pair(void* smem_dst, const CUtensorM
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(mbar_cluster), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
+}
+// 32-bit load from another CTA's shared memory (a shared::cluster address from mapa).
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
 }
 // Arrive (release, cluster scope) on an mbarrier of another CTA of the cluster.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t mbar_cluster) {

@@ -6,12 +6,23 @@
   GEMMs, RoPE+QK-norm, tcgen05 flash attention) in one pass; every layer's normalised
   keys and values land in a ``[B, T_max, H*D]`` cache (the projection buffer's own
   layout, so the copy is a strided row copy);
-* decode: one token per sequence per step -- mix+norm -> QKV GEMM -> RoPE+QK-norm at
-  the device-side position -> cache append -> single-query attention over the cache
-  -> projection + residual -> norm -> relu^2 MLP -> final norm -> lm_head -> greedy
-  argmax (argmax of the softcapped logits = argmax of the raw ones).  Position and
-  length live in device memory and the argmax feeds the next step's input in device
-  memory, so the whole step is captured once in a CUDA graph and replayed.
+* decode: one token per sequence per step, five launches per block through the
+  decode GEMM (``csrc/kernels/decode_gemm.cu``: swapped-operand tcgen05 tiles, split-K
+  over a thread-block cluster reduced in distributed shared memory, programmatic
+  dependent launch so each kernel's weight stream starts under the previous kernel):
+    1. QKV projection of the mixed residual with its RMS norm folded in (row scale),
+       RoPE + QK-norm at the device-side position, k / v rows written into the cache;
+    2. split single-query attention over the cache;
+    3. attention projection + residual;
+    4. MLP up-projection with the RMS norm folded in, relu^2;
+    5. MLP down-projection + residual, then the next block's residual mix
+       (lambda_r x + lambda_0 x0), so the next QKV projection reads it directly;
+  then the lm_head with the final norm folded in and a greedy argmax (argmax of the
+  softcapped logits = argmax of the raw ones).  Position and length live in device
+  memory and the argmax feeds the next step's input in device memory, so the whole step
+  is captured once in a CUDA graph and replayed.  Every buffer of the step is allocated
+  once, up front; the KV caches are head-major ([B, H, T_max, D]) so each (sequence,
+  head) of the decode attention streams one contiguous range.
 
 ``generate_reference`` recomputes the full forward for every new token; it is the
 oracle the cached path is tested against and the path for non-plain members.
@@ -25,6 +36,9 @@ import torch
 
 from ..ops import gemm
 from ..ops._ext import C, err_word
+
+# epilogues of the decode GEMM (csrc/kernels/decode_gemm.cu)
+DEC_PLAIN, DEC_RES, DEC_RELU2, DEC_MIX, DEC_QKV = 0, 1, 2, 3, 4
 from ..ops.flash_attention import flash_fwd, supported
 from ..ops.fused import w16
 
@@ -66,8 +80,13 @@ class Generator:
         L = cfg.n_layer
         dev = self.dev
         bf = torch.bfloat16
-        self.kc = [torch.zeros(self.B, self.Tmax, self.Cd, dtype=bf, device=dev) for _ in range(L)]
-        self.vc = [torch.zeros(self.B, self.Tmax, self.Cd, dtype=bf, device=dev) for _ in range(L)]
+        # head_dim 128 (the fused decode step): head-major caches [B, H, T_max, D], so each
+        # (sequence, head) of the decode attention reads one contiguous stream; otherwise
+        # the projection buffer's token-major layout [B, T_max, H*D]
+        self.fused_decode = self.D == 128 and self.B <= 128
+        shape = (self.B, self.H, self.Tmax, self.D) if self.fused_decode else (self.B, self.Tmax, self.Cd)
+        self.kc = [torch.zeros(shape, dtype=bf, device=dev) for _ in range(L)]
+        self.vc = [torch.zeros(shape, dtype=bf, device=dev) for _ in range(L)]
         self.counters = torch.zeros(2, dtype=torch.int32, device=dev)  # [position, cache length]
         self.idx = torch.zeros(self.B, 1, dtype=torch.int32, device=dev)
         self.graph = None
@@ -89,6 +108,18 @@ class Generator:
         cos, sin = model.cos, model.sin
         self.cos = cos.reshape(-1, cos.shape[-1]).to(bf).contiguous()
         self.sin = sin.reshape(-1, sin.shape[-1]).to(bf).contiguous()
+        # decode-step buffers (fixed addresses: the step is captured in a CUDA graph)
+        Bm, Cd = self.B, self.Cd
+        self.d_x0 = torch.empty(Bm, Cd, dtype=bf, device=dev)
+        self.d_xm = torch.empty(Bm, Cd, dtype=bf, device=dev)
+        self.d_h = torch.empty(Bm, Cd, dtype=bf, device=dev)
+        self.d_rstd = torch.empty(Bm, dtype=torch.float32, device=dev)
+        self.d_q = torch.empty(Bm, Cd, dtype=bf, device=dev)
+        self.d_y = torch.empty(Bm, Cd, dtype=bf, device=dev)
+        self.d_x = torch.empty(Bm, Cd, dtype=bf, device=dev)
+        self.d_act = torch.empty(Bm, self.wfc[0].shape[0], dtype=bf, device=dev)
+        self.d_xf = torch.empty(Bm, Cd, dtype=bf, device=dev)
+        self.d_logits = torch.empty(Bm, self.wlm.shape[0], dtype=bf, device=dev)
 
     # ------------------------------------------------------------------ prefill
     def _block_rows(self, i, x, x0, M, T, pos_t=None, prefill=True):
@@ -102,15 +133,19 @@ class Generator:
         C().rope_norm_fwd(qkv, 0, 2 * H, D, self.cos, self.sin, T, 0, None, qkn, pos_t)
         if prefill:
             B = M // T
-            self.kc[i][:B, :T].copy_(qkn[:, Cd:].view(B, T, Cd))
-            self.vc[i][:B, :T].copy_(qkv[:, 2 * Cd:].view(B, T, Cd))
+            if self.fused_decode:
+                self.kc[i][:B, :, :T].copy_(qkn[:, Cd:].view(B, T, H, D).transpose(1, 2))
+                self.vc[i][:B, :, :T].copy_(qkv[:, 2 * Cd:].view(B, T, H, D).transpose(1, 2))
+            else:
+                self.kc[i][:B, :T].copy_(qkn[:, Cd:].view(B, T, Cd))
+                self.vc[i][:B, :T].copy_(qkv[:, 2 * Cd:].view(B, T, Cd))
             y, _ = flash_fwd(qkn[:, :Cd], qkn[:, Cd:], qkv[:, 2 * Cd:], B, T, H, D, self.scale, True)
         else:
             C().kv_append(qkn[:, Cd:], qkv[:, 2 * Cd:], self.kc[i], self.vc[i], self.counters[0:1])
             y = torch.empty((M, Cd), dtype=torch.bfloat16, device=self.dev)
             if D == 128:   # cache length split over several CTAs per (batch, head)
                 C().decode_attn_split(qkn[:, :Cd], self.kc[i], self.vc[i], self.counters[1:2], H, D, self.scale, y,
-                                      self.att_ws, self.att_cnt, self.att_splits)
+                                      self.att_ws, self.att_cnt, self.att_splits, False)
             else:
                 C().decode_attn(qkn[:, :Cd], self.kc[i], self.vc[i], self.counters[1:2], H, D, self.scale, y)
         if prefill:
@@ -157,13 +192,47 @@ class Generator:
 
     # ------------------------------------------------------------------ decode
     def _decode_step(self):
-        x0 = self._embed(self.idx)
-        x = x0
-        for i in range(len(self.wqkv)):
-            x = self._block_rows(i, x, x0, self.B, 1, pos_t=self.counters[0:1], prefill=False)
-        logits = self._head(x)
+        if not self.fused_decode:
+            x0 = self._embed(self.idx)
+            x = x0
+            for i in range(len(self.wqkv)):
+                x = self._block_rows(i, x, x0, self.B, 1, pos_t=self.counters[0:1], prefill=False)
+            logits = self._head(x)
+        else:
+            logits = self._fused_step()
         C().argmax_rows(logits, self.V, self.idx, self.tokens, self.counters, self.start)
         C().step_advance(self.counters)
+
+    def _fused_step(self):
+        """One decode step of the plain member with head_dim 128 through the decode GEMM:
+        five launches per block (see the module docstring)."""
+        c = C()
+        err = err_word(self.dev)
+        x0, xm, q, y, x, act, xf = self.d_x0, self.d_xm, self.d_q, self.d_y, self.d_x, self.d_act, self.d_xf
+        c.embed_norm_fwd(self.idx, self.wte, x0, self.d_rstd)
+        lr, l0 = self.lam[0]
+        c.mix_norm_fwd(x0, x0, lr, l0, xm, self.d_h, self.d_rstd)   # block 0's mix: x = x0
+        pos, ln = self.counters[0:1], self.counters[1:2]
+        L = len(self.wqkv)
+        for i in range(L):
+            c.decode_gemm(xm, self.wqkv[i], q, DEC_QKV, True, None, None, None, None, 0.0, self.cos, self.sin,
+                          pos, self.kc[i], self.vc[i], self.H, 0, True, err)
+            c.decode_attn_split(q, self.kc[i], self.vc[i], ln, self.H, self.D, self.scale, y, self.att_ws,
+                                self.att_cnt, self.att_splits, True)
+            c.decode_gemm(y, self.wo[i], x, DEC_RES, False, xm, None, None, None, 0.0, None, None, None, None, None,
+                          0, 0, True, err)
+            c.decode_gemm(x, self.wfc[i], act, DEC_RELU2, True, None, None, None, None, float(self.tau), None, None,
+                          None, None, None, 0, 0, True, err)
+            if i + 1 < L:
+                nr, n0 = self.lam[i + 1]
+                c.decode_gemm(act, self.wp[i], xm, DEC_MIX, False, x, x0, nr, n0, 0.0, None, None, None, None, None,
+                              0, 0, True, err)
+            else:
+                c.decode_gemm(act, self.wp[i], xf, DEC_RES, False, x, None, None, None, 0.0, None, None, None, None,
+                              None, 0, 0, True, err)
+        c.decode_gemm(xf, self.wlm, self.d_logits, DEC_PLAIN, True, None, None, None, None, 0.0, None, None, None,
+                      None, None, 0, 0, True, err)
+        return self.d_logits
 
     @torch.no_grad()
     def generate(self, prompts: torch.Tensor, max_new_tokens: int, use_graph: bool = True) -> torch.Tensor:

@@ -239,4 +239,5 @@ if __name__ == "__main__":
     import json
     import sys
     if "--decode-profile" in sys.argv:
-        print(json.dumps(profile_decode()))
+        n = int(sys.argv[sys.argv.index("--steps") + 1]) if "--steps" in sys.argv else 3
+        print(json.dumps(profile_decode(n)))
