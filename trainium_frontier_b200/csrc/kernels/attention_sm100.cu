@@ -397,9 +397,17 @@ __device__ __forceinline__ float2 exp2_poly2(float2 v) {
   return make_float2(v.x < -126.f ? 0.f : rx, v.y < -126.f ? 0.f : ry);
 }
 
-constexpr int kFwd2Slots = 4;  // K / V ring depth
-constexpr size_t kFwd2Smem = 1024 + 2 * 32768 + kFwd2Slots * 32768 + 32768 + 24 * 8 + 16;
+constexpr int kFwd2Slots = 5;  // K / V ring depth
+constexpr size_t kFwd2Smem = 1024 + 2 * 32768 + kFwd2Slots * 32768 + 24 * 8 + 16;
 
+// Two 128-query tiles per CTA, K/V streamed through a 5-slot TMA ring; TMEM holds S_t and
+// O_t for both tiles (4 x 128 columns).  The softmax of tile t writes P_t (bf16) back into
+// the first 64 columns of S_t and the P V MMA reads it from TMEM as its A operand, so P
+// never goes through shared memory.  Since S_t(j+1) would overwrite P_t(j), the MMA warp
+// issues S_t(j+1) right after P_t(j) V_j (tcgen05 MMAs of one thread run in issue order);
+// the two tiles alternate, so the tensor pipe runs one tile's P V and next S while the
+// other tile's softmax runs.  The commit that signals S_t(j) also covers P_t(j-1) V_{j-1},
+// so the softmax may rescale O_t as soon as it sees S_t(j).
 __global__ void __launch_bounds__(320, 1)
     fa_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const FaArgs a) {
@@ -413,16 +421,14 @@ __global__ void __launch_bounds__(320, 1)
   constexpr int NS = kFwd2Slots;
   uint8_t* sQ = smem;                 // [2] tiles
   uint8_t* sKV = sQ + 2 * TILE;       // [NS] slots
-  uint8_t* sP = sKV + NS * TILE;      // one tile, used by the two softmax groups in turn
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + TILE);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + NS * TILE);
   uint64_t* bar_q = bars + 0;
   uint64_t* kv_full = bars + 1;          // [NS]
   uint64_t* kv_empty = bars + 1 + NS;    // [NS]
   uint64_t* s_full = bars + 1 + 2 * NS;  // [2]
-  uint64_t* s_free = s_full + 2;         // [2]
-  uint64_t* p_full = s_free + 2;         // [2]
-  uint64_t* pv_done = p_full + 2;        // [2]
-  uint64_t* drain = pv_done + 2;
+  uint64_t* p_full = s_full + 2;         // [2]
+  uint64_t* o_done = p_full + 2;         // [2]
+  uint64_t* drain = o_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -445,9 +451,8 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
-      mbar_init(&s_free[t], 128);
       mbar_init(&p_full[t], 128);
-      mbar_init(&pv_done[t], 1);
+      mbar_init(&o_done[t], 1);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -508,13 +513,11 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0) {
       bool ok = mbar_wait(bar_q, 0, abort_flag, a.err, ERR_TIMEOUT_MMA);
       const uint32_t q_addr[2] = {smem_u32(sQ), smem_u32(sQ + TILE)};
-      const uint32_t p_addr[2] = {smem_u32(sP), smem_u32(sP)};
       auto kv_wait = [&](int item) -> bool {
         return mbar_wait(&kv_full[item % NS], (item / NS) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA);
       };
       auto issue_s = [&](int t, int j) -> bool {
         if (!kv_wait(2 * j)) return false;
-        if (j >= 1 && !mbar_wait(&s_free[t], (j - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) return false;
         tc_fence_after();
         const uint32_t k_addr = smem_u32(sKV + ((2 * j) % NS) * TILE);
 #pragma unroll
@@ -529,26 +532,33 @@ __global__ void __launch_bounds__(320, 1)
         tc_fence_after();
         const uint32_t v_addr = smem_u32(sKV + ((2 * j + 1) % NS) * TILE);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_bf16(tmem + 256 + t * 128, desc_kmajor(p_addr[t], kk), desc_mnmajor(v_addr, kk), IDESC_O,
-                    (j > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&pv_done[t]);
+        for (int kk = 0; kk < 8; ++kk)  // P_t(j): 16 keys = 8 packed columns per MMA
+          umma_bf16_tmem_a(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, desc_mnmajor(v_addr, kk), IDESC_O,
+                           (j > 0 || kk > 0) ? 1u : 0u);
         return true;
       };
       if (ok) ok = issue_s(0, 0) && issue_s(1, 0);
       if (ok) umma_commit(&kv_empty[0]);  // K_0 read by both tiles
       for (int j = 0; j < n1 && ok; ++j) {
         fa_stamp(a.trace, 0, j, 0);
-        if (j + 1 < n0 && !issue_s(0, j + 1)) { ok = false; break; }
-        fa_stamp(a.trace, 0, j, 1);
-        if (j < n0 && !issue_pv(0, j)) { ok = false; break; }
-        fa_stamp(a.trace, 0, j, 2);
+        if (j < n0) {
+          if (!issue_pv(0, j)) { ok = false; break; }
+          fa_stamp(a.trace, 0, j, 1);
+          if (j + 1 < n0) {
+            if (!issue_s(0, j + 1)) { ok = false; break; }
+          } else {
+            umma_commit(&o_done[0]);
+          }
+          fa_stamp(a.trace, 0, j, 2);
+        }
+        if (!issue_pv(1, j)) { ok = false; break; }
+        fa_stamp(a.trace, 0, j, 3);
         if (j + 1 < n1) {
           if (!issue_s(1, j + 1)) { ok = false; break; }
-          umma_commit(&kv_empty[(2 * (j + 1)) % NS]);  // K_{j+1} done
+          umma_commit(&kv_empty[(2 * (j + 1)) % NS]);  // K_{j+1} read by both tiles
+        } else {
+          umma_commit(&o_done[1]);
         }
-        fa_stamp(a.trace, 0, j, 3);
-        if (!issue_pv(1, j)) { ok = false; break; }
         fa_stamp(a.trace, 0, j, 4);
         umma_commit(&kv_empty[(2 * j + 1) % NS]);      // V_j done
       }
@@ -588,8 +598,6 @@ __global__ void __launch_bounds__(320, 1)
         }
         tmem_ld_wait();
       }
-      tc_fence_before();
-      mbar_arrive(&s_free[t]);
       if (a.causal && j == qt) {  // diagonal tile: keys after this query row are masked
 #pragma unroll
         for (int i = 0; i < 128; ++i)
@@ -624,41 +632,30 @@ __global__ void __launch_bounds__(320, 1)
       const float2 s01 = __fadd2_rn(__fadd2_rn(sm4[0], sm4[1]), __fadd2_rn(sm4[2], sm4[3]));
       l = l * alpha + (s01.x + s01.y);
       if (stamp) fa_stamp(a.trace, 1 + t, j, 2);
-      // The shared P tile is free once the P V MMA of the other tile's previous turn has
-      // completed (P0(j) follows P1(j-1), P1(j) follows P0(j)); by then this tile's own
-      // previous P V has completed too (issued earlier), so O_t can be rescaled.
-      {
-        const int ot = t == 0 ? 1 : (j < n0 ? 0 : 1);
-        const int oj = t == 0 ? j - 1 : (j < n0 ? j : j - 1);
-        if (oj >= 0 && !mbar_wait_warp(&pv_done[ot], oj & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
-      }
-      if (stamp) fa_stamp(a.trace, 1 + t, j, 3);
-      if (j >= 1) {
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, grow)) {
+      // O_t is stable: the commit that signalled S_t(j) covered P_t(j-1) V_{j-1}
+      if (j >= 1 && __any_sync(0xffffffffu, grow)) {
 #pragma unroll 1
-          for (int cc = 0; cc < D / 32; ++cc) {
-            uint32_t o[32];
-            __syncwarp();
-            tmem_ld_32x32b_x32(tO + lane_off + cc * 32, o);
-            tmem_ld_wait();
+        for (int cc = 0; cc < D / 32; ++cc) {
+          uint32_t o[32];
+          __syncwarp();
+          tmem_ld_32x32b_x32(tO + lane_off + cc * 32, o);
+          tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st_32x32b_x32(tO + lane_off + cc * 32, o);
-          }
-          tmem_st_wait();
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st_32x32b_x32(tO + lane_off + cc * 32, o);
         }
       }
-#pragma unroll
-      for (int cc = 0; cc < 16; ++cc)
-        *reinterpret_cast<uint4*>(sP + (cc >> 3) * kPanel + sw128_chunk_offset(r, cc & 7)) =
-            make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
-      fence_proxy_async_smem();
+      if (stamp) fa_stamp(a.trace, 1 + t, j, 3);
+      // P_t(j) over the first 64 columns of S_t(j) (already in registers)
+      __syncwarp();
+      tmem_st_32x32b_x32(tS + lane_off, *reinterpret_cast<const uint32_t(*)[32]>(pk));
+      tmem_st_32x32b_x32(tS + lane_off + 32, *reinterpret_cast<const uint32_t(*)[32]>(pk + 32));
+      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[t]);
       if (stamp) fa_stamp(a.trace, 1 + t, j, 4);
     }
-    if (ok && mbar_wait_warp(&pv_done[t], (n_t - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) {
+    if (ok && mbar_wait_warp(&o_done[t], 0, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) {
       tc_fence_after();
       const float inv_l = 1.f / l;
       __nv_bfloat16* dst = a.O + (long long)(row0 + t * 128 + r) * a.ldo + h * D;

@@ -84,7 +84,20 @@ struct DecGemmArgs {
   long long cs_b, cs_h, cs_t;
   int Tmax;
   int* err;
+  unsigned long long* trace;  // optional phase timeline (globaltimer ns) of the first and last CTA
 };
+
+// Phase timeline (off unless a buffer is installed with decode_gemm_trace_set): the first
+// and the last CTA of the grid write %globaltimer at each phase into trace[slot * 16 + e].
+//   0 entry, 1 set-up done, 2 weight loads issued, 3 grid dependency resolved (producer),
+//   4 first stage landed (MMA), 5 last MMA issued, 6 sums of squares done, 7 MMAs complete
+//   (epilogue), 8 partial tile in shared memory, 9 first cluster barrier passed,
+//   10 rows reduced and stored, 11 second cluster barrier passed
+__device__ __forceinline__ void dg_stamp(unsigned long long* tr, int e) {
+  if (tr == nullptr) return;
+  const unsigned last = gridDim.x - 1;
+  if (blockIdx.x == 0 || blockIdx.x == last) tr[(blockIdx.x == 0 ? 0 : 16) + e] = globaltimer_ns();
+}
 
 __device__ __forceinline__ float dg_warp_sum(float v) {
 #pragma unroll
@@ -121,6 +134,7 @@ __global__ void __launch_bounds__(kDgThreads, 1)
   const int kb1 = (int)((long long)(crank + 1) * a.kb_total / S);
   const int nk = kb1 - kb0;
   const uint32_t tcols = (uint32_t)a.Mpad;  // 32, 64 or 128: a power of two >= 32
+  if (threadIdx.x == 0) dg_stamp(a.trace, 0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -142,6 +156,7 @@ __global__ void __launch_bounds__(kDgThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) dg_stamp(a.trace, 1);
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -155,7 +170,9 @@ __global__ void __launch_bounds__(kDgThreads, 1)
         out_valid |= 1u << i;
         tma_load_3d(sW + i * kDgWBytes, &tmW, &full[i], (kb0 + i) * kDgBK, nb * kDgBM, 0);
       }
+      dg_stamp(a.trace, 2);
       griddep_wait();
+      dg_stamp(a.trace, 3);
       for (int i = 0; i < pre; ++i) tma_load_3d(sX + i * XB, &tmX, &full[i], (kb0 + i) * kDgBK, 0, 0);
       for (int i = pre; i < nk; ++i) {
         const int s = i % STAGES;
@@ -195,6 +212,7 @@ __global__ void __launch_bounds__(kDgThreads, 1)
           ok = false;
           break;
         }
+        if (i == 0) dg_stamp(a.trace, 4);
         tc_fence_after();
         const uint32_t wa = smem_u32(sW + s * kDgWBytes), xa = smem_u32(sX + s * XB);
 #pragma unroll
@@ -205,6 +223,7 @@ __global__ void __launch_bounds__(kDgThreads, 1)
       }
       // arrives once every MMA issued above has completed (at once if there were none)
       umma_commit(done);
+      dg_stamp(a.trace, 5);
       if (!ok) *abort_flag = 1;
     }
   } else {
@@ -243,7 +262,9 @@ __global__ void __launch_bounds__(kDgThreads, 1)
         }
       }
     }
+    if (threadIdx.x == 64) dg_stamp(a.trace, 6);
     const bool ok = mbar_wait_warp(done, 0, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE);
+    if (threadIdx.x == 64) dg_stamp(a.trace, 7);
     tc_fence_after();
     const int q = warp & 3;  // the TMEM lane quarter this warp may read
     const int n = q * 32 + lane;
@@ -261,9 +282,11 @@ __global__ void __launch_bounds__(kDgThreads, 1)
     }
     tc_fence_before();
     griddep_launch_dependents();
+    if (threadIdx.x == 64) dg_stamp(a.trace, 8);
   }
   // every CTA's partial tile and sums of squares are written (release / acquire, cluster)
   cluster_sync();
+  if (threadIdx.x == 64) dg_stamp(a.trace, 9);
 
   if (warp >= 2) {
     // ------------------------------------------------------------ epilogue, part 2
@@ -405,9 +428,11 @@ __global__ void __launch_bounds__(kDgThreads, 1)
       }
     }
   }
+  if (threadIdx.x == 64) dg_stamp(a.trace, 10);
   // no CTA leaves (or frees TMEM) while a peer may still read its shared memory
   tc_fence_before();
   cluster_sync();
+  if (threadIdx.x == 64) dg_stamp(a.trace, 11);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, tcols);
@@ -415,6 +440,19 @@ __global__ void __launch_bounds__(kDgThreads, 1)
 }
 
 // ------------------------------------------------------------------------ host side
+static unsigned long long* g_dg_trace = nullptr;
+
+// Install (or with None remove) a uint64 [32] buffer that the next decode GEMM launches
+// fill with the phase timeline of their first and last CTA (see dg_stamp).
+void decode_gemm_trace_set(c10::optional<torch::Tensor> buf) {
+  if (buf.has_value()) {
+    TORCH_CHECK(buf->is_cuda() && buf->scalar_type() == at::kLong && buf->numel() >= 32, "int64 [32]");
+    g_dg_trace = reinterpret_cast<unsigned long long*>(buf->data_ptr<int64_t>());
+  } else {
+    g_dg_trace = nullptr;
+  }
+}
+
 static size_t dg_smem_bytes(int stages, int mpad) {
   return 1024 + (size_t)stages * (kDgWBytes + (size_t)mpad * 128) + 128 * 4 + 16 * 4 + (2 * stages + 2) * 8 + 16;
 }
@@ -530,10 +568,11 @@ void decode_gemm(torch::Tensor X, torch::Tensor W, torch::Tensor out, int64_t ep
   c10::cuda::CUDAGuard guard(X.device());
   const int tiles = (int)((N + kDgBM - 1) / kDgBM);
   const int sms = num_sms(X.get_device());
-  // Pipeline depth and cluster size: few weight tiles -> one CTA per SM with 8 stages in
-  // flight and 8-way split-K; many -> 4 stages (two CTAs per SM when Mpad <= 64).
-  const bool deep = (int64_t)tiles * kDgMaxSplit <= sms && a.Mpad <= 64;
-  const int slots = deep ? sms : (a.Mpad <= 64 ? 2 * sms : sms);
+  // Pipeline depth and cluster size, so that every k-block of a CTA is in flight at once:
+  // few weight tiles -> 10 stages, one CTA per SM and 8-way split-K (long K); otherwise
+  // 5 stages (two CTAs per SM when Mpad is 32) and the widest split that fits one wave.
+  const bool deep = (int64_t)tiles * kDgMaxSplit <= sms && a.Mpad <= 32;
+  const int slots = deep ? sms : (a.Mpad <= 32 ? 2 * sms : sms);
   int S = 1;
   if (split > 0) {
     TORCH_CHECK(split == 1 || split == 2 || split == 4 || split == 8, "split must be 1, 2, 4 or 8");
@@ -541,14 +580,15 @@ void decode_gemm(torch::Tensor X, torch::Tensor W, torch::Tensor out, int64_t ep
   } else {
     while (S < kDgMaxSplit && (int64_t)tiles * S * 2 <= slots && S * 2 <= a.kb_total) S *= 2;
   }
+  a.trace = g_dg_trace;
   TORCH_CHECK(S <= a.kb_total, "more K splits than K blocks");
   TORCH_CHECK((M + S - 1) / S * S >= M, "row split");
   a.S = S;
   const CUtensorMap tw = make_tmap_bf16(W.data_ptr(), K, N, W.stride(0), kDgBK, kDgBM, 1, 0);
   const CUtensorMap tx = make_tmap_bf16(X.data_ptr(), K, M, X.stride(0), kDgBK, (uint32_t)a.Mpad, 1, 0);
   auto stream = at::cuda::getCurrentCUDAStream();
-  if (deep) dg_launch<8>(tw, tx, a, tiles, pdl, stream);
-  else dg_launch<4>(tw, tx, a, tiles, pdl, stream);
+  if (deep) dg_launch<10>(tw, tx, a, tiles, pdl, stream);
+  else dg_launch<5>(tw, tx, a, tiles, pdl, stream);
 }
 
 }  // namespace tfb

@@ -1,6 +1,6 @@
 """Kernel micro-benchmarks: CUDA-event timing of the hot kernels against the roofline.
 
-Usage: ``python -m trainium_frontier_b200.utils.kernel_bench [gemm|all] [--json PATH]``
+Usage: ``python -m trainium_frontier_b200.utils.kernel_bench [gemm|attn|decode|all] [--json PATH]``
 
 Each case: 3+ warm-up launches, then timed launches with an L2 flush (a write of a
 buffer larger than the 126 MB L2) between them, CUDA events on the launching stream
@@ -169,9 +169,9 @@ def trace_fa_fwd(dev, B: int = 16, T: int = 2048, H: int = 10, D: int = 128) -> 
     C().fa_trace_set(None)
     t = buf.view(4, 64, 8).cpu()
     t0 = int(t[t > 0].min())
-    names = {0: ["step top", "S0(j+1) issued", "PV0(j) issued", "S1(j+1) issued", "PV1(j) issued"],
-             1: ["loop top", "S ready", "P computed", "P tile free", "P stored"],
-             2: ["loop top", "S ready", "P computed", "P tile free", "P stored"]}
+    names = {0: ["step top", "PV0(j) issued", "S0(j+1) issued", "PV1(j) issued", "S1(j+1) issued"],
+             1: ["loop top", "S ready", "P computed", "O rescaled", "P in TMEM"],
+             2: ["loop top", "S ready", "P computed", "O rescaled", "P in TMEM"]}
     out = {}
     for r, role in enumerate(["mma", "softmax0", "softmax1"]):
         rows = []
@@ -217,7 +217,65 @@ def trace_fa_bwd(dev, B: int = 16, T: int = 2048, H: int = 10, D: int = 128) -> 
     return out
 
 
+DG_PHASES = ["entry", "set-up done", "weight loads issued", "grid dependency resolved", "first stage landed",
+             "last MMA issued", "sums of squares done", "MMAs complete", "partial tile stored",
+             "cluster barrier 1", "rows reduced + stored", "cluster barrier 2"]
+
+
+def bench_decode_gemm(dev, peaks, M: int = 32, reps: int = 50) -> list[dict]:
+    """Decode-step linears of the d20 model (M = 32 rows) through the decode GEMM: per
+    shape, the event-timed mean of `reps` back-to-back launches cycling over enough weight
+    copies (> L2) that every launch streams its weights from HBM, with and without
+    programmatic dependent launch, and the phase timeline (ns from CTA 0's entry) of the
+    first and last CTA of one launch."""
+    from ..ops._ext import C, err_word
+    shapes = [("qkv", 3840, 1280, 4, True), ("attn proj", 1280, 1280, 1, False), ("fc", 5120, 1280, 2, True),
+              ("mlp proj", 1280, 5120, 1, False), ("lm_head", 8192, 1280, 0, True)]
+    err = err_word(dev)
+    out = []
+    for name, N, K, epi, norm in shapes:
+        copies = max(2, (160 << 20) // (N * K * 2) + 1)
+        ws = [(torch.randn(N, K, device=dev) * K ** -0.5).bfloat16() for _ in range(copies)]
+        x = torch.randn(M, K, device=dev).bfloat16()
+        r = torch.randn(M, N, device=dev).bfloat16()
+        y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        epi_c = 1 if epi in (1, 4) else (2 if epi == 2 else 0)   # QKV shape timed with the residual epilogue
+
+        def run(pdl, i):
+            C().decode_gemm(x, ws[i % copies], y, epi_c, norm, r if epi_c == 1 else None, None, None, None, 0.0,
+                            None, None, None, None, None, 0, 0, pdl, err)
+        row = {"name": name, "N": N, "K": K, "weight_mb": N * K * 2 / 1e6}
+        for pdl in (False, True):
+            for i in range(5):
+                run(pdl, i)
+            torch.cuda.synchronize(dev)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for i in range(reps):
+                run(pdl, i)
+            e.record()
+            torch.cuda.synchronize(dev)
+            us = s.elapsed_time(e) * 1000 / reps
+            key = "pdl" if pdl else "plain"
+            row[f"us_{key}"] = us
+            row[f"gbs_{key}"] = N * K * 2 / us / 1e3
+            row[f"frac_hbm_{key}"] = row[f"gbs_{key}"] / peaks["hbm_gbs"]
+        buf = torch.zeros(32, dtype=torch.int64, device=dev)
+        C().decode_gemm_trace_set(buf)
+        run(False, 0)
+        torch.cuda.synchronize(dev)
+        C().decode_gemm_trace_set(None)
+        t = buf.cpu().tolist()
+        t0 = t[0]
+        row["timeline_first_cta"] = {p: (t[i] - t0 if t[i] else None) for i, p in enumerate(DG_PHASES)}
+        row["timeline_last_cta"] = {p: (t[16 + i] - t0 if t[16 + i] else None) for i, p in enumerate(DG_PHASES)}
+        out.append(row)
+        del ws
+    return out
+
+
 def main():
+    ap = argparse.ArgumentParser()def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("what", nargs="?", default="gemm")
     ap.add_argument("--one", default="", help="run one small case: gemm | gemm_relu2 | gemm_dw | fa_fwd | fa_bwd")
@@ -247,6 +305,13 @@ def main():
         for r in out["gemm"]:
             print(f"{r['name']:>20s}  {r['ms']:8.3f} ms  {r['tflops']:7.1f} TF/s ({r['frac_of_measured']:.2f} of "
                   f"{peaks['source']})   torch {r['torch_ms']:8.3f} ms {r['torch_tflops']:7.1f} TF/s")
+    if args.what in ("decode", "all"):
+        out["decode_gemm"] = bench_decode_gemm(dev, peaks)
+        for r in out["decode_gemm"]:
+            print(f"{r['name']:>12s} {r['weight_mb']:6.1f} MB  plain {r['us_plain']:6.2f} us ({r['frac_hbm_plain']:.2f} of HBM)"
+                  f"  pdl {r['us_pdl']:6.2f} us ({r['frac_hbm_pdl']:.2f})")
+            for cta in ("timeline_first_cta", "timeline_last_cta"):
+                print(f"   {cta}: " + ", ".join(f"{k}={v}" for k, v in r[cta].items()))
     if args.what in ("attn", "all"):
         out["attention"] = bench_attention(dev, peaks)
         for r in out["attention"]:
