@@ -61,7 +61,7 @@ constexpr float kDgNormEps = 1.1920928955078125e-07f;  // F.rms_norm's default f
 
 struct DecGemmArgs {
   int M, N, K, Mpad;
-  int kb_total, S;
+  int kb_total, S, mr;
   int epi, row_norm;
   const __nv_bfloat16* X;  // the TMA operand, also read directly for the sums of squares
   long long ldx;
@@ -91,8 +91,8 @@ struct DecGemmArgs {
 // and the last CTA of the grid write %globaltimer at each phase into trace[slot * 16 + e].
 //   0 entry, 1 set-up done, 2 weight loads issued, 3 grid dependency resolved (producer),
 //   4 first stage landed (MMA), 5 last MMA issued, 6 sums of squares done, 7 MMAs complete
-//   (epilogue), 8 partial tile in shared memory, 9 first cluster barrier passed,
-//   10 rows reduced and stored, 11 second cluster barrier passed
+//   (epilogue), 8 partial tile in shared memory, 9 pushes to the owners issued,
+//   10 every peer's partials received, 11 rows finished and pushes read
 __device__ __forceinline__ void dg_stamp(unsigned long long* tr, int e) {
   if (tr == nullptr) return;
   const unsigned last = gridDim.x - 1;
@@ -106,6 +106,18 @@ __device__ __forceinline__ float dg_warp_sum(float v) {
 }
 __device__ __forceinline__ float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// Bulk copy of `bytes` (a multiple of 16) from this CTA's shared memory to another CTA's
+// (dst and mbar: shared::cluster addresses); completion counted on that CTA's mbarrier.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "r"(smem_u32(src)), "r"(bytes), "r"(mbar)
+               : "memory");
+}
+
 template <int STAGES>
 __global__ void __launch_bounds__(kDgThreads, 1)
     decode_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
@@ -113,27 +125,35 @@ __global__ void __launch_bounds__(kDgThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int XB = a.Mpad * 128;  // bytes of one X stage (Mpad rows x 64 bf16)
+  const int S = a.S, mr = a.mr;  // cluster size; rows finished per rank (a multiple of 4)
   uint8_t* sW = smem;
   uint8_t* sX = smem + STAGES * kDgWBytes;
-  // [Mpad][128] fp32 partial tile; reuses the weight ring once every MMA has read it
+  // [S * mr][128] fp32 partial tile of this CTA's K slice; reuses the weight ring once
+  // every MMA of this CTA has read it
   float* part = reinterpret_cast<float*>(smem);
-  float* ssq = reinterpret_cast<float*>(sX + STAGES * XB);  // [128] partial sums of squares
-  float* scratch = ssq + 128;                                 // [16] QK-norm cross-warp sums
+  float* recv = reinterpret_cast<float*>(sX + STAGES * XB);  // [S][mr][128] partials of this rank's rows
+  float* rssq = recv + S * mr * kDgBM;                       // [S][mr] their sums of squares
+  float* ssq = rssq + S * mr;                                // [132] this K slice's sums of squares
+  float* scratch = ssq + 132;                                // [16] QK-norm cross-warp sums
   uint64_t* full = reinterpret_cast<uint64_t*>(scratch + 16);
   uint64_t* empty = full + STAGES;
   uint64_t* done = empty + STAGES;
   uint64_t* drain = done + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* recv_bar = drain + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int S = a.S;
   const int crank = (int)cluster_ctarank();
   const int nb = (int)cluster_id_x();
   const int kb0 = (int)((long long)crank * a.kb_total / S);
   const int kb1 = (int)((long long)(crank + 1) * a.kb_total / S);
   const int nk = kb1 - kb0;
   const uint32_t tcols = (uint32_t)a.Mpad;  // 32, 64 or 128: a power of two >= 32
+  const int m_lo = crank * mr, m_hi = min(a.M, m_lo + mr);  // rows this rank finishes
+  const bool owner = m_lo < a.M;
+  // every sender pushes mr rows of partials (+ mr sums of squares) to each owner
+  const uint32_t push_bytes = (uint32_t)(mr * kDgBM * 4 + (a.row_norm ? mr * 4 : 0));
   if (threadIdx.x == 0) dg_stamp(a.trace, 0);
 
   if (threadIdx.x == 0) {
@@ -143,6 +163,9 @@ __global__ void __launch_bounds__(kDgThreads, 1)
     }
     mbar_init(done, 1);
     mbar_init(drain, 1);
+    mbar_init(recv_bar, 1);
+    // the phase completes once this arrival and every peer's pushed bytes are in
+    if (owner) mbar_arrive_expect_tx(recv_bar, (uint32_t)S * push_bytes);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmW);
@@ -156,6 +179,8 @@ __global__ void __launch_bounds__(kDgThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // this CTA's barriers are initialised: peers may push into it once they have waited
+  cluster_arrive_release();
   if (threadIdx.x == 0) dg_stamp(a.trace, 1);
 
   if (warp == 0) {
@@ -198,13 +223,14 @@ __global__ void __launch_bounds__(kDgThreads, 1)
         }
       }
     }
+    __syncwarp();
+    cluster_wait_acquire();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_bf16(kDgBM, a.Mpad, false, false);
       bool ok = true;
       griddep_wait();  // the bounded waits below then time this kernel's loads, not its predecessor
-
       for (int i = 0; i < nk; ++i) {
         const int s = i % STAGES;
         const uint32_t ph = (uint32_t)((i / STAGES) & 1);
@@ -226,9 +252,12 @@ __global__ void __launch_bounds__(kDgThreads, 1)
       dg_stamp(a.trace, 5);
       if (!ok) *abort_flag = 1;
     }
+    __syncwarp();
+    cluster_wait_acquire();
   } else {
-    // ------------------------------------------------------------ epilogue, part 1
+    // ------------------------------------------------------------ epilogue
     const int ew = warp - 2;
+    const int et = threadIdx.x - 64;
     griddep_wait();
     if (a.row_norm) {
       // warp ew sums rows ew, ew + 4, ...; eight rows' loads are issued together so the
@@ -266,42 +295,45 @@ __global__ void __launch_bounds__(kDgThreads, 1)
     const bool ok = mbar_wait_warp(done, 0, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE);
     if (threadIdx.x == 64) dg_stamp(a.trace, 7);
     tc_fence_after();
-    const int q = warp & 3;  // the TMEM lane quarter this warp may read
-    const int n = q * 32 + lane;
-    for (int c0 = 0; c0 < a.Mpad; c0 += 32) {
-      uint32_t r[32];
-      if (ok && nk > 0) {
-        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, r);
-        tmem_ld_wait();
-      } else {
+    {
+      const int q = warp & 3;  // the TMEM lane quarter this warp may read
+      const int n = q * 32 + lane;
+      for (int c0 = 0; c0 < a.Mpad; c0 += 32) {
+        uint32_t r[32];
+        if (ok && nk > 0) {
+          tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, r);
+          tmem_ld_wait();
+        } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) r[j] = 0u;
+          for (int jj = 0; jj < 32; ++jj) r[jj] = 0u;
+        }
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) part[(c0 + jj) * kDgBM + n] = __uint_as_float(r[jj]);
       }
-#pragma unroll
-      for (int j = 0; j < 32; ++j) part[(c0 + j) * kDgBM + n] = __uint_as_float(r[j]);
     }
     tc_fence_before();
+    fence_proxy_async_smem();  // the bulk copies below read `part` / `ssq` through the async proxy
+    named_bar_sync(1, 128);
     griddep_launch_dependents();
     if (threadIdx.x == 64) dg_stamp(a.trace, 8);
-  }
-  // every CTA's partial tile and sums of squares are written (release / acquire, cluster)
-  cluster_sync();
-  if (threadIdx.x == 64) dg_stamp(a.trace, 9);
-
-  if (warp >= 2) {
-    // ------------------------------------------------------------ epilogue, part 2
-    const int et = threadIdx.x - 64;
-    const int slot = et >> 6, j = et & 63;  // two rows at a time, thread pair (j, j + 64)
-    const int mr = (a.M + S - 1) / S;
-    const int m_lo = crank * mr, m_hi = min(a.M, m_lo + mr);
-    uint32_t pb[kDgMaxSplit], sb[kDgMaxSplit];
-#pragma unroll
-    for (int p = 0; p < kDgMaxSplit; ++p) {
-      if (p < S) {
-        pb[p] = mapa_shared(smem_u32(part), (uint32_t)p);
-        sb[p] = mapa_shared(smem_u32(ssq), (uint32_t)p);
+    cluster_wait_acquire();  // every peer's barriers are initialised
+    if (threadIdx.x == 64) {
+      // push rows [r * mr, r * mr + mr) of the partial tile (and their sums of squares) to
+      // rank r, into its slot for this rank; completion counts on rank r's recv_bar
+      for (int r = 0; r < S; ++r) {
+        if (r * mr >= a.M) break;
+        const uint32_t rbar = mapa_shared(smem_u32(recv_bar), (uint32_t)r);
+        bulk_copy_to_peer(mapa_shared(smem_u32(recv + (size_t)crank * mr * kDgBM), (uint32_t)r),
+                          part + (size_t)r * mr * kDgBM, (uint32_t)(mr * kDgBM * 4), rbar);
+        if (a.row_norm)
+          bulk_copy_to_peer(mapa_shared(smem_u32(rssq + crank * mr), (uint32_t)r), ssq + r * mr, (uint32_t)(mr * 4), rbar);
       }
+      bulk_commit_group();
+      dg_stamp(a.trace, 9);
     }
+
+    // ---------------------------------------------------------- finish this rank's rows
+    const int slot = et >> 6, j = et & 63;  // two rows at a time, thread pair (j, j + 64)
     const int n0 = nb * kDgBM;
     const int ca = n0 + j, cb = n0 + j + 64;
     const bool va = ca < a.N, vb = cb < a.N;
@@ -312,29 +344,10 @@ __global__ void __launch_bounds__(kDgThreads, 1)
       lr = *a.lam_r;
       l0 = *a.lam_0;
     }
-    // U rows per pass of each thread pair: every distributed-shared-memory and global load
-    // of the U rows is issued before any of them is used
     constexpr int U = 4;
-    for (int mb = m_lo + slot; mb < m_hi; mb += 2 * U) {
-      float v0[U], v1[U], ss[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) v0[u] = v1[u] = ss[u] = 0.f;
-#pragma unroll
-      for (int p = 0; p < kDgMaxSplit; ++p) {
-        if (p < S) {  // rank order: the sum is the same on every launch
-#pragma unroll
-          for (int u = 0; u < U; ++u) {
-            const int m = mb + 2 * u;
-            if (m < m_hi) {
-              const uint32_t off = (uint32_t)((m * kDgBM + j) * 4);
-              v0[u] += ld_dsmem_f32(pb[p] + off);
-              v1[u] += ld_dsmem_f32(pb[p] + off + 256);
-              if (a.row_norm) ss[u] += ld_dsmem_f32(sb[p] + (uint32_t)(m * 4));
-            }
-          }
-        }
-      }
-      float ra[U], rb[U], xa[U], xb[U];
+    float ra[U], rb[U], xa[U], xb[U];
+    // residual / x0 values of a batch of U rows (issued before the partials are awaited)
+    auto load_rows = [&](int mb) {
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int m = mb + 2 * u;
@@ -350,89 +363,118 @@ __global__ void __launch_bounds__(kDgThreads, 1)
           if (vb) xb[u] = __bfloat162float(x0row[cb]);
         }
       }
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        if (a.row_norm) {
-          const float rs = rsqrtf(ss[u] / (float)a.K + kDgNormEps);
-          v0[u] *= rs;
-          v1[u] *= rs;
-        }
-      }
-      if (a.epi != DEC_QKV) {
+    };
+    if (owner) {
+      load_rows(m_lo + slot);
+      mbar_wait_warp(recv_bar, 0, abort_flag, a.err, ERR_TIMEOUT_PEER);
+      // one decision for all four warps (the QKV path has named barriers per warp pair)
+      named_bar_sync(1, 128);
+      const bool got = *abort_flag == 0;
+      if (threadIdx.x == 64) dg_stamp(a.trace, 10);
+      for (int mb = m_lo + slot; mb < m_hi && got; mb += 2 * U) {
+        if (mb != m_lo + slot) load_rows(mb);
+        float v0[U], v1[U], ss[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-          const int m = mb + 2 * u;
-          if (m >= m_hi) continue;
-          float y0 = v0[u], y1 = v1[u];
-          if (a.epi == DEC_RES) {
-            y0 += ra[u];
-            y1 += rb[u];
-          } else if (a.epi == DEC_RELU2) {
-            const float h0 = bf16r(y0) - a.tau, h1 = bf16r(y1) - a.tau;
-            y0 = h0 > 0.f ? h0 * h0 : 0.f;
-            y1 = h1 > 0.f ? h1 * h1 : 0.f;
-          } else if (a.epi == DEC_MIX) {
-            y0 = lr * bf16r(y0 + ra[u]) + l0 * xa[u];
-            y1 = lr * bf16r(y1 + rb[u]) + l0 * xb[u];
-          }
-          __nv_bfloat16* orow = a.out + (long long)m * a.ldo;
-          if (va) orow[ca] = __float2bfloat16_rn(y0);
-          if (vb) orow[cb] = __float2bfloat16_rn(y1);
-        }
-      } else {  // DEC_QKV (128-wide heads, one head per tile)
-        const bool in_cache = pos >= 0 && pos < a.Tmax;
-        if (nb < 2 * a.H) {
-          const int tp = in_cache ? pos : 0;  // table row (out-of-range positions write no cache row)
-          const float c = __bfloat162float(a.cosb[(long long)tp * 64 + j]);
-          const float sn = __bfloat162float(a.sinb[(long long)tp * 64 + j]);
-          float y1[U], y2[U];
+          v0[u] = v1[u] = ss[u] = 0.f;
+          const int ml = mb + 2 * u - m_lo;
+          if (ml + m_lo < m_hi) {
 #pragma unroll
-          for (int u = 0; u < U; ++u) {
-            const float x1 = bf16r(v0[u]), x2 = bf16r(v1[u]);
-            y1[u] = x1 * c + x2 * sn;
-            y2[u] = x2 * c - x1 * sn;
-            const float t = dg_warp_sum(y1[u] * y1[u] + y2[u] * y2[u]);
-            if (lane == 0) scratch[(slot * 2 + (warp & 1)) * U + u] = t;
-          }
-          named_bar_sync(1 + slot, 64);
-          float tot[U];
-#pragma unroll
-          for (int u = 0; u < U; ++u) tot[u] = scratch[(slot * 2) * U + u] + scratch[(slot * 2 + 1) * U + u];
-          named_bar_sync(1 + slot, 64);
-#pragma unroll
-          for (int u = 0; u < U; ++u) {
-            const int m = mb + 2 * u;
-            if (m >= m_hi) continue;
-            const float r = rsqrtf(tot[u] / 128.f + kDgNormEps);
-            const __nv_bfloat16 z1 = __float2bfloat16_rn(y1[u] * r), z2 = __float2bfloat16_rn(y2[u] * r);
-            if (nb < a.H) {
-              __nv_bfloat16* orow = a.out + (long long)m * a.ldo;
-              orow[nb * 128 + j] = z1;
-              orow[nb * 128 + j + 64] = z2;
-            } else if (in_cache) {
-              __nv_bfloat16* kr = a.kc + (long long)m * a.cs_b + (long long)pos * a.cs_t + (long long)(nb - a.H) * a.cs_h;
-              kr[j] = z1;
-              kr[j + 64] = z2;
+            for (int p = 0; p < kDgMaxSplit; ++p) {
+              if (p < S) {  // rank order: the sum is the same on every launch
+                const float* src = recv + ((size_t)p * mr + ml) * kDgBM;
+                v0[u] += src[j];
+                v1[u] += src[j + 64];
+                if (a.row_norm) ss[u] += rssq[p * mr + ml];
+              }
             }
           }
-        } else if (in_cache) {
+        }
+        if (a.row_norm) {
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const float rs = rsqrtf(ss[u] / (float)a.K + kDgNormEps);
+            v0[u] *= rs;
+            v1[u] *= rs;
+          }
+        }
+        if (a.epi != DEC_QKV) {
 #pragma unroll
           for (int u = 0; u < U; ++u) {
             const int m = mb + 2 * u;
             if (m >= m_hi) continue;
-            __nv_bfloat16* vr = a.vc + (long long)m * a.cs_b + (long long)pos * a.cs_t + (long long)(nb - 2 * a.H) * a.cs_h;
-            vr[j] = __float2bfloat16_rn(bf16r(v0[u]));
-            vr[j + 64] = __float2bfloat16_rn(bf16r(v1[u]));
+            float y0 = v0[u], y1 = v1[u];
+            if (a.epi == DEC_RES) {
+              y0 += ra[u];
+              y1 += rb[u];
+            } else if (a.epi == DEC_RELU2) {
+              const float h0 = bf16r(y0) - a.tau, h1 = bf16r(y1) - a.tau;
+              y0 = h0 > 0.f ? h0 * h0 : 0.f;
+              y1 = h1 > 0.f ? h1 * h1 : 0.f;
+            } else if (a.epi == DEC_MIX) {
+              y0 = lr * bf16r(y0 + ra[u]) + l0 * xa[u];
+              y1 = lr * bf16r(y1 + rb[u]) + l0 * xb[u];
+            }
+            __nv_bfloat16* orow = a.out + (long long)m * a.ldo;
+            if (va) orow[ca] = __float2bfloat16_rn(y0);
+            if (vb) orow[cb] = __float2bfloat16_rn(y1);
+          }
+        } else {  // DEC_QKV (128-wide heads, one head per tile)
+          const bool in_cache = pos >= 0 && pos < a.Tmax;
+          if (nb < 2 * a.H) {
+            const int tp = in_cache ? pos : 0;  // table row (out-of-range positions write no cache row)
+            const float c = __bfloat162float(a.cosb[(long long)tp * 64 + j]);
+            const float sn = __bfloat162float(a.sinb[(long long)tp * 64 + j]);
+            float y1[U], y2[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+              const float x1 = bf16r(v0[u]), x2 = bf16r(v1[u]);
+              y1[u] = x1 * c + x2 * sn;
+              y2[u] = x2 * c - x1 * sn;
+              const float t = dg_warp_sum(y1[u] * y1[u] + y2[u] * y2[u]);
+              if (lane == 0) scratch[(slot * 2 + (warp & 1)) * U + u] = t;
+            }
+            named_bar_sync(2 + slot, 64);
+            float tot[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) tot[u] = scratch[(slot * 2) * U + u] + scratch[(slot * 2 + 1) * U + u];
+            named_bar_sync(2 + slot, 64);
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+              const int m = mb + 2 * u;
+              if (m >= m_hi) continue;
+              const float r = rsqrtf(tot[u] / 128.f + kDgNormEps);
+              const __nv_bfloat16 z1 = __float2bfloat16_rn(y1[u] * r), z2 = __float2bfloat16_rn(y2[u] * r);
+              if (nb < a.H) {
+                __nv_bfloat16* orow = a.out + (long long)m * a.ldo;
+                orow[nb * 128 + j] = z1;
+                orow[nb * 128 + j + 64] = z2;
+              } else if (in_cache) {
+                __nv_bfloat16* kr = a.kc + (long long)m * a.cs_b + (long long)pos * a.cs_t + (long long)(nb - a.H) * a.cs_h;
+                kr[j] = z1;
+                kr[j + 64] = z2;
+              }
+            }
+          } else if (in_cache) {
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+              const int m = mb + 2 * u;
+              if (m >= m_hi) continue;
+              __nv_bfloat16* vr = a.vc + (long long)m * a.cs_b + (long long)pos * a.cs_t + (long long)(nb - 2 * a.H) * a.cs_h;
+              vr[j] = __float2bfloat16_rn(bf16r(v0[u]));
+              vr[j + 64] = __float2bfloat16_rn(bf16r(v1[u]));
+            }
           }
         }
       }
     }
+    if (threadIdx.x == 64) {
+      bulk_wait_group_read<0>();  // the pushes have read `part` before the CTA's memory is released
+      dg_stamp(a.trace, 11);
+    }
   }
-  if (threadIdx.x == 64) dg_stamp(a.trace, 10);
-  // no CTA leaves (or frees TMEM) while a peer may still read its shared memory
   tc_fence_before();
-  cluster_sync();
-  if (threadIdx.x == 64) dg_stamp(a.trace, 11);
+  __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, tcols);
@@ -453,15 +495,16 @@ void decode_gemm_trace_set(c10::optional<torch::Tensor> buf) {
   }
 }
 
-static size_t dg_smem_bytes(int stages, int mpad) {
-  return 1024 + (size_t)stages * (kDgWBytes + (size_t)mpad * 128) + 128 * 4 + 16 * 4 + (2 * stages + 2) * 8 + 16;
+static size_t dg_smem_bytes(int stages, int mpad, int S, int mr) {
+  return 1024 + (size_t)stages * (kDgWBytes + (size_t)mpad * 128) + (size_t)S * mr * (kDgBM * 4 + 4) + 132 * 4 + 16 * 4 +
+         (2 * stages + 3) * 8 + 16;
 }
 
 template <int STAGES>
 static void dg_launch(const CUtensorMap& tw, const CUtensorMap& tx, const DecGemmArgs& a, int tiles, bool pdl,
                       cudaStream_t stream) {
   auto kern = decode_gemm_kernel<STAGES>;
-  const size_t smem = dg_smem_bytes(STAGES, a.Mpad);
+  const size_t smem = dg_smem_bytes(STAGES, a.Mpad, a.S, a.mr);
   TORCH_CHECK(smem <= 232448, "decode GEMM shared memory above the per-CTA limit");
   static int smem_set = 0;
   if ((int)smem > smem_set) {
@@ -568,9 +611,9 @@ void decode_gemm(torch::Tensor X, torch::Tensor W, torch::Tensor out, int64_t ep
   c10::cuda::CUDAGuard guard(X.device());
   const int tiles = (int)((N + kDgBM - 1) / kDgBM);
   const int sms = num_sms(X.get_device());
-  // Pipeline depth and cluster size, so that every k-block of a CTA is in flight at once:
-  // few weight tiles -> 10 stages, one CTA per SM and 8-way split-K (long K); otherwise
-  // 5 stages (two CTAs per SM when Mpad is 32) and the widest split that fits one wave.
+  // Pipeline depth and cluster size: few weight tiles -> 10 stages, one CTA per SM and
+  // 8-way split-K (long K); otherwise 4 stages (two CTAs per SM when Mpad is 32) and the
+  // widest split that fits one wave.
   const bool deep = (int64_t)tiles * kDgMaxSplit <= sms && a.Mpad <= 32;
   const int slots = deep ? sms : (a.Mpad <= 32 ? 2 * sms : sms);
   int S = 1;
@@ -582,13 +625,14 @@ void decode_gemm(torch::Tensor X, torch::Tensor W, torch::Tensor out, int64_t ep
   }
   a.trace = g_dg_trace;
   TORCH_CHECK(S <= a.kb_total, "more K splits than K blocks");
-  TORCH_CHECK((M + S - 1) / S * S >= M, "row split");
   a.S = S;
+  a.mr = (int)(((M + S - 1) / S + 3) / 4 * 4);  // rows per rank, a multiple of 4 (16-byte pushes)
+  TORCH_CHECK((int64_t)S * a.mr <= 128, "row split");
   const CUtensorMap tw = make_tmap_bf16(W.data_ptr(), K, N, W.stride(0), kDgBK, kDgBM, 1, 0);
   const CUtensorMap tx = make_tmap_bf16(X.data_ptr(), K, M, X.stride(0), kDgBK, (uint32_t)a.Mpad, 1, 0);
   auto stream = at::cuda::getCurrentCUDAStream();
   if (deep) dg_launch<10>(tw, tx, a, tiles, pdl, stream);
-  else dg_launch<5>(tw, tx, a, tiles, pdl, stream);
+  else dg_launch<4>(tw, tx, a, tiles, pdl, stream);
 }
 
 }  // namespace tfb

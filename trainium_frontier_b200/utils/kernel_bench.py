@@ -274,8 +274,43 @@ def bench_decode_gemm(dev, peaks, M: int = 32, reps: int = 50) -> list[dict]:
     return out
 
 
+def bench_decode_attention(dev, peaks, B: int = 32, H: int = 10, D: int = 128, L: int = 576, Tmax: int = 896,
+                           reps: int = 50) -> list[dict]:
+    """Split decode attention over a head-major KV cache (the decode step's layout) for a
+    sweep of cache-length splits: event-timed mean of `reps` launches cycling over enough
+    cache copies (> L2) that every launch streams K and V from HBM."""
+    from ..ops._ext import C
+    per = B * H * Tmax * D * 2 * 2
+    copies = max(2, (200 << 20) // per + 1)
+    caches = [(torch.randn(B, H, Tmax, D, device=dev).bfloat16(), torch.randn(B, H, Tmax, D, device=dev).bfloat16())
+              for _ in range(copies)]
+    q = torch.randn(B, H * D, device=dev).bfloat16()
+    ln = torch.tensor([L], dtype=torch.int32, device=dev)
+    out = torch.empty(B, H * D, device=dev, dtype=torch.bfloat16)
+    rows = []
+    for splits in (3, 5, 7, 10, 14, 16):
+        ws = torch.zeros(B * H * splits * (D + 4), device=dev)
+        cnt = torch.zeros(B * H, dtype=torch.int32, device=dev)
+
+        def run(i):
+            kc, vc = caches[i % copies]
+            C().decode_attn_split(q, kc, vc, ln, H, D, D ** -0.5, out, ws, cnt, splits, False)
+        for i in range(5):
+            run(i)
+        torch.cuda.synchronize(dev)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for i in range(reps):
+            run(i)
+        e.record()
+        torch.cuda.synchronize(dev)
+        us = s.elapsed_time(e) * 1000 / reps
+        gbs = B * H * L * D * 2 * 2 / us / 1e3
+        rows.append({"splits": splits, "ctas": B * H * splits, "us": us, "gbs": gbs, "frac_hbm": gbs / peaks["hbm_gbs"]})
+    return rows
+
+
 def main():
-    ap = argparse.ArgumentParser()def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("what", nargs="?", default="gemm")
     ap.add_argument("--one", default="", help="run one small case: gemm | gemm_relu2 | gemm_dw | fa_fwd | fa_bwd")
@@ -312,6 +347,10 @@ def main():
                   f"  pdl {r['us_pdl']:6.2f} us ({r['frac_hbm_pdl']:.2f})")
             for cta in ("timeline_first_cta", "timeline_last_cta"):
                 print(f"   {cta}: " + ", ".join(f"{k}={v}" for k, v in r[cta].items()))
+        out["decode_attention"] = bench_decode_attention(dev, peaks)
+        for r in out["decode_attention"]:
+            print(f"  decode attention splits {r['splits']:2d} ({r['ctas']} CTAs): {r['us']:6.2f} us "
+                  f"{r['gbs']:7.1f} GB/s ({r['frac_hbm']:.2f} of HBM)")
     if args.what in ("attn", "all"):
         out["attention"] = bench_attention(dev, peaks)
         for r in out["attention"]:
