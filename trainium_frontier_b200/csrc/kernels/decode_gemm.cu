@@ -506,6 +506,9 @@ static void dg_launch(const CUtensorMap& tw, const CUtensorMap& tx, const DecGem
   auto kern = decode_gemm_kernel<STAGES>;
   const size_t smem = dg_smem_bytes(STAGES, a.Mpad, a.S, a.mr);
   TORCH_CHECK(smem <= 232448, "decode GEMM shared memory above the per-CTA limit");
+  // the partial tile ([max(Mpad, S * mr)][128] fp32) reuses the weight + activation rings
+  TORCH_CHECK((size_t)std::max(a.Mpad, a.S * a.mr) * kDgBM * 4 <= (size_t)STAGES * (kDgWBytes + (size_t)a.Mpad * 128),
+              "decode GEMM: pipeline too shallow to hold the partial tile");
   static int smem_set = 0;
   if ((int)smem > smem_set) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -614,8 +617,20 @@ void decode_gemm(torch::Tensor X, torch::Tensor W, torch::Tensor out, int64_t ep
   // Pipeline depth and cluster size: few weight tiles -> 10 stages, one CTA per SM and
   // 8-way split-K (long K); otherwise 4 stages (two CTAs per SM when Mpad is 32) and the
   // widest split that fits one wave.
-  const bool deep = (int64_t)tiles * kDgMaxSplit <= sms && a.Mpad <= 32;
-  const int slots = deep ? sms : (a.Mpad <= 32 ? 2 * sms : sms);
+  // TFB_DG_STAGES (default 4) / TFB_DG_DEEP_STAGES (default 10, 0 = never deep) override
+  // the two pipeline depths; each must be one of 2, 3, 4, 6, 8, 10.
+  static const int env_stages = [] {
+    const char* e = getenv("TFB_DG_STAGES");
+    return e ? atoi(e) : 4;
+  }();
+  static const int env_deep = [] {
+    const char* e = getenv("TFB_DG_DEEP_STAGES");
+    return e ? atoi(e) : 10;
+  }();
+  const bool deep = env_deep > 0 && (int64_t)tiles * kDgMaxSplit <= sms && a.Mpad <= 32;
+  const int stages = deep ? env_deep : env_stages;
+  const size_t smem_est = dg_smem_bytes(stages, a.Mpad, kDgMaxSplit, 16);
+  const int slots = sms * std::max<int>(1, (int)std::min<size_t>(2, 228 * 1024 / (smem_est + 1024)));
   int S = 1;
   if (split > 0) {
     TORCH_CHECK(split == 1 || split == 2 || split == 4 || split == 8, "split must be 1, 2, 4 or 8");
@@ -631,8 +646,15 @@ void decode_gemm(torch::Tensor X, torch::Tensor W, torch::Tensor out, int64_t ep
   const CUtensorMap tw = make_tmap_bf16(W.data_ptr(), K, N, W.stride(0), kDgBK, kDgBM, 1, 0);
   const CUtensorMap tx = make_tmap_bf16(X.data_ptr(), K, M, X.stride(0), kDgBK, (uint32_t)a.Mpad, 1, 0);
   auto stream = at::cuda::getCurrentCUDAStream();
-  if (deep) dg_launch<10>(tw, tx, a, tiles, pdl, stream);
-  else dg_launch<4>(tw, tx, a, tiles, pdl, stream);
+  switch (stages) {
+    case 2: dg_launch<2>(tw, tx, a, tiles, pdl, stream); break;
+    case 3: dg_launch<3>(tw, tx, a, tiles, pdl, stream); break;
+    case 4: dg_launch<4>(tw, tx, a, tiles, pdl, stream); break;
+    case 6: dg_launch<6>(tw, tx, a, tiles, pdl, stream); break;
+    case 8: dg_launch<8>(tw, tx, a, tiles, pdl, stream); break;
+    case 10: dg_launch<10>(tw, tx, a, tiles, pdl, stream); break;
+    default: TORCH_CHECK(false, "decode GEMM pipeline depth must be 2, 3, 4, 6, 8 or 10");
+  }
 }
 
 }  // namespace tfb

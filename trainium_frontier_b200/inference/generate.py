@@ -32,6 +32,8 @@ is what prefill and the oracle reproduce.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from ..ops import gemm
@@ -84,6 +86,8 @@ class Generator:
         # (sequence, head) of the decode attention reads one contiguous stream; otherwise
         # the projection buffer's token-major layout [B, T_max, H*D]
         self.fused_decode = self.D == 128 and self.B <= 128
+        # programmatic dependent launch of the decode kernels (TFB_DECODE_PDL=0 turns it off)
+        self.pdl = os.environ.get("TFB_DECODE_PDL", "1") != "0"
         shape = (self.B, self.H, self.Tmax, self.D) if self.fused_decode else (self.B, self.Tmax, self.Cd)
         self.kc = [torch.zeros(shape, dtype=bf, device=dev) for _ in range(L)]
         self.vc = [torch.zeros(shape, dtype=bf, device=dev) for _ in range(L)]
@@ -221,22 +225,22 @@ class Generator:
         L = len(self.wqkv)
         for i in range(L):
             c.decode_gemm(xm, self.wqkv[i], q, DEC_QKV, True, None, None, None, None, 0.0, self.cos, self.sin,
-                          pos, self.kc[i], self.vc[i], self.H, 0, True, err)
+                          pos, self.kc[i], self.vc[i], self.H, 0, self.pdl, err)
             c.decode_attn_split(q, self.kc[i], self.vc[i], ln, self.H, self.D, self.scale, y, self.att_ws,
-                                self.att_cnt, self.att_splits, True)
+                                self.att_cnt, self.att_splits, self.pdl)
             c.decode_gemm(y, self.wo[i], x, DEC_RES, False, xm, None, None, None, 0.0, None, None, None, None, None,
-                          0, 0, True, err)
+                          0, 0, self.pdl, err)
             c.decode_gemm(x, self.wfc[i], act, DEC_RELU2, True, None, None, None, None, float(self.tau), None, None,
-                          None, None, None, 0, 0, True, err)
+                          None, None, None, 0, 0, self.pdl, err)
             if i + 1 < L:
                 nr, n0 = self.lam[i + 1]
                 c.decode_gemm(act, self.wp[i], xm, DEC_MIX, False, x, x0, nr, n0, 0.0, None, None, None, None, None,
-                              0, 0, True, err)
+                              0, 0, self.pdl, err)
             else:
                 c.decode_gemm(act, self.wp[i], xf, DEC_RES, False, x, None, None, None, 0.0, None, None, None, None,
-                              None, 0, 0, True, err)
+                              None, 0, 0, self.pdl, err)
         c.decode_gemm(xf, self.wlm, self.d_logits, DEC_PLAIN, True, None, None, None, None, 0.0, None, None, None,
-                      None, None, 0, 0, True, err)
+                      None, None, 0, 0, self.pdl, err)
         return self.d_logits
 
     @torch.no_grad()
