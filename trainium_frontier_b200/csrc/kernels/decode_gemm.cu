@@ -617,15 +617,19 @@ void decode_gemm(torch::Tensor X, torch::Tensor W, torch::Tensor out, int64_t ep
   // Pipeline depth and cluster size: few weight tiles -> 10 stages, one CTA per SM and
   // 8-way split-K (long K); otherwise 4 stages (two CTAs per SM when Mpad is 32) and the
   // widest split that fits one wave.
-  // TFB_DG_STAGES (default 4) / TFB_DG_DEEP_STAGES (default 10, 0 = never deep) override
-  // the two pipeline depths; each must be one of 2, 3, 4, 6, 8, 10.
+  // Pipeline depth: 3 stages, two CTAs per SM, and the widest split-K that fits one wave.
+  // Measured on the d20 decode step (batch 32, 50 graph replays): 3 stages 1.113 ms,
+  // 2: 1.121, 4: 1.212, 6: 1.104 (one CTA per SM); a "deep" mode (10 stages, one CTA per
+  // SM, 8-way split for few-tile shapes) 1.325, because a CTA that fills an SM leaves no
+  // room for the next kernel's CTAs to launch early under programmatic dependent launch.
+  // TFB_DG_STAGES / TFB_DG_DEEP_STAGES (0 = off) override (2, 3, 4, 6, 8 or 10).
   static const int env_stages = [] {
     const char* e = getenv("TFB_DG_STAGES");
-    return e ? atoi(e) : 4;
+    return e ? atoi(e) : 3;
   }();
   static const int env_deep = [] {
     const char* e = getenv("TFB_DG_DEEP_STAGES");
-    return e ? atoi(e) : 10;
+    return e ? atoi(e) : 0;
   }();
   const bool deep = env_deep > 0 && (int64_t)tiles * kDgMaxSplit <= sms && a.Mpad <= 32;
   const int stages = deep ? env_deep : env_stages;

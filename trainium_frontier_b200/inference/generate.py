@@ -96,12 +96,11 @@ class Generator:
         self.graph = None
         self.tokens = None
         self.ws: dict = {}   # decode GEMM workspaces (zeroed fp32 sums + counters) per shape
-        # cache-length splits of the decode attention: one wave of CTAs (eight 128-thread
-        # CTAs fit an SM at the kernel's register count), at most 16 per (sequence, head);
-        # measured at batch 32 x 10 heads x 576 cached keys: 3 splits 22.7 us, 5: 26.6,
-        # 7: 26.7, 16: 35.2 (utils/kernel_bench.py decode)
-        sms = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 148
-        self.att_splits = max(1, min(16, (sms * 8) // (self.B * self.H), self.Tmax // 64))
+        # cache-length splits of the decode attention, one per 128 cache rows (at most 16).
+        # In isolation 3 splits (one wave) ran faster at batch 32 x 10 heads x 576 keys
+        # (22.7 vs 26.7 us, utils/kernel_bench.py decode), but inside the decode step, where
+        # the next projection's CTAs launch early, 7 splits gave the faster step
+        self.att_splits = max(1, min(16, self.Tmax // 128))
         self.att_ws = torch.zeros(self.B * self.H * self.att_splits * (self.D + 4), dtype=torch.float32, device=dev)
         self.att_cnt = torch.zeros(self.B * self.H, dtype=torch.int32, device=dev)
         blocks = list(model.transformer.h)

@@ -4,14 +4,16 @@ Per gradient bucket (a chunk of ``bucket_layers`` transformer blocks):
 
 1. ownership: the chunk's Muon matrices are grouped into units (c_q/c_k/c_v of a block
    stay together so the fused QKV GEMM keeps reading one [3C, C] view; c_proj, c_fc and
-   the MLP projection are units of one) and assigned to ranks largest-first onto the
-   least-loaded rank.  The flat buffers of the chunk are laid out rank-major -- rank 0's
+   the MLP projection are units of one) and assigned largest-first (by Newton-Schulz
+   cost) to the rank with the least cost accumulated over all buckets so far.  The flat buffers of the chunk are laid out rank-major -- rank 0's
    units, rank 1's units, ... each segment padded to the largest -- so
 2. one ``reduce_scatter`` (AVG) of the chunk delivers to every rank the averaged
    gradient of exactly the matrices it owns; it is launched on a side stream the
    moment backward leaves the chunk (overlapped with the rest of backward);
 3. the owner runs momentum / Nesterov / Newton-Schulz / NorMuon on its matrices and
-   writes the final bf16 update ``g`` (what the reference subtracts after scaling);
+   writes the final bf16 update ``g`` (what the reference subtracts after scaling); the
+   fused path gathers the owner's matrices of every bucket into one stack per (group,
+   shape) first, so the batched Newton-Schulz GEMMs stay large at 8 ranks;
 4. one ``all_gather`` of the bf16 updates gives every rank every matrix's ``g``, and
    every rank applies ``w -= lr g + lr wd w [g w >= 0]`` itself (identical inputs ->
    identical fp32 masters on all ranks, at half the bytes of gathering fp32 weights).
@@ -65,6 +67,10 @@ def plan_buckets(model, muon_param_ids: set[int], world: int, bucket_layers: int
     blocks = list(model.transformer.h)
     L = len(blocks)
     plans = []
+    # Newton-Schulz cost accumulated over the buckets: each unit goes to the rank with the
+    # least total so far, so the owners' whole-step work is balanced (a per-bucket greedy
+    # alone hands the heaviest unit of every bucket to the same rank)
+    cum = [0.0] * world
     for c in range(math.ceil(L / bucket_layers)):
         lay = tuple(range(c * bucket_layers, min(L, (c + 1) * bucket_layers)))
         units: list[Unit] = []
@@ -84,9 +90,10 @@ def plan_buckets(model, muon_param_ids: set[int], world: int, bucket_layers: int
         loads = [0] * world
         owners: list[list[Unit]] = [[] for _ in range(world)]
         for u in sorted(units, key=lambda u: -unit_cost(u)):
-            r = min(range(world), key=lambda i: (cost[i], loads[i]))
+            r = min(range(world), key=lambda i: (cum[i], cost[i], loads[i]))
             owners[r].append(u)
             cost[r] += unit_cost(u)
+            cum[r] += unit_cost(u)
             loads[r] += u.numel
         # inside a rank: group by shape so each (rank, shape) run is one contiguous stack
         for r in range(world):
@@ -411,11 +418,47 @@ def _fused_owner_direction(dm, grp, g, st, coef, out):
                       min(grp["ns_steps"], len(POLAR_EXPRESS_COEFFS)), coef=coef, out=out)
 
 
+def _owner_stacks(self):
+    """This rank's matrices over ALL buckets, one stack per (param group, shape):
+    [(group, shape, runs, K, grad stack, update stack, state)], built once.  The per-run
+    momentum / second-moment states become views of one stack per (group, shape), so the
+    owner math runs a few large batched Newton-Schulz GEMMs instead of several small ones
+    per bucket (at 8 ranks an owner holds an eighth of each bucket, too little to fill
+    the GPU)."""
+    if getattr(self, "_stacks", None) is not None:
+        return self._stacks
+    by: dict = {}
+    for b in range(len(self.plans)):
+        for shape, params, off in self._owned_runs(b):
+            grp = self.group_of[id(params[0])]
+            by.setdefault((id(grp), shape), (grp, shape, []))[2].append((b, params, off, len(params)))
+    stacks = []
+    for grp, shape, runs in by.values():
+        Kt = sum(r[3] for r in runs)
+        red_dim = -1 if shape[-2] >= shape[-1] else -2
+        sshape = (Kt, shape[-2], 1) if red_dim == -1 else (Kt, 1, shape[-1])
+        mb = torch.zeros(Kt, *shape, dtype=torch.float32, device=self.device)
+        second = torch.zeros(sshape, dtype=torch.float32, device=self.device)
+        k = 0
+        for _, params, _, K in runs:
+            old = self.state.get(id(params[0]))
+            if old is not None:  # e.g. restored from a checkpoint before the first step
+                mb[k:k + K].copy_(old["mb"])
+                second[k:k + K].copy_(old["second"])
+            self.state[id(params[0])] = {"mb": mb[k:k + K], "second": second[k:k + K]}
+            k += K
+        gbuf = torch.empty(Kt, *shape, dtype=torch.float32, device=self.device)
+        obuf = torch.empty(Kt, *shape, dtype=torch.bfloat16, device=self.device)
+        stacks.append((grp, shape, runs, Kt, gbuf, obuf, {"mb": mb, "second": second}))
+    self._stacks = stacks
+    return stacks
+
+
 def _step_fused(self, update_adamw: bool = True) -> None:
-    """Owner math bucket by bucket on the main stream; as soon as every owner has written
-    bucket b's updates (a device barrier issued on the comm stream after this rank's
-    bucket-b work), the gather + apply of bucket b runs on the comm stream while the main
-    stream goes on with the Newton-Schulz of bucket b+1."""
+    """Owner math on whole-step stacks on the main stream (this rank's matrices of every
+    bucket, gathered per (group, shape) from the reduce-scatter outputs), updates scattered
+    into the symmetric update buffer, then one device barrier and one gather + apply
+    launch over every bucket."""
     opt = self.opt
     self.mark("opt:start")
     for g in opt.param_groups:
@@ -433,26 +476,36 @@ def _step_fused(self, update_adamw: bool = True) -> None:
     coef = self.clip_coef.reshape(1) if self.clip_coef is not None else None
     main = torch.cuda.current_stream(self.device)
     side = self.comm if self.comm is not None else main
-    for b in range(len(self.plans)):
-        S = self.plans[b].seg_numel
-        seg = self.recv[b]
-        base = self.goff[b] + self.rank * S
-        for shape, params, off in self._owned_runs(b):
-            K = len(params)
-            n = K * params[0].numel()
-            grp = self.group_of[id(params[0])]
-            g = seg[off:off + n].view(K, *shape)
-            _fused_owner_direction(self, grp, g, self._state(params, grp), coef,
-                                   self.upd[base + off:base + off + n].view(K, *shape))
-        side.wait_stream(main)
-        with torch.cuda.stream(side):
-            self._barrier()  # every owner's bucket-b updates are in its update buffer
-            self.C.symm_ag_apply(self.upd_peers, self._runs_table(b))
-    self.mark("opt:owner Newton-Schulz + NorMuon (gather-apply overlapped)")
+    for grp, shape, runs, Kt, gbuf, obuf, st in self._owner_stacks():
+        numel = shape[-2] * shape[-1]
+        gflat, oflat = gbuf.view(-1), obuf.view(-1)
+        k = 0
+        for b, params, off, K in runs:
+            gflat[k * numel:(k + K) * numel].copy_(self.recv[b][off:off + K * numel])
+            k += K
+        _fused_owner_direction(self, grp, gbuf, st, coef, obuf)
+        k = 0
+        for b, params, off, K in runs:
+            base = self.goff[b] + self.rank * self.plans[b].seg_numel
+            self.upd[base + off:base + off + K * numel].copy_(oflat[k * numel:(k + K) * numel])
+            k += K
+    self.mark("opt:owner Newton-Schulz + NorMuon")
+    side.wait_stream(main)
+    with torch.cuda.stream(side):
+        self._barrier()  # every owner's updates are in its update buffer
+        self.C.symm_ag_apply(self.upd_peers, self._runs_table_all())
     main.wait_stream(side)
-    self.mark("opt:gather-apply tail")
+    self.mark("opt:gather-apply")
     self._barrier()  # peers are done reading this rank's gradient and update buffers
     self.mark("opt:final barrier")
+
+
+def _runs_table_all(self) -> torch.Tensor:
+    tab = getattr(self, "_runs_all", None)
+    if tab is None:
+        tab = torch.cat([self._runs_table(b) for b in range(len(self.plans))], 0)
+        self._runs_all = tab
+    return tab
 
 
 def _runs_table(self, b: int) -> torch.Tensor:
@@ -477,4 +530,6 @@ def _runs_table(self, b: int) -> torch.Tensor:
 
 
 DistMuon._step_fused = _step_fused
+DistMuon._owner_stacks = _owner_stacks
 DistMuon._runs_table = _runs_table
+DistMuon._runs_table_all = _runs_table_all
