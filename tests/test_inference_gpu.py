@@ -85,10 +85,11 @@ def test_split_decode_attention_kernel(cuda_device, layout):
         assert int(cnt.abs().sum()) == 0
 
 
-@pytest.mark.parametrize("splits,pdl", [(1, False), (3, True), (7, True)])
+@pytest.mark.parametrize("splits,pdl", [(2, False), (3, True), (7, True)])
 def test_bulk_decode_attention_kernel(cuda_device, splits, pdl):
     """Head-major cache streamed by bulk copies in 32-key pieces (the piece holding the
-    newest row issued after the grid dependency): every length, counters left zeroed."""
+    newest row issued after the grid dependency): every length, counters left zeroed.
+    A split holds all of its rows in shared memory (at most 400 keys of head_dim 128)."""
     from trainium_frontier_b200.ops._ext import C, check_errors, err_word
     torch.manual_seed(2)
     B, Tm, H, D = 3, 640, 4, 128
