@@ -83,29 +83,3 @@ def test_split_decode_attention_kernel(cuda_device, layout):
         ref = torch.softmax(qf @ kf.transpose(-1, -2) * D ** -0.5, -1) @ vf
         assert (out.float().view(B, H, D) - ref.squeeze(2)).abs().max().item() < 2e-2, L
         assert int(cnt.abs().sum()) == 0
-
-
-@pytest.mark.parametrize("splits,pdl", [(2, False), (3, True), (7, True)])
-def test_bulk_decode_attention_kernel(cuda_device, splits, pdl):
-    """Head-major cache streamed by bulk copies in 32-key pieces (the piece holding the
-    newest row issued after the grid dependency): every length, counters left zeroed.
-    A split holds all of its rows in shared memory (at most 400 keys of head_dim 128)."""
-    from trainium_frontier_b200.ops._ext import C, check_errors, err_word
-    torch.manual_seed(2)
-    B, Tm, H, D = 3, 640, 4, 128
-    q = torch.randn(B, H * D, device=cuda_device).to(torch.bfloat16)
-    kc = torch.randn(B, H, Tm, D, device=cuda_device).to(torch.bfloat16)
-    vc = torch.randn(B, H, Tm, D, device=cuda_device).to(torch.bfloat16)
-    ws = torch.zeros(B * H * splits * (D + 4), device=cuda_device)
-    cnt = torch.zeros(B * H, dtype=torch.int32, device=cuda_device)
-    for L in (1, 31, 33, 77, 513, 640):
-        ln = torch.tensor([L], dtype=torch.int32, device=cuda_device)
-        pos = torch.tensor([L - 1], dtype=torch.int32, device=cuda_device)
-        out = torch.empty(B, H * D, dtype=torch.bfloat16, device=cuda_device)
-        C().decode_attn_bulk(q, kc, vc, ln, pos, H, D, D ** -0.5, out, ws, cnt, splits, pdl, err_word(cuda_device))
-        qf = q.float().view(B, H, 1, D)
-        kf, vf = kc[:, :, :L].float(), vc[:, :, :L].float()
-        ref = torch.softmax(qf @ kf.transpose(-1, -2) * D ** -0.5, -1) @ vf
-        assert (out.float().view(B, H, D) - ref.squeeze(2)).abs().max().item() < 2e-2, L
-        assert int(cnt.abs().sum()) == 0
-    check_errors()

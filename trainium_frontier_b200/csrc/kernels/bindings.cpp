@@ -56,9 +56,6 @@ void decode_gemm(torch::Tensor X, torch::Tensor W, torch::Tensor out, int64_t ep
                  c10::optional<torch::Tensor> sin, c10::optional<torch::Tensor> pos, c10::optional<torch::Tensor> kc,
                  c10::optional<torch::Tensor> vc, int64_t H, int64_t split, bool pdl, torch::Tensor err);
 void decode_gemm_trace_set(c10::optional<torch::Tensor> buf);
-void decode_attn_bulk(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache, torch::Tensor len,
-                      torch::Tensor pos, int64_t H, int64_t D, double scale, torch::Tensor out, torch::Tensor ws,
-                      torch::Tensor cnt, int64_t splits, bool pdl, torch::Tensor err);
 void kv_append(torch::Tensor k, torch::Tensor v, torch::Tensor kcache, torch::Tensor vcache, torch::Tensor pos);
 void step_advance(torch::Tensor counters);
 void argmax_rows(torch::Tensor logits, int64_t V, torch::Tensor idx_out, c10::optional<torch::Tensor> tokens,
@@ -109,7 +106,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_attn_split", &tfb::decode_attn_split);
   m.def("decode_gemm", &tfb::decode_gemm);
   m.def("decode_gemm_trace_set", &tfb::decode_gemm_trace_set);
-  m.def("decode_attn_bulk", &tfb::decode_attn_bulk);
   m.def("kv_append", &tfb::kv_append);
   m.def("step_advance", &tfb::step_advance);
   m.def("argmax_rows", &tfb::argmax_rows);

@@ -251,212 +251,6 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_split_kernel(
   }
 }
 
-// decode_attn_bulk: the split decode attention over a head-major cache ([B, H, T_max, D],
-// each (sequence, head) one contiguous range of rows), with the keys and values of a CTA's
-// split streamed into shared memory by bulk copies (cp.async.bulk, completion on an
-// mbarrier per piece of 32 keys) instead of per-thread loads: every byte of the split is
-// in flight at once, and the warps read rows from shared memory as their piece lands.
-// Launched as a programmatic dependent of the QKV projection: the cache rows below the
-// current position were written by earlier steps, so their pieces are issued before
-// griddepcontrol.wait and stream while the projection is still running; only the piece
-// that holds the new row, and q, wait for it.  Math and combine as decode_attn_split.
-constexpr int kAbPiece = 32;      // keys per bulk piece (= 4 warps x 8 keys per iteration)
-constexpr int kAbMaxPieces = 64;
-
-template <int D>
-__global__ void __launch_bounds__(kDecThreads) decode_attn_bulk_kernel(
-    const __nv_bfloat16* __restrict__ q, long long ldq, const __nv_bfloat16* __restrict__ kc,
-    const __nv_bfloat16* __restrict__ vc, long long cs_b, long long cs_h, const int* __restrict__ len_ptr,
-    const int* __restrict__ pos_ptr, int len_max, __nv_bfloat16* __restrict__ out, long long ldo, int H, float scale,
-    int splits, int max_chunk, float* __restrict__ ws, int* __restrict__ cnt, int* __restrict__ err) {
-  static_assert(D == 128, "a half-warp covers the 128 dims, 8 per lane");
-  constexpr int kPartStride = D + 4;
-  constexpr int NW = kDecThreads / 32;
-  constexpr int KPH = 4;        // keys per half-warp per iteration
-  constexpr int KPW = 2 * KPH;  // keys per warp per iteration (NW * KPW = kAbPiece)
-  static_assert(NW * KPW == kAbPiece, "one piece per iteration of the CTA");
-  extern __shared__ __align__(128) uint8_t ab_smem[];
-  __nv_bfloat16* sK = reinterpret_cast<__nv_bfloat16*>(ab_smem);  // [max_chunk][D]
-  __nv_bfloat16* sV = sK + (size_t)max_chunk * D;                  // [max_chunk][D]
-  __shared__ uint64_t bars[kAbMaxPieces];
-  __shared__ float s_m[NW], s_l[NW];
-  __shared__ __align__(16) float s_o[NW][D];
-  __shared__ int s_last;
-  __shared__ int s_abort;
-  const int bh = blockIdx.x / splits, sp = blockIdx.x % splits;
-  const int b = bh / H, h = bh % H;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int half = lane >> 4, hl = lane & 15;
-  // the length and position counters were written by earlier kernels of the step (all
-  // complete once the QKV projection, this kernel's predecessor, let it launch)
-  int L = *len_ptr;
-  L = L < 1 ? 1 : (L > len_max ? len_max : L);
-  const int pos = *pos_ptr;
-  const int chunk = (L + splits - 1) / splits;
-  const int k0 = sp * chunk, k1 = min(L, k0 + chunk);
-  const int nkeys = max(0, k1 - k0);
-  const int npieces = (nkeys + kAbPiece - 1) / kAbPiece;
-  const __nv_bfloat16* kb = kc + (long long)b * cs_b + (long long)h * cs_h;
-  const __nv_bfloat16* vb = vc + (long long)b * cs_b + (long long)h * cs_h;
-  if (threadIdx.x == 0) {
-    s_abort = 0;
-    for (int p = 0; p < npieces; ++p) mbar_init(&bars[p], 1);
-    fence_barrier_init();
-  }
-  __syncthreads();
-  auto issue = [&](int p) {
-    const int a0 = k0 + p * kAbPiece, a1 = min(k1, a0 + kAbPiece);
-    const uint32_t bytes = (uint32_t)(a1 - a0) * D * 2;
-    mbar_arrive_expect_tx(&bars[p], 2 * bytes);
-    bulk_load(sK + (size_t)(a0 - k0) * D, kb + (long long)a0 * D, bytes, &bars[p]);
-    bulk_load(sV + (size_t)(a0 - k0) * D, vb + (long long)a0 * D, bytes, &bars[p]);
-  };
-  auto holds_new = [&](int p) {
-    const int a0 = k0 + p * kAbPiece, a1 = min(k1, a0 + kAbPiece);
-    return pos >= a0 && pos < a1;
-  };
-  if (threadIdx.x == 0)
-    for (int p = 0; p < npieces; ++p)
-      if (!holds_new(p)) issue(p);
-  griddep_wait();  // q and the new cache row are the QKV projection's output
-  if (threadIdx.x == 0)
-    for (int p = 0; p < npieces; ++p)
-      if (holds_new(p)) issue(p);
-  griddep_launch_dependents();
-  float qs[8];
-  {
-    const uint4 qu = *reinterpret_cast<const uint4*>(q + (long long)b * ldq + h * D + 8 * hl);
-    const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&qu);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = __bfloat1622float2(q2[i]);
-      qs[2 * i] = f.x * scale;
-      qs[2 * i + 1] = f.y * scale;
-    }
-  }
-  float m = -INFINITY, l = 0.f, o[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) o[i] = 0.f;
-  for (int p = 0; p < npieces; ++p) {
-    const int kw = k0 + p * kAbPiece + warp * KPW;
-    if (!mbar_wait_warp(&bars[p], 0, &s_abort, err, ERR_TIMEOUT_EPILOGUE)) break;
-    if (kw >= k1) continue;
-    uint4 ku[KPH], vu[KPH];
-#pragma unroll
-    for (int j = 0; j < KPH; ++j) {
-      const int k = min(kw + half + 2 * j, k1 - 1);  // clamped: past-the-end keys are masked below
-      ku[j] = *reinterpret_cast<const uint4*>(sK + (size_t)(k - k0) * D + 8 * hl);
-      vu[j] = *reinterpret_cast<const uint4*>(sV + (size_t)(k - k0) * D + 8 * hl);
-    }
-    float sd[KPH];
-#pragma unroll
-    for (int j = 0; j < KPH; ++j) {
-      const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&ku[j]);
-      float acc = 0.f;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(k2[i]);
-        acc += qs[2 * i] * f.x + qs[2 * i + 1] * f.y;
-      }
-      sd[j] = acc;
-    }
-#pragma unroll
-    for (int off = 8; off > 0; off >>= 1)
-#pragma unroll
-      for (int j = 0; j < KPH; ++j) sd[j] += __shfl_xor_sync(0xffffffffu, sd[j], off);
-    float mx = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < KPH; ++j) {
-      if (kw + half + 2 * j >= k1) sd[j] = -INFINITY;
-      mx = fmaxf(mx, sd[j]);
-    }
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-    mx = fmaxf(mx, m);
-    const float corr = __expf(m - mx);
-    l *= corr;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) o[i] *= corr;
-#pragma unroll
-    for (int j = 0; j < KPH; ++j) {
-      const float pj = __expf(sd[j] - mx);
-      const __nv_bfloat162* v2 = reinterpret_cast<const __nv_bfloat162*>(&vu[j]);
-      l += pj;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(v2[i]);
-        o[2 * i] += pj * f.x;
-        o[2 * i + 1] += pj * f.y;
-      }
-    }
-    m = mx;
-  }
-  if (s_abort && threadIdx.x == 0) {
-    // a piece never completed: give copies still in flight a bounded moment to land
-    // before this CTA's shared memory is released
-    for (int p = 0; p < npieces; ++p) {
-      const unsigned long long t0 = globaltimer_ns();
-      while (!mbar_try_wait(&bars[p], 0))
-        if (globaltimer_ns() - t0 > 100000000ull) break;
-    }
-  }
-  l += __shfl_xor_sync(0xffffffffu, l, 16);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) o[i] += __shfl_xor_sync(0xffffffffu, o[i], 16);
-  if (lane == 0) {
-    s_m[warp] = m;
-    s_l[warp] = l;
-  }
-  if (half == 0) {
-    *reinterpret_cast<float4*>(&s_o[warp][8 * hl]) = make_float4(o[0], o[1], o[2], o[3]);
-    *reinterpret_cast<float4*>(&s_o[warp][8 * hl + 4]) = make_float4(o[4], o[5], o[6], o[7]);
-  }
-  __syncthreads();
-  float* part = ws + ((long long)bh * splits + sp) * kPartStride;
-  if (warp == 0) {
-    float M = s_m[0];
-#pragma unroll
-    for (int w = 1; w < NW; ++w) M = fmaxf(M, s_m[w]);
-    float Lsum = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int w = 0; w < NW; ++w) {
-      const float f = s_m[w] == -INFINITY ? 0.f : __expf(s_m[w] - M);
-      Lsum += f * s_l[w];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) acc[j] += f * s_o[w][4 * lane + j];
-    }
-    *reinterpret_cast<float4*>(part + 4 * lane) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-    if (lane == 0) {
-      part[D] = M;
-      part[D + 1] = Lsum;
-    }
-    __threadfence();
-    __syncwarp();
-    if (lane == 0) s_last = atomicAdd(cnt + bh, 1) == splits - 1;
-  }
-  __syncthreads();
-  if (!s_last) return;
-  if (warp == 0) {
-    __threadfence();
-    const float* base = ws + (long long)bh * splits * kPartStride;
-    float M = -INFINITY;
-    for (int t = 0; t < splits; ++t) M = fmaxf(M, __ldcg(base + t * kPartStride + D));
-    float Lsum = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int t = 0; t < splits; ++t) {
-      const float mt = __ldcg(base + t * kPartStride + D);
-      const float f = mt == -INFINITY ? 0.f : __expf(mt - M);
-      Lsum += f * __ldcg(base + t * kPartStride + D + 1);
-      const float4 ot = __ldcg(reinterpret_cast<const float4*>(base + t * kPartStride + 4 * lane));
-      acc[0] += f * ot.x; acc[1] += f * ot.y; acc[2] += f * ot.z; acc[3] += f * ot.w;
-    }
-    const float inv = 1.f / Lsum;
-    uint2 u;
-    u.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
-    u.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
-    *reinterpret_cast<uint2*>(out + (long long)b * ldo + h * D + 4 * lane) = u;
-    if (lane == 0) cnt[bh] = 0;
-  }
-}
-
 // cache[b, pos, :] = src[b, :] for k and v (pos read from device memory).
 __global__ void kv_append_kernel(const __nv_bfloat16* __restrict__ ksrc, long long ldk,
                                  const __nv_bfloat16* __restrict__ vsrc, long long ldv, __nv_bfloat16* __restrict__ kc,
@@ -647,59 +441,5 @@ void decode_attn_split(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcac
                                     (float)scale, (int)splits, ws.data_ptr<float>(), cnt.data_ptr<int>()));
 }
 
-
-// Head-major caches [B, H, T_max, D] only (one contiguous range per (sequence, head)).
-// pos: the row the predecessor kernel writes this step (its bulk piece waits for it).
-// ws / cnt as decode_attn_split.
-void decode_attn_bulk(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache, torch::Tensor len,
-                      torch::Tensor pos, int64_t H, int64_t D, double scale, torch::Tensor out, torch::Tensor ws,
-                      torch::Tensor cnt, int64_t splits, bool pdl, torch::Tensor err) {
-  TORCH_CHECK(D == 128, "bulk decode attention supports head_dim 128");
-  TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kBFloat16 && kcache.scalar_type() == at::kBFloat16 &&
-                  vcache.scalar_type() == at::kBFloat16, "bf16 inputs");
-  TORCH_CHECK(kcache.dim() == 4 && kcache.is_contiguous() && vcache.is_contiguous() && kcache.sizes() == vcache.sizes() &&
-                  kcache.size(1) == H && kcache.size(3) == D,
-              "head-major contiguous caches [B, H, T_max, D]");
-  auto a16 = [](const torch::Tensor& t) { return (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0; };
-  TORCH_CHECK(a16(q) && a16(kcache) && a16(vcache) && (q.stride(0) * 2) % 16 == 0 && q.stride(1) == 1 &&
-                  out.stride(1) == 1 && (out.stride(0) * 2) % 8 == 0 && (reinterpret_cast<uintptr_t>(out.data_ptr()) & 7) == 0,
-              "aligned q / caches / output");
-  const int64_t B = q.size(0);
-  const int tmax = (int)kcache.size(2);
-  TORCH_CHECK(kcache.size(0) >= B, "cache batch");
-  TORCH_CHECK(splits >= 1 && splits <= 64, "splits 1..64");
-  const int max_chunk = (int)((tmax + splits - 1) / splits);
-  TORCH_CHECK((max_chunk + kAbPiece - 1) / kAbPiece <= kAbMaxPieces, "too many keys per split");
-  TORCH_CHECK(ws.scalar_type() == at::kFloat && ws.numel() >= B * H * splits * (D + 4), "workspace size");
-  TORCH_CHECK((reinterpret_cast<uintptr_t>(ws.data_ptr()) & 15) == 0, "workspace must be 16-byte aligned");
-  TORCH_CHECK(cnt.scalar_type() == at::kInt && cnt.numel() >= B * H, "counter size");
-  c10::cuda::CUDAGuard guard(q.device());
-  const size_t smem = (size_t)max_chunk * D * 2 * 2;
-  TORCH_CHECK(smem <= 200 * 1024, "split too long for shared memory");
-  static size_t smem_set = 0;
-  if (smem > smem_set) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(decode_attn_bulk_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    smem_set = smem;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.gridDim = dim3((unsigned)(B * H * splits), 1, 1);
-  cfg.blockDim = dim3(kDecThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = at::cuda::getCurrentCUDAStream();
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, decode_attn_bulk_kernel<128>,
-                                    reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), (long long)q.stride(0),
-                                    reinterpret_cast<const __nv_bfloat16*>(kcache.data_ptr()),
-                                    reinterpret_cast<const __nv_bfloat16*>(vcache.data_ptr()), (long long)kcache.stride(0),
-                                    (long long)kcache.stride(1), (const int*)len.data_ptr<int>(),
-                                    (const int*)pos.data_ptr<int>(), tmax,
-                                    reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (long long)out.stride(0), (int)H,
-                                    (float)scale, (int)splits, max_chunk, ws.data_ptr<float>(), cnt.data_ptr<int>(),
-                                    err.data_ptr<int>()));
-}
 
 }  // namespace tfb

@@ -12,9 +12,7 @@
   dependent launch so each kernel's weight stream starts under the previous kernel):
     1. QKV projection of the mixed residual with its RMS norm folded in (row scale),
        RoPE + QK-norm at the device-side position, k / v rows written into the cache;
-    2. split single-query attention over the cache, its keys and values streamed into
-       shared memory by bulk copies (the rows of earlier steps start streaming while
-       the QKV projection is still running);
+    2. split single-query attention over the cache;
     3. attention projection + residual;
     4. MLP up-projection with the RMS norm folded in, relu^2;
     5. MLP down-projection + residual, then the next block's residual mix
@@ -103,8 +101,6 @@ class Generator:
         # (22.7 vs 26.7 us, utils/kernel_bench.py decode), but inside the decode step, where
         # the next projection's CTAs launch early, 7 splits gave the faster step
         self.att_splits = max(1, min(16, self.Tmax // 128))
-        # the bulk-copy attention holds a split's keys and values in shared memory
-        self.att_bulk = -(-self.Tmax // self.att_splits) * self.D * 4 <= 200 * 1024
         self.att_ws = torch.zeros(self.B * self.H * self.att_splits * (self.D + 4), dtype=torch.float32, device=dev)
         self.att_cnt = torch.zeros(self.B * self.H, dtype=torch.int32, device=dev)
         blocks = list(model.transformer.h)
@@ -229,12 +225,8 @@ class Generator:
         for i in range(L):
             c.decode_gemm(xm, self.wqkv[i], q, DEC_QKV, True, None, None, None, None, 0.0, self.cos, self.sin,
                           pos, self.kc[i], self.vc[i], self.H, 0, self.pdl, err)
-            if self.att_bulk:
-                c.decode_attn_bulk(q, self.kc[i], self.vc[i], ln, pos, self.H, self.D, self.scale, y, self.att_ws,
-                                   self.att_cnt, self.att_splits, self.pdl, err)
-            else:
-                c.decode_attn_split(q, self.kc[i], self.vc[i], ln, self.H, self.D, self.scale, y, self.att_ws,
-                                    self.att_cnt, self.att_splits, self.pdl)
+            c.decode_attn_split(q, self.kc[i], self.vc[i], ln, self.H, self.D, self.scale, y, self.att_ws,
+                                self.att_cnt, self.att_splits, self.pdl)
             c.decode_gemm(y, self.wo[i], x, DEC_RES, False, xm, None, None, None, 0.0, None, None, None, None, None,
                           0, 0, self.pdl, err)
             c.decode_gemm(x, self.wfc[i], act, DEC_RELU2, True, None, None, None, None, float(self.tau), None, None,

@@ -287,34 +287,26 @@ def bench_decode_attention(dev, peaks, B: int = 32, H: int = 10, D: int = 128, L
     q = torch.randn(B, H * D, device=dev).bfloat16()
     ln = torch.tensor([L], dtype=torch.int32, device=dev)
     out = torch.empty(B, H * D, device=dev, dtype=torch.bfloat16)
-    from ..ops._ext import err_word
-    pos = torch.tensor([L - 1], dtype=torch.int32, device=dev)
-    err = err_word(dev)
     rows = []
-    for kernel in ("split", "bulk"):
-        for splits in (3, 5, 7, 10, 14, 16):
-            ws = torch.zeros(B * H * splits * (D + 4), device=dev)
-            cnt = torch.zeros(B * H, dtype=torch.int32, device=dev)
+    for splits in (3, 5, 7, 10, 14, 16):
+        ws = torch.zeros(B * H * splits * (D + 4), device=dev)
+        cnt = torch.zeros(B * H, dtype=torch.int32, device=dev)
 
-            def run(i):
-                kc, vc = caches[i % copies]
-                if kernel == "split":
-                    C().decode_attn_split(q, kc, vc, ln, H, D, D ** -0.5, out, ws, cnt, splits, False)
-                else:
-                    C().decode_attn_bulk(q, kc, vc, ln, pos, H, D, D ** -0.5, out, ws, cnt, splits, False, err)
-            for i in range(5):
-                run(i)
-            torch.cuda.synchronize(dev)
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record()
-            for i in range(reps):
-                run(i)
-            e.record()
-            torch.cuda.synchronize(dev)
-            us = s.elapsed_time(e) * 1000 / reps
-            gbs = B * H * L * D * 2 * 2 / us / 1e3
-            rows.append({"kernel": kernel, "splits": splits, "ctas": B * H * splits, "us": us, "gbs": gbs,
-                         "frac_hbm": gbs / peaks["hbm_gbs"]})
+        def run(i):
+            kc, vc = caches[i % copies]
+            C().decode_attn_split(q, kc, vc, ln, H, D, D ** -0.5, out, ws, cnt, splits, False)
+        for i in range(5):
+            run(i)
+        torch.cuda.synchronize(dev)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for i in range(reps):
+            run(i)
+        e.record()
+        torch.cuda.synchronize(dev)
+        us = s.elapsed_time(e) * 1000 / reps
+        gbs = B * H * L * D * 2 * 2 / us / 1e3
+        rows.append({"splits": splits, "ctas": B * H * splits, "us": us, "gbs": gbs, "frac_hbm": gbs / peaks["hbm_gbs"]})
     return rows
 
 
@@ -357,7 +349,7 @@ def main():
                 print(f"   {cta}: " + ", ".join(f"{k}={v}" for k, v in r[cta].items()))
         out["decode_attention"] = bench_decode_attention(dev, peaks)
         for r in out["decode_attention"]:
-            print(f"  decode attention ({r['kernel']}) splits {r['splits']:2d} ({r['ctas']} CTAs): {r['us']:6.2f} us "
+            print(f"  decode attention splits {r['splits']:2d} ({r['ctas']} CTAs): {r['us']:6.2f} us "
                   f"{r['gbs']:7.1f} GB/s ({r['frac_hbm']:.2f} of HBM)")
     if args.what in ("attn", "all"):
         out["attention"] = bench_attention(dev, peaks)
