@@ -1155,8 +1155,8 @@ __global__ void __launch_bounds__(448, 1)
         fa_stamp(a.trace, 0, it, 1);
         tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)  // dV += P^T dO
-          umma_bf16(tDV, desc_kmajor(pd_addr, kk), desc_mnmajor(do_addr, kk), IDESC_KV, (it > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < 8; ++kk)  // dV += P^T dO, P^T from TMEM (over S^T's first 64 columns)
+          umma_bf16_tmem_a(tDV, tR0 + kk * 8, desc_mnmajor(do_addr, kk), IDESC_KV, (it > 0 || kk > 0) ? 1u : 0u);
         umma_commit(dv_done);
         umma_commit(do_empty);  // dO read by dP^T and dV
         if (it + 1 < n_it && !issue_s(it + 1)) { ok = false; break; }
@@ -1249,22 +1249,18 @@ __global__ void __launch_bounds__(448, 1)
           pk[(e >> 1) + 1] = pack_bf16x2(p1.x, p1.y);
         }
       }
+      // P^T back into TMEM over the first 64 columns of S^T (this thread's 64 queries as 32
+      // packed columns): the dV MMA reads it as its A operand, and S^T(i+1) is issued only
+      // after that MMA (one thread's tcgen05 MMAs run in issue order)
+      __syncwarp();
+      tmem_st_32x32b_x32(tR0 + lane_off + half * 32, pk);
+      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(s_free);
-      if (stamp) fa_stamp(a.trace, 1, it, 2);
-      if (it >= 1 && !mbar_wait_warp(pds_free, (it - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
-      if (stamp) fa_stamp(a.trace, 1, it, 3);
-#pragma unroll
-      for (int q = 0; q < 8; ++q)
-        *reinterpret_cast<uint4*>(sPD + half * kPanel + sw128_chunk_offset(r, q)) =
-            make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-      fence_proxy_async_smem();
-      tc_fence_before();
       mbar_arrive(p_full);
-      if (stamp) fa_stamp(a.trace, 1, it, 4);
+      if (stamp) fa_stamp(a.trace, 1, it, 2);
       if (!mbar_wait_warp(dp_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
-      if (!mbar_wait_warp(dv_done, it & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
-      if (stamp) fa_stamp(a.trace, 1, it, 5);
+      if (stamp) fa_stamp(a.trace, 1, it, 3);
       tc_fence_after();
 #pragma unroll
       for (int h2 = 0; h2 < 2; ++h2) {
@@ -1288,6 +1284,10 @@ __global__ void __launch_bounds__(448, 1)
           pk[(e >> 1) + 1] = pack_bf16x2(sb.x, sb.y);
         }
       }
+      if (stamp) fa_stamp(a.trace, 1, it, 4);
+      // the dS tile is free once dQ(i-1) and dK(i-1) have read it
+      if (it >= 1 && !mbar_wait_warp(pds_free, (it - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      if (stamp) fa_stamp(a.trace, 1, it, 5);
 #pragma unroll
       for (int q = 0; q < 8; ++q)
         *reinterpret_cast<uint4*>(sPD + half * kPanel + sw128_chunk_offset(r, q)) =

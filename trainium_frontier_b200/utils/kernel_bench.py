@@ -202,7 +202,7 @@ def trace_fa_bwd(dev, B: int = 16, T: int = 2048, H: int = 10, D: int = 128) -> 
     t = buf.view(4, 64, 8).cpu()
     t0 = int(t[t > 0].min())
     names = {0: ["dP issued", "P ready", "S(i+1) issued", "dS ready", "loop top", "dO landed", "dQ drained"],
-             1: ["loop top", "S ready", "P computed", "P/dS tile free", "P stored", "dP+dV done", "dS stored"],
+             1: ["loop top", "S ready", "P in TMEM", "dP ready", "dS computed", "dS tile free", "dS stored"],
              2: ["loop top", "dQ ready", "dQ read"], 3: ["Q issued", "dO issued"]}
     roles = ["mma", "softmax", "drain", "producer"]
     out = {}
