@@ -390,6 +390,11 @@ def test_muon_owner_kernels_match_reference_math(cuda_device, shape):
     muon_owner_update(g.clone(), mb.clone(), second.clone(), mom, one_mom, one_b2, 5, out=out)
     upd = (w - w2)  # = bf16(lr) u + decay
     assert torch.isfinite(out.float()).all() and out.float().abs().max() > 0
+    # bit-reproducible: replicas that each run the optimizer on identical gradients (the
+    # bucketed all-reduce path) must keep identical fp32 masters
+    out2 = torch.empty_like(out)
+    muon_owner_update(g.clone(), mb.clone(), second.clone(), mom, one_mom, one_b2, 5, out=out2)
+    assert torch.equal(out, out2)
 
 
 def test_embed_grad_deterministic_with_frequent_tokens(cuda_device):

@@ -122,8 +122,8 @@ void muon_apply(torch::Tensor w, torch::Tensor g, torch::Tensor lr, torch::Tenso
 // stack of K matrices [K, r, c] (reference train.py:3608-3647):
 //   muon_fro_scale  x = x / d with d = bf16(bf16(bf16(||x||_F) * 1.01) + 1e-6): the
 //                   reference's normalisation in its bf16 op order (norm rounded to bf16,
-//                   each scalar op rounded, IEEE division), from the fp32 sums of squares
-//                   muon_pre accumulated;
+//                   each scalar op rounded, IEEE division), from the fp32 partial sums
+//                   of squares muon_pre wrote (added here in a fixed order);
 //   normuon_*       the NorMuon second moment on the Newton-Schulz output gq:
 //                   v_mean = mean over the reduced dim of gq^2 (columns of a tall or
 //                   square matrix, rows of a wide one); second = lerp(second, v_mean, 1-b2);
@@ -132,9 +132,12 @@ void muon_apply(torch::Tensor w, torch::Tensor g, torch::Tensor lr, torch::Tenso
 //                   computed from v_mean as the reference does.
 __device__ __forceinline__ float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
-__global__ void muon_fro_scale_kernel(__nv_bfloat16* __restrict__ x, long long per, const float* __restrict__ fro) {
+__global__ void muon_fro_scale_kernel(__nv_bfloat16* __restrict__ x, long long per, const float* __restrict__ fro,
+                                      int nparts) {
   const int k = blockIdx.y;
-  const float nrm = bf16r(sqrtf(fro[k]));
+  float ss = 0.f;
+  for (int p = 0; p < nparts; ++p) ss += fro[(long long)k * nparts + p];  // fixed order
+  const float nrm = bf16r(sqrtf(ss));
   const float d = bf16r(bf16r(nrm * 1.01f) + 1e-6f);
   uint4* xv = reinterpret_cast<uint4*>(x + (long long)k * per);
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < per / 8; i += (long long)gridDim.x * blockDim.x) {
@@ -286,15 +289,17 @@ __global__ void normuon_apply_kernel(const __nv_bfloat16* __restrict__ gq, const
   }
 }
 
+// fro: fp32 [K, P] partial sums of squares per matrix (muon_pre's), added in order.
 void muon_fro_scale(torch::Tensor x, torch::Tensor fro) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 3 && x.is_contiguous(), "x bf16 [K, r, c]");
-  TORCH_CHECK(fro.scalar_type() == at::kFloat && fro.numel() >= x.size(0), "fro fp32 [K]");
+  TORCH_CHECK(fro.scalar_type() == at::kFloat && fro.dim() == 2 && fro.size(0) == x.size(0) && fro.is_contiguous(),
+              "fro fp32 [K, P]");
   const long long per = x.size(1) * x.size(2);
   TORCH_CHECK(per % 8 == 0, "matrix size % 8");
   c10::cuda::CUDAGuard guard(x.device());
   dim3 grid((unsigned)std::max<long long>(1, std::min<long long>((per / 8 + 255) / 256, 64)), (unsigned)x.size(0));
   muon_fro_scale_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), per, fro.data_ptr<float>());
+      reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), per, fro.data_ptr<float>(), (int)fro.size(1));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -12,7 +12,8 @@
 //                    averages, writes the fp32 result and accumulates its sum of squares
 //                    (the global-norm partial) -- reduce + norm in one pass;
 //   muon_pre         clip scale, momentum lerp, Nesterov lerp, bf16 cast and per-matrix
-//                    sum of squares (Frobenius norm) of the owner's stacks in one pass;
+//                    sum of squares (Frobenius norm) of the owner's stacks in one pass
+//                    (kMuonPreBlocks partial sums per matrix, added in order later);
 //   symm_ag_apply    all-gather + apply: for every matrix of a bucket, read its bf16
 //                    update from the owner's update buffer (peer load) and apply
 //                    w -= bf16(lr) g + lr wd w [g w >= 0] to the fp32 master and its bf16
@@ -30,6 +31,7 @@
 namespace tfb {
 
 constexpr int kMaxRanks = 8;
+constexpr int kMuonPreBlocks = 64;  // blocks (and partial sums) per matrix of muon_pre
 
 struct PeerF32 { const float* p[kMaxRanks]; };
 struct PeerBf16 { const __nv_bfloat16* p[kMaxRanks]; };
@@ -148,7 +150,10 @@ __global__ void muon_pre_kernel(const float* __restrict__ g, float* __restrict__
   if (threadIdx.x == 0) {
     float t = 0.f;
     for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
-    atomicAdd(fro + k, t);
+    // one partial per block, summed in block order by the consumer: the norm (and so the
+    // whole Muon step) is bit-reproducible, which replicas that each run the optimizer on
+    // identical gradients rely on
+    fro[(long long)k * gridDim.x + blockIdx.x] = t;
   }
 }
 
@@ -259,13 +264,16 @@ void symm_rs(std::vector<int64_t> peer_ptrs, int64_t src_off, int64_t n, torch::
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// fro: fp32 [K, kMuonPreBlocks] partial sums of squares (every entry written).
 void muon_pre(torch::Tensor g, torch::Tensor mb, torch::Tensor x, c10::optional<torch::Tensor> coef, torch::Tensor mom,
               torch::Tensor one_mom, torch::Tensor fro) {
   TORCH_CHECK(g.dim() == 3 && g.is_contiguous() && mb.is_contiguous() && x.is_contiguous(), "[K, r, c] stacks");
   const int K = (int)g.size(0);
   const long long per = g.size(1) * g.size(2);
   TORCH_CHECK(per % 4 == 0, "matrix size % 4");
-  dim3 grid((unsigned)std::max<long long>(1, std::min<long long>((per / 4 + 255) / 256, 64)), K);
+  TORCH_CHECK(fro.scalar_type() == at::kFloat && fro.is_contiguous() && fro.numel() == (int64_t)K * kMuonPreBlocks,
+              "fro fp32 [K, 64] partial sums");
+  dim3 grid((unsigned)kMuonPreBlocks, K);
   muon_pre_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       g.data_ptr<float>(), mb.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), per, K,
       coef.has_value() ? coef->data_ptr<float>() : nullptr, mom.data_ptr<float>(), one_mom.data_ptr<float>(),

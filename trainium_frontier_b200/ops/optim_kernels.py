@@ -42,7 +42,7 @@ def muon_owner_update(g: torch.Tensor, mb: torch.Tensor, second: torch.Tensor, m
     from . import newton_schulz as ns
     K = g.shape[0]
     x = torch.empty(g.shape, dtype=torch.bfloat16, device=g.device)
-    fro = torch.zeros(K, dtype=torch.float32, device=g.device)
+    fro = torch.empty(K, 64, dtype=torch.float32, device=g.device)  # per-block partial sums (fixed order)
     C().muon_pre(g, mb, x, None if coef is None else coef.reshape(1), mom.reshape(1), one_mom.reshape(1), fro)
     C().muon_fro_scale(x, fro)
     gq = ns.newton_schulz(x, ns_steps)
