@@ -1123,10 +1123,11 @@ __global__ void __launch_bounds__(448, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    // Order per query tile i: dP^T(i), dV(i), S^T(i+1), dQ(i), dK(i) -- S^T(i+1) goes out
-    // before the wait for dS(i), so the softmax warps find it done when they move on and
-    // compute P(i+1) while the tensor core runs dQ(i) and dK(i); dQ(i) goes first so that
-    // its drain frees R1 for dP^T(i+1) while dK(i) still runs.
+    // Order per query tile i: dP^T(i) queries 0..63, dV(i), S^T(i+1), dP^T(i) queries
+    // 64..127, dQ(i), dK(i) -- S^T(i+1) goes out before the wait for dS(i), so the softmax
+    // warps find it done when they move on and compute P(i+1) while the tensor core runs
+    // dQ(i) and dK(i); dQ(i) goes first so that its drain frees R1 for dP^T(i+1) while dK(i)
+    // still runs, one 64-column half at a time.
     if (lane == 0) {
       bool ok = mbar_wait(bar_kv, 0, abort_flag, a.err, ERR_TIMEOUT_MMA);
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), pd_addr = smem_u32(sPD), do_addr = smem_u32(sDO);
@@ -1157,12 +1158,6 @@ __global__ void __launch_bounds__(448, 1)
         for (int kk = 0; kk < D / 16; ++kk)
           umma_bf16(tR1, desc_kmajor(v_addr, kk), desc_kmajor(do_addr, kk), IDESC_DP, kk > 0 ? 1u : 0u);
         umma_commit(dp_full);
-        if (it >= 1 && !mbar_wait(dq_free_hi, (it - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          umma_bf16(tR1 + 64, desc_kmajor(v_addr, kk), desc_kmajor(do_addr + 8192u, kk), IDESC_DP, kk > 0 ? 1u : 0u);
-        umma_commit(dp_full_hi);
         fa_stamp(a.trace, 0, it, 0);
         if (!mbar_wait(p_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
         fa_stamp(a.trace, 0, it, 1);
@@ -1171,9 +1166,17 @@ __global__ void __launch_bounds__(448, 1)
         for (int kk = 0; kk < 8; ++kk)  // dV += P^T dO, P^T from TMEM (over S^T's first 64 columns)
           umma_bf16_tmem_a(tDV, tR0 + kk * 8, desc_mnmajor(do_addr, kk), IDESC_KV, (it > 0 || kk > 0) ? 1u : 0u);
         umma_commit(dv_done);
-        umma_commit(do_empty);  // dO read by dP^T and dV
         if (it + 1 < n_it && !issue_s(it + 1)) { ok = false; break; }
         fa_stamp(a.trace, 0, it, 2);
+        // the second dP^T half goes after dV and S^T(i+1), which do not depend on it, so the
+        // slower second half of the dQ drain holds up only the warps that need it
+        if (it >= 1 && !mbar_wait(dq_free_hi, (it - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_bf16(tR1 + 64, desc_kmajor(v_addr, kk), desc_kmajor(do_addr + 8192u, kk), IDESC_DP, kk > 0 ? 1u : 0u);
+        umma_commit(dp_full_hi);
+        umma_commit(do_empty);  // dO read by both dP^T halves and dV
         if (!mbar_wait(ds_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
         fa_stamp(a.trace, 0, it, 3);
         tc_fence_after();
