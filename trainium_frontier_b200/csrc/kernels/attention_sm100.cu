@@ -973,8 +973,7 @@ __global__ void __launch_bounds__(448, 1)
   constexpr int D = 128;
   constexpr uint32_t TILE = 128u * D * 2u;
   constexpr uint32_t STG = 128u * 32u * 4u;  // one 32-column fp32 dQ slice
-  constexpr uint32_t IDESC_SS = umma_idesc_bf16(128, 128, false, false);  // S^T
-  constexpr uint32_t IDESC_DP = umma_idesc_bf16(128, 64, false, false);   // dP^T, one 64-query half
+  constexpr uint32_t IDESC_SS = umma_idesc_bf16(128, 128, false, false);  // S^T, dP^T
   constexpr uint32_t IDESC_KV = umma_idesc_bf16(128, D, false, true);     // dV, dK
   constexpr uint32_t IDESC_Q = umma_idesc_bf16(128, D, true, true);       // dQ
 
@@ -1012,9 +1011,7 @@ __global__ void __launch_bounds__(448, 1)
   uint64_t* drain = bars + 17;
   uint64_t* stg_full = bars + 18;  // [2]
   uint64_t* stg_free = bars + 20;  // [2]
-  uint64_t* dq_free_hi = bars + 22;  // dQ's columns 64..127 read (dq_free: columns 0..63)
-  uint64_t* dp_full_hi = bars + 23;  // dP^T's queries 64..127 ready (dp_full: 0..63)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1044,8 +1041,6 @@ __global__ void __launch_bounds__(448, 1)
     mbar_init(ds_full, 256);
     mbar_init(dq_full, 1);
     mbar_init(dq_free, 128);
-    mbar_init(dq_free_hi, 128);
-    mbar_init(dp_full_hi, 1);
     mbar_init(pds_free, 1);
     mbar_init(kv_done, 1);
     mbar_init(drain, 1);
@@ -1123,11 +1118,10 @@ __global__ void __launch_bounds__(448, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    // Order per query tile i: dP^T(i) queries 0..63, dV(i), S^T(i+1), dP^T(i) queries
-    // 64..127, dQ(i), dK(i) -- S^T(i+1) goes out before the wait for dS(i), so the softmax
-    // warps find it done when they move on and compute P(i+1) while the tensor core runs
-    // dQ(i) and dK(i); dQ(i) goes first so that its drain frees R1 for dP^T(i+1) while dK(i)
-    // still runs, one 64-column half at a time.
+    // Order per query tile i: dP^T(i), dV(i), S^T(i+1), dQ(i), dK(i) -- S^T(i+1) goes out
+    // before the wait for dS(i), so the softmax warps find it done when they move on and
+    // compute P(i+1) while the tensor core runs dQ(i) and dK(i); dQ(i) goes first so that
+    // its drain frees R1 for dP^T(i+1) while dK(i) still runs.
     if (lane == 0) {
       bool ok = mbar_wait(bar_kv, 0, abort_flag, a.err, ERR_TIMEOUT_MMA);
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), pd_addr = smem_u32(sPD), do_addr = smem_u32(sDO);
@@ -1149,14 +1143,12 @@ __global__ void __launch_bounds__(448, 1)
         fa_stamp(a.trace, 0, it, 4);
         if (!mbar_wait(do_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
         fa_stamp(a.trace, 0, it, 5);
-        // dP^T = V dO^T in two 64-query halves, each as soon as the drain warps have read
-        // that half of dQ(i-1) out of R1 (queries 64h..64h+63 are rows 64h.. of the dO tile)
         if (it >= 1 && !mbar_wait(dq_free, (it - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
         fa_stamp(a.trace, 0, it, 6);
         tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          umma_bf16(tR1, desc_kmajor(v_addr, kk), desc_kmajor(do_addr, kk), IDESC_DP, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < D / 16; ++kk)  // dP^T = V dO^T
+          umma_bf16(tR1, desc_kmajor(v_addr, kk), desc_kmajor(do_addr, kk), IDESC_SS, kk > 0 ? 1u : 0u);
         umma_commit(dp_full);
         fa_stamp(a.trace, 0, it, 0);
         if (!mbar_wait(p_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
@@ -1166,17 +1158,9 @@ __global__ void __launch_bounds__(448, 1)
         for (int kk = 0; kk < 8; ++kk)  // dV += P^T dO, P^T from TMEM (over S^T's first 64 columns)
           umma_bf16_tmem_a(tDV, tR0 + kk * 8, desc_mnmajor(do_addr, kk), IDESC_KV, (it > 0 || kk > 0) ? 1u : 0u);
         umma_commit(dv_done);
+        umma_commit(do_empty);  // dO read by dP^T and dV
         if (it + 1 < n_it && !issue_s(it + 1)) { ok = false; break; }
         fa_stamp(a.trace, 0, it, 2);
-        // the second dP^T half goes after dV and S^T(i+1), which do not depend on it, so the
-        // slower second half of the dQ drain holds up only the warps that need it
-        if (it >= 1 && !mbar_wait(dq_free_hi, (it - 1) & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          umma_bf16(tR1 + 64, desc_kmajor(v_addr, kk), desc_kmajor(do_addr + 8192u, kk), IDESC_DP, kk > 0 ? 1u : 0u);
-        umma_commit(dp_full_hi);
-        umma_commit(do_empty);  // dO read by both dP^T halves and dV
         if (!mbar_wait(ds_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_MMA)) { ok = false; break; }
         fa_stamp(a.trace, 0, it, 3);
         tc_fence_after();
@@ -1275,10 +1259,7 @@ __global__ void __launch_bounds__(448, 1)
       mbar_arrive(s_free);
       mbar_arrive(p_full);
       if (stamp) fa_stamp(a.trace, 1, it, 2);
-      if (!mbar_wait_warp(half == 0 ? dp_full : dp_full_hi, it & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) {
-        ok = false;
-        break;
-      }
+      if (!mbar_wait_warp(dp_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
       if (stamp) fa_stamp(a.trace, 1, it, 3);
       tc_fence_after();
 #pragma unroll
@@ -1352,8 +1333,7 @@ __global__ void __launch_bounds__(448, 1)
       if (!mbar_wait_warp(dq_full, it & 1, abort_flag, a.err, ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
       if (issuer) fa_stamp(a.trace, 2, it, 1);
       tc_fence_after();
-      // two 64-column halves (64 registers); each half of R1 is released as soon as it has
-      // been read, so the next dP^T half can go into it while the rest drains
+      // two 64-column halves (64 registers); R1 is released once both have been read
 #pragma unroll 1
       for (int hh = 0; hh < 2 && ok; ++hh) {
         uint32_t o[2][32];
@@ -1361,9 +1341,11 @@ __global__ void __launch_bounds__(448, 1)
         tmem_ld_32x32b_x32(tR1 + lane_off + hh * 64, o[0]);
         tmem_ld_32x32b_x32(tR1 + lane_off + hh * 64 + 32, o[1]);
         tmem_ld_wait();
-        tc_fence_before();
-        mbar_arrive(hh == 0 ? dq_free : dq_free_hi);  // this half of R1 may take the next dP^T half
-        if (hh == 1 && issuer) fa_stamp(a.trace, 2, it, 2);
+        if (hh == 1) {
+          tc_fence_before();
+          mbar_arrive(dq_free);  // R1 may take dP^T of the next tile
+          if (issuer) fa_stamp(a.trace, 2, it, 2);
+        }
 #pragma unroll
         for (int c2 = 0; c2 < 2; ++c2, ++g) {
           const int cc = hh * 2 + c2;
