@@ -8,10 +8,12 @@
 //    shared memory is spent on 128-row padding of X; the accumulator is 128 TMEM lanes
 //    (weight rows) x Mpad fp32 columns (activation rows);
 //  * split-K over a thread-block cluster of S CTAs (S in 1, 2, 4, 8): every CTA of a
-//    cluster owns the same 128 weight rows and a slice of K, and the partial tiles are
-//    summed through distributed shared memory (ld.shared::cluster).  No fp32 workspace in
-//    global memory, no atomics, nothing to re-zero between launches, so a captured CUDA
-//    graph replays it as is;
+//    cluster owns the same 128 weight rows and a slice of K; each CTA pushes the rows of
+//    its partial tile that rank r finishes into rank r's shared memory with one bulk copy
+//    (cp.async.bulk shared::cta -> shared::cluster, counted on rank r's mbarrier), and
+//    rank r adds the S partials in rank order.  No fp32 workspace in global memory, no
+//    atomics, nothing to re-zero between launches, so a captured CUDA graph replays it
+//    as is;
 //  * programmatic dependent launch: the weight slabs do not depend on the previous kernel,
 //    so the producer issues their TMA loads before griddepcontrol.wait, and each CTA
 //    triggers its dependents once its MMAs are done, so the next kernel's weight stream
@@ -29,9 +31,11 @@
 //    squares of its K slice of X to the cluster reduction.
 //
 // Warp roles (192 threads): warp 0 lane 0 TMA producer, warp 1 TMEM owner + MMA issuer,
-// warps 2-5 epilogue (sums of squares, TMEM -> shared partial tile, then the cluster
-// reduction of the rows this CTA owns: rank r of the cluster finishes rows
-// [r * ceil(M / S), (r + 1) * ceil(M / S))).  Every wait is bounded (sm100_common.cuh).
+// warps 2-5 epilogue (sums of squares, TMEM -> shared partial tile, the pushes, then the
+// rows this CTA owns: rank r of the cluster finishes rows [r * mr, (r + 1) * mr), mr =
+// ceil(M / S) rounded up to 4).  One cluster barrier, split into an arrive after set-up
+// and a wait before the first push, guarantees every peer's mbarrier is initialised.
+// Every wait is bounded (sm100_common.cuh).
 //
 // The ops fused here are the reference's per-block decode math (train.py:2564-2567
 // attention inputs, train.py:2415-2420 rotary, train.py:1432-1433 norm, train.py:2218-2234
