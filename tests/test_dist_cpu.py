@@ -214,3 +214,25 @@ def test_dist_muon_matches_allreduce(tmp_path):
             assert torch.allclose(v, ref, rtol=1e-2, atol=1e-4), k
         else:  # AdamW tensors: eps=1e-10 turns rounding-level gradient noise into +-lr steps
             assert (v - ref).abs().mean() <= 2e-2 * ref.abs().mean() + 1e-6, k
+
+
+def test_owner_plan_balances_whole_step_cost():
+    """Distributed-Muon ownership: every matrix has exactly one owner, and each rank's
+    Newton-Schulz cost summed over all buckets is balanced (the greedy carries each rank's
+    cost from bucket to bucket instead of restarting, which used to hand the heaviest unit
+    of every bucket to the same rank)."""
+    sys.path.insert(0, ROOT)
+    from trainium_frontier_b200.config import preset
+    from trainium_frontier_b200.models.gpt import GPT
+    from trainium_frontier_b200.parallel.dist_muon import plan_buckets, unit_cost
+    cfg = preset("tiny", depth=8, n_embd=256, head_dim=64, seq_len=256)
+    with torch.device("meta"):
+        model = GPT(cfg.model_config(), cfg)
+    muon_ids = {id(p) for b in model.transformer.h for p in b.parameters() if p.dim() == 2}
+    for world in (2, 4, 8):
+        plans = plan_buckets(model, muon_ids, world, bucket_layers=2)
+        owned = [id(p) for pl in plans for r in range(world) for u in pl.owners[r] for p in u.params]
+        assert sorted(owned) == sorted(muon_ids)  # each matrix owned once
+        tot = [sum(unit_cost(u) for pl in plans for u in pl.owners[r]) for r in range(world)]
+        biggest = max(unit_cost(u) for pl in plans for r in range(world) for u in pl.owners[r])
+        assert max(tot) - min(tot) <= biggest + 1e-12, (world, tot)
