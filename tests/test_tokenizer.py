@@ -110,3 +110,22 @@ def test_trusted_artifact(tmp_path):
     assert tok.get_vocab_size() == 8192
     text = "Hello world, this is a test."
     assert tok.decode(tok.encode(text)) == text
+
+
+def test_harness_ensure_tokenizer(tok, tmp_path):
+    """The harness's setup step verifies and unpacks a named archive (none: nothing to do)."""
+    from trainium_frontier_b200.harness import ensure_tokenizer
+    assert ensure_tokenizer(tmp_path, None) is None
+    src = tmp_path / "src"
+    tok.save(src)
+    archive = tmp_path / "tok.zip"
+    with zipfile.ZipFile(archive, "w") as z:
+        z.write(src / "tokenizer.pkl", "tokenizer.pkl")
+        z.write(src / "token_bytes.pt", "token_bytes.pt")
+    sha = lambda p: hashlib.sha256(p.read_bytes()).hexdigest()  # noqa: E731
+    back = ensure_tokenizer(tmp_path / "cache", archive, expected_sha=sha(archive), pkl_sha=sha(src / "tokenizer.pkl"),
+                            token_bytes_sha=sha(src / "token_bytes.pt"), expected_vocab=600)
+    assert (tmp_path / "cache" / "tokenizer" / "tokenizer.pkl").exists()
+    assert back.encode("the model") == tok.encode("the model")
+    with pytest.raises(RuntimeError):
+        ensure_tokenizer(tmp_path / "cache2", archive)  # the trusted pins do not match this archive

@@ -96,6 +96,18 @@ def ensure_data(cache_dir: str | Path = CACHE_DIR, stream_tokens: int = 1 << 20,
     return manifest
 
 
+def ensure_tokenizer(cache_dir: str | Path = CACHE_DIR, archive: str | Path | None = None, **pins):
+    """Verify the trusted tokenizer archive (its SHA-256 pins, or ``pins`` overrides:
+    ``expected_sha``, ``pkl_sha``, ``token_bytes_sha``, ``expected_vocab``), unpack it into
+    ``<cache_dir>/tokenizer`` and return the loaded ``Tokenizer``; None when no archive is
+    named.  The training pipeline itself runs on the synthetic corpus.
+    Reference counterpart: ``ensure_tokenizer`` (``prepare.py:368-396``)."""
+    if not archive:
+        return None
+    from .data.tokenizer import Tokenizer
+    return Tokenizer.from_zip(archive, Path(cache_dir) / "tokenizer", **pins)
+
+
 # --------------------------------------------------------------------------- static checks
 FORBIDDEN_IMPORT_ROOTS = frozenset({"socket", "subprocess", "requests", "urllib", "http", "ftplib"})
 FORBIDDEN_ATTR_CALLS = frozenset({("os", "system"), ("os", "popen"), ("shutil", "rmtree"), ("subprocess", "run"),
@@ -233,6 +245,8 @@ def main(argv: list[str] | None = None) -> None:
     s = sub.add_parser("setup")
     s.add_argument("--cache-dir", default=str(CACHE_DIR))
     s.add_argument("--stream-tokens", type=int, default=1 << 20)
+    s.add_argument("--tokenizer-zip", default=os.environ.get("NEURON_COMPETITION_R1_TOKENIZER_PATH", ""),
+                   help="trusted 8192-token tokenizer archive to verify and unpack (optional)")
     c = sub.add_parser("check")
     c.add_argument("--train-py", required=True)
     c.add_argument("--launch-command", default=None)
@@ -247,6 +261,9 @@ def main(argv: list[str] | None = None) -> None:
     a = ap.parse_args(argv)
     if a.cmd == "setup":
         m = ensure_data(a.cache_dir, a.stream_tokens)
+        tok = ensure_tokenizer(a.cache_dir, a.tokenizer_zip)
+        if tok is not None:
+            print(f"tokenizer verified: vocab {tok.get_vocab_size()}, BOS {tok.get_bos_token_id()}")
         print(f"setup complete: {a.cache_dir} (token bytes {m['token_bytes_sha256'][:12]}...)")
     elif a.cmd == "check":
         w = check_submission(a.train_py, a.launch_command)
