@@ -1,0 +1,73 @@
+"""Text training rows (CPU): tokenized documents packed BOS-aligned best-fit by the
+native DocPacker, from an iterable of strings or from parquet row groups."""
+import random
+
+import pytest
+import torch
+
+from trainium_frontier_b200.data.text_loader import parquet_documents, text_dataloader
+from trainium_frontier_b200.data.tokenizer import train_bpe
+
+
+def _docs(n, seed=0):
+    rnd = random.Random(seed)
+    words = ["alpha", "beta", "gamma", "delta", "tensor", "core", "über", "42", "kernel", "memory"]
+    return [f"doc{i} " + " ".join(rnd.choice(words) for _ in range(rnd.randint(3, 60))) for i in range(n)]
+
+
+@pytest.fixture(scope="module")
+def tok():
+    return train_bpe(_docs(300, seed=7), vocab_size=400)
+
+
+def test_rows_are_bos_aligned_documents(tok):
+    docs = _docs(2000)
+    T = 128
+    batches = list(text_dataloader(tok, docs, batch_size=4, seq_len=T, buffer_min=32))
+    assert batches, "no rows"
+    bos = tok.get_bos_token_id()
+    encoded = {tuple(tok.encode(d)) for d in docs}
+    whole = 0
+    for x, y in batches:
+        assert x.dtype == torch.int32 and y.dtype == torch.int64 and x.shape == (4, T) and y.shape == (4, T)
+        assert torch.equal(x[:, 1:].long(), y[:, :-1])
+        for row in torch.cat([x, y[:, -1:].int()], 1).tolist():
+            assert row[0] == bos  # every row starts with a document
+            # split at BOS: every piece is a document, whole or (the last one) cropped
+            starts = [i for i, t in enumerate(row) if t == bos]
+            for a, b in zip(starts, starts[1:] + [len(row)]):
+                piece = tuple(row[a + 1:b])
+                if b < len(row):
+                    assert piece in encoded
+                    whole += 1
+                else:
+                    assert any(e[:len(piece)] == piece for e in encoded)
+    assert whole > 0
+
+
+def test_rank_striding_and_end_of_data(tok):
+    docs = _docs(400, seed=3)
+    T = 64
+    seen = []
+    for r in range(2):
+        n = 0
+        for x, _ in text_dataloader(tok, docs, batch_size=2, seq_len=T, rank=r, world=2, buffer_min=8):
+            n += x.shape[0]
+            seen.append(x)
+        assert n > 0
+    # the two ranks' first rows differ (different documents)
+    assert not torch.equal(seen[0], seen[-1])
+
+
+def test_parquet_documents(tok, tmp_path):
+    pa = pytest.importorskip("pyarrow")
+    import pyarrow.parquet as pq
+    docs = _docs(300, seed=5)
+    path = tmp_path / "shard.parquet"
+    pq.write_table(pa.table({"text": docs}), path, row_group_size=50)
+    assert list(parquet_documents([path])) == docs
+    r0 = list(parquet_documents([path], rank=0, world=2))
+    r1 = list(parquet_documents([path], rank=1, world=2))
+    assert sorted(r0 + r1) == sorted(docs) and len(r0) == 150  # 6 row groups, alternating
+    x, y = next(text_dataloader(tok, parquet_documents([path]), batch_size=2, seq_len=64, buffer_min=16))
+    assert x[0, 0] == tok.get_bos_token_id()

@@ -103,6 +103,40 @@ class ZipfDocSource {
   std::vector<double> cdf_;
 };
 
+// One row of capacity `cap` from the buffered documents: the longest document that still
+// fits the remaining capacity is placed whole; if none fits, the shortest one is cropped
+// to fill the row.  `refill` tops the buffer up before every pick (synthetic source) or
+// is a no-op (documents pushed by the caller).  Returns false if the buffer ran dry.
+template <typename Refill>
+bool fill_row(std::vector<std::vector<int64_t>>& buf, int32_t* row, int64_t cap, Refill refill) {
+  int64_t pos = 0;
+  while (pos < cap) {
+    refill();
+    if (buf.empty()) return false;
+    const int64_t remaining = cap - pos;
+    int64_t best = -1, best_len = 0;
+    for (int64_t i = 0; i < int64_t(buf.size()); ++i) {
+      const int64_t n = int64_t(buf[i].size());
+      if (n <= remaining && n > best_len) { best = i; best_len = n; }
+    }
+    if (best >= 0) {
+      const auto& d = buf[best];
+      for (int64_t j = 0; j < best_len; ++j) row[pos + j] = int32_t(d[j]);
+      pos += best_len;
+      buf.erase(buf.begin() + best);
+    } else {
+      int64_t shortest = 0;
+      for (int64_t i = 1; i < int64_t(buf.size()); ++i)
+        if (buf[i].size() < buf[shortest].size()) shortest = i;
+      const auto& d = buf[shortest];
+      for (int64_t j = 0; j < remaining; ++j) row[pos + j] = int32_t(d[j]);
+      pos += remaining;
+      buf.erase(buf.begin() + shortest);
+    }
+  }
+  return true;
+}
+
 class BestFitPacker {
  public:
   BestFitPacker(int64_t vocab, double zipf_s, double mean_doc_len, uint64_t seed, int64_t bos,
@@ -117,33 +151,10 @@ class BestFitPacker {
     const int64_t B = rows.size(0), cap = rows.size(1);
     int32_t* out = rows.data_ptr<int32_t>();
     pybind11::gil_scoped_release nogil;
-    for (int64_t r = 0; r < B; ++r) {
-      int32_t* row = out + r * cap;
-      int64_t pos = 0;
-      while (pos < cap) {
-        while (int64_t(buf_.size()) < buffer_min_) buf_.push_back(src_.next_doc());
-        const int64_t remaining = cap - pos;
-        int64_t best = -1, best_len = 0;
-        for (int64_t i = 0; i < int64_t(buf_.size()); ++i) {
-          const int64_t n = int64_t(buf_[i].size());
-          if (n <= remaining && n > best_len) { best = i; best_len = n; }
-        }
-        if (best >= 0) {
-          const auto& d = buf_[best];
-          for (int64_t j = 0; j < best_len; ++j) row[pos + j] = int32_t(d[j]);
-          pos += best_len;
-          buf_.erase(buf_.begin() + best);
-        } else {
-          int64_t shortest = 0;
-          for (int64_t i = 1; i < int64_t(buf_.size()); ++i)
-            if (buf_[i].size() < buf_[shortest].size()) shortest = i;
-          const auto& d = buf_[shortest];
-          for (int64_t j = 0; j < remaining; ++j) row[pos + j] = int32_t(d[j]);
-          pos += remaining;
-          buf_.erase(buf_.begin() + shortest);
-        }
-      }
-    }
+    auto refill = [this] {
+      while (int64_t(buf_.size()) < buffer_min_) buf_.push_back(src_.next_doc());
+    };
+    for (int64_t r = 0; r < B; ++r) fill_row(buf_, out + r * cap, cap, refill);
   }
 
   // Contiguous (unpacked) token stream: documents back to back, used by the
@@ -176,6 +187,44 @@ class BestFitPacker {
   int64_t stream_pos_ = 0;
 };
 
+// The same packing over documents the caller supplies (tokenized text): push() appends
+// whole documents (BOS first) to the buffer; fill() packs rows while the buffer holds at
+// least `buffer_min` documents at the start of a row (with `drain`, until it is empty, for
+// the end of the data) and returns how many rows of [r0, B) it completed.  Unlike the
+// synthetic source, which tops the buffer up before every pick, the caller refills
+// between fill() calls, so within one row the buffer may dip below buffer_min.
+class DocPacker {
+ public:
+  explicit DocPacker(int64_t buffer_min) : buffer_min_(buffer_min) {}
+
+  void push(torch::Tensor doc) {
+    TORCH_CHECK(doc.device().is_cpu() && doc.dim() == 1 && doc.numel() > 0, "a non-empty 1-D host tensor");
+    auto d = doc.to(torch::kInt64).contiguous();
+    const int64_t* p = d.data_ptr<int64_t>();
+    buf_.emplace_back(p, p + d.numel());
+  }
+
+  int64_t buffered() const { return int64_t(buf_.size()); }
+
+  int64_t fill(torch::Tensor rows, int64_t r0, bool drain) {
+    TORCH_CHECK(rows.dtype() == torch::kInt32 && rows.is_contiguous() && rows.dim() == 2 && rows.device().is_cpu(),
+                "rows must be a contiguous int32 [B, T+1] host tensor");
+    const int64_t B = rows.size(0), cap = rows.size(1);
+    int32_t* out = rows.data_ptr<int32_t>();
+    pybind11::gil_scoped_release nogil;
+    int64_t r = r0;
+    for (; r < B; ++r) {
+      if (buf_.empty() || (!drain && int64_t(buf_.size()) < buffer_min_)) break;
+      if (!fill_row(buf_, out + r * cap, cap, [] {})) break;
+    }
+    return r - r0;
+  }
+
+ private:
+  int64_t buffer_min_;
+  std::vector<std::vector<int64_t>> buf_;
+};
+
 torch::Tensor token_bytes_table(int64_t vocab, uint64_t seed, int64_t lo, int64_t hi,
                                 int64_t n_special) {
   auto t = torch::empty({vocab}, torch::kInt32);
@@ -200,5 +249,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("fill", &BestFitPacker::fill)
       .def("fill_stream", &BestFitPacker::fill_stream)
       .def("next_doc", &BestFitPacker::next_doc);
+  pybind11::class_<DocPacker>(m, "DocPacker")
+      .def(pybind11::init<int64_t>(), pybind11::arg("buffer_min"))
+      .def("push", &DocPacker::push)
+      .def("buffered", &DocPacker::buffered)
+      .def("fill", &DocPacker::fill, pybind11::arg("rows"), pybind11::arg("r0"), pybind11::arg("drain"));
   m.def("token_bytes_table", &token_bytes_table, "seeded per-token byte lengths");
 }
