@@ -71,3 +71,39 @@ def test_parquet_documents(tok, tmp_path):
     assert sorted(r0 + r1) == sorted(docs) and len(r0) == 150  # 6 row groups, alternating
     x, y = next(text_dataloader(tok, parquet_documents([path]), batch_size=2, seq_len=64, buffer_min=16))
     assert x[0, 0] == tok.get_bos_token_id()
+
+
+def test_trainer_on_text_files(tok, tmp_path, monkeypatch):
+    """--text-data / --tokenizer-zip: the trainer packs rows from parquet text tokenized
+    with the verified archive (epochs repeat when the files run out) and takes steps."""
+    import hashlib
+    import zipfile
+    pa = pytest.importorskip("pyarrow")
+    import pyarrow.parquet as pq
+    from trainium_frontier_b200.config import preset
+    from trainium_frontier_b200.train import Trainer
+    for i in range(2):
+        pq.write_table(pa.table({"text": _docs(150, seed=20 + i)}), tmp_path / f"s{i}.parquet", row_group_size=30)
+    src = tmp_path / "tok"
+    tok.save(src)
+    archive = tmp_path / "tok.zip"
+    with zipfile.ZipFile(archive, "w") as z:
+        z.write(src / "tokenizer.pkl", "tokenizer.pkl")
+        z.write(src / "token_bytes.pt", "token_bytes.pt")
+    sha = lambda p: hashlib.sha256(p.read_bytes()).hexdigest()  # noqa: E731
+    monkeypatch.setenv("NEURON_COMPETITION_R1_TOKENIZER_SHA256", sha(archive))
+    monkeypatch.setenv("NEURON_COMPETITION_R1_TOKENIZER_PKL_SHA256", sha(src / "tokenizer.pkl"))
+    monkeypatch.setenv("NEURON_COMPETITION_R1_TOKEN_BYTES_SHA256", sha(src / "token_bytes.pt"))
+    monkeypatch.setenv("NEURON_COMPETITION_R1_CACHE_DIR", str(tmp_path / "cache"))
+    V = tok.get_vocab_size()
+    cfg = preset("tiny", depth=2, n_embd=128, head_dim=64, seq_len=64, vocab_size=V, device_batch_size=2,
+                 total_batch_size=2 * 64, progress_mode="steps", num_steps=5, text_data=str(tmp_path / "s*.parquet"),
+                 tokenizer_zip=str(archive))
+    tr = Trainer(cfg, torch.device("cpu"))
+    rows = tr.loader.next()
+    assert rows.shape == (2, 65) and int(rows[0, 0]) == tok.get_bos_token_id() and int(rows.max()) < V
+    losses = [tr.train_step() for _ in range(3)]
+    assert all(l == l for l in losses)
+    for _ in range(40):  # well past one epoch of the two small files
+        tr.loader.next()
+    assert tr.loader.packer.epoch >= 1

@@ -226,6 +226,8 @@ class RunConfig:
     synthetic_epoch_tokens: int = 0    # tokens per epoch of the synthetic train stream per rank; 0 = endless
     epoch_shuffle: bool = False        # from epoch 2 on, a fresh order (seed + epoch) instead of epoch 1 replayed
     epoch_shuffle_seed: int = 1234
+    text_data: str = ""                # glob of parquet files with a "text" column: train on them instead
+    tokenizer_zip: str = ""            # the tokenizer archive the text is tokenized with (SHA-verified)
     # ---- reference switches with a real effect here --------------------------------
     grad_bucket: bool = False          # one flat-buffer gradient all-reduce: maps to grad_sync=bucket under auto
     transposed_linear: bool = False    # [in, out] weight storage: not built (changes the checkpoint layout)

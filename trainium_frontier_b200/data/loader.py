@@ -109,13 +109,17 @@ class PackedRowLoader:
 
     def __init__(self, batch_size: int, seq_len: int, device: torch.device, split: str = "train",
                  seed: int | None = None, rank: int | None = None, vocab: int = 8192, depth: int = 2,
-                 epoch_tokens: int = 0, epoch_shuffle: bool = False, epoch_shuffle_seed: int = 1234):
+                 epoch_tokens: int = 0, epoch_shuffle: bool = False, epoch_shuffle_seed: int = 1234,
+                 packer=None):
         if rank is None:
             rank = get_dist_info()[1]
         self.B, self.T = batch_size, seq_len
         self.device = torch.device(device)
-        self.packer = EpochPacker(split, rank, seed, vocab, epoch_rows=_epoch_rows(epoch_tokens, seq_len),
-                                  shuffle=epoch_shuffle, shuffle_seed=epoch_shuffle_seed)
+        # any object with fill(host int32 [B, T+1]) can stand in for the synthetic stream
+        # (data.text_loader.TextPacker for text files)
+        self.packer = packer if packer is not None else EpochPacker(
+            split, rank, seed, vocab, epoch_rows=_epoch_rows(epoch_tokens, seq_len), shuffle=epoch_shuffle,
+            shuffle_seed=epoch_shuffle_seed)
         cuda = self.device.type == "cuda"
         self.depth = depth
         self.host = [torch.empty((batch_size, seq_len + 1), dtype=torch.int32, pin_memory=cuda)

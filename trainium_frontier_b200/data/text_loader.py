@@ -88,3 +88,48 @@ def text_dataloader(tokenizer, documents: Iterable[str], batch_size: int, seq_le
         x = rows[:, :-1].to(dev, non_blocking=pin)
         y = rows[:, 1:].to(dev, dtype=torch.int64, non_blocking=pin)
         yield x, y
+
+
+class TextPacker:
+    """Endless packed rows from text files for the trainer: ``fill(rows)`` fills a host
+    ``[B, T+1]`` int32 tensor (the interface of the synthetic packers, so
+    ``PackedRowLoader`` double-buffers it the same way), starting the next epoch over the
+    files when the documents run out.  Rank ``rank`` of ``world`` reads every
+    ``world``-th parquet row group."""
+
+    def __init__(self, tokenizer, paths, rank: int = 0, world: int = 1, column: str = "text",
+                 buffer_min: int = BUFFER_MIN, num_threads: int = 4):
+        self.tok, self.paths, self.rank, self.world = tokenizer, list(paths), rank, world
+        self.column, self.buffer_min, self.num_threads = column, buffer_min, num_threads
+        if not self.paths:
+            raise ValueError("no text data files")
+        self.packer = _native().DocPacker(buffer_min)
+        self.epoch = 0
+        self._docs = parquet_documents(self.paths, column, rank, world)
+
+    def _top_up(self, want: int) -> None:
+        bos = self.tok.get_bos_token_id()
+        fresh_epoch = False
+        while self.packer.buffered() < want:
+            chunk = []
+            for s in self._docs:
+                chunk.append(s)
+                if len(chunk) == ENCODE_CHUNK:
+                    break
+            if not chunk:
+                if fresh_epoch:
+                    raise ValueError("the text data holds too few documents to fill the packing buffer")
+                self.epoch += 1
+                fresh_epoch = True
+                self._docs = parquet_documents(self.paths, self.column, self.rank, self.world)
+                continue
+            fresh_epoch = False
+            for ids in self.tok.encode(chunk, prepend=bos, num_threads=self.num_threads):
+                self.packer.push(torch.tensor(ids, dtype=torch.int64))
+
+    def fill(self, rows: torch.Tensor) -> None:
+        want = self.buffer_min + rows.shape[1] // 2 + 1
+        r = 0
+        while r < rows.shape[0]:
+            self._top_up(want)
+            r += self.packer.fill(rows, r, False)

@@ -54,6 +54,11 @@ def _sha256(path: Path) -> str:
     return h.hexdigest()
 
 
+def _pin(env: str, default: str, given: str | None) -> str:
+    """An explicit hash, else the environment override, else the pinned default."""
+    return given if given is not None else os.environ.get(env, default)
+
+
 def _require_sha(path: Path, expected: str, what: str) -> None:
     if not expected:
         raise RuntimeError(f"refusing to load {path}: no expected SHA-256 for the {what}")
@@ -70,10 +75,12 @@ class Tokenizer:
 
     # ------------------------------------------------------------------ loading
     @classmethod
-    def from_directory(cls, directory, *, expected_sha: str = PKL_SHA256,
+    def from_directory(cls, directory, *, expected_sha: str | None = None,
                        expected_vocab: int | None = VOCAB_SIZE) -> "Tokenizer":
+        """``expected_sha`` None: the pinned hash (or its environment override, read now)."""
         path = Path(directory) / "tokenizer.pkl"
-        _require_sha(path, expected_sha, "tokenizer.pkl")
+        _require_sha(path, _pin("NEURON_COMPETITION_R1_TOKENIZER_PKL_SHA256", PKL_SHA256, expected_sha),
+                     "tokenizer.pkl")
         with open(path, "rb") as f:
             enc = pickle.load(f)
         tok = cls(enc)
@@ -85,10 +92,12 @@ class Tokenizer:
         return tok
 
     @classmethod
-    def from_zip(cls, archive, cache_dir, *, expected_sha: str = ARTIFACT_SHA256, pkl_sha: str = PKL_SHA256,
-                 token_bytes_sha: str = TOKEN_BYTES_SHA256, expected_vocab: int | None = VOCAB_SIZE) -> "Tokenizer":
+    def from_zip(cls, archive, cache_dir, *, expected_sha: str | None = None, pkl_sha: str | None = None,
+                 token_bytes_sha: str | None = None, expected_vocab: int | None = VOCAB_SIZE) -> "Tokenizer":
+        """Hashes left None: the pinned ones (or their environment overrides, read now)."""
         archive, cache_dir = Path(archive), Path(cache_dir)
-        _require_sha(archive, expected_sha, "tokenizer archive")
+        _require_sha(archive, _pin("NEURON_COMPETITION_R1_TOKENIZER_SHA256", ARTIFACT_SHA256, expected_sha),
+                     "tokenizer archive")
         cache_dir.mkdir(parents=True, exist_ok=True)
         with zipfile.ZipFile(archive) as z:
             for name in ("tokenizer.pkl", "token_bytes.pt"):
@@ -96,7 +105,9 @@ class Tokenizer:
                 if member is None:
                     raise RuntimeError(f"{archive} has no {name}")
                 (cache_dir / name).write_bytes(z.read(member))
-        _require_sha(cache_dir / "token_bytes.pt", token_bytes_sha, "token_bytes.pt")
+        _require_sha(cache_dir / "token_bytes.pt",
+                     _pin("NEURON_COMPETITION_R1_TOKEN_BYTES_SHA256", TOKEN_BYTES_SHA256, token_bytes_sha),
+                     "token_bytes.pt")
         return cls.from_directory(cache_dir, expected_sha=pkl_sha, expected_vocab=expected_vocab)
 
     # ------------------------------------------------------------------ interface

@@ -89,7 +89,8 @@ class Trainer:
         self.loader = PackedRowLoader(self.rows_per_micro, cfg.seq_len, self.device, "train",
                                       rank=rank // cfg.pp, epoch_tokens=cfg.synthetic_epoch_tokens,
                                       epoch_shuffle=cfg.epoch_shuffle,
-                                      epoch_shuffle_seed=cfg.epoch_shuffle_seed) if build_loader else None
+                                      epoch_shuffle_seed=cfg.epoch_shuffle_seed,
+                                      packer=self._text_packer(rank // cfg.pp, data_ranks)) if build_loader else None
         self.step_idx = 0
         self._adamw_applied_last = True   # AdamW gradients are zeroed only after they were applied
         self.loss_scale = cfg.loss_scale
@@ -161,6 +162,23 @@ class Trainer:
     @property
     def h2d_bytes_per_step(self) -> int:
         return self.grad_accum * self.rows_per_micro * (self.cfg.seq_len + 1) * 4
+
+    def _text_packer(self, rank: int, world: int):
+        """Packed rows from ``--text-data`` parquet files tokenized with ``--tokenizer-zip``
+        (None: the synthetic stream)."""
+        cfg = self.cfg
+        if not cfg.text_data:
+            return None
+        import glob
+        from .data.text_loader import TextPacker
+        from .data.tokenizer import Tokenizer
+        from .harness import CACHE_DIR
+        if not cfg.tokenizer_zip:
+            raise ValueError("--text-data needs --tokenizer-zip (the tokenizer the text is encoded with)")
+        # the model's vocabulary must be the tokenizer's (from_zip checks it)
+        cache = os.environ.get("NEURON_COMPETITION_R1_CACHE_DIR", str(CACHE_DIR))
+        tok = Tokenizer.from_zip(cfg.tokenizer_zip, os.path.join(cache, "tokenizer"), expected_vocab=cfg.vocab_size)
+        return TextPacker(tok, sorted(glob.glob(cfg.text_data)), rank, world)
 
     def progress(self, elapsed: float) -> float:
         if self.cfg.progress_mode == "steps":
