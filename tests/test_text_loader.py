@@ -96,9 +96,10 @@ def test_trainer_on_text_files(tok, tmp_path, monkeypatch):
     monkeypatch.setenv("NEURON_COMPETITION_R1_TOKEN_BYTES_SHA256", sha(src / "token_bytes.pt"))
     monkeypatch.setenv("NEURON_COMPETITION_R1_CACHE_DIR", str(tmp_path / "cache"))
     V = tok.get_vocab_size()
+    pq.write_table(pa.table({"text": _docs(60, seed=99)}), tmp_path / "val.parquet", row_group_size=20)
     cfg = preset("tiny", depth=2, n_embd=128, head_dim=64, seq_len=64, vocab_size=V, device_batch_size=2,
                  total_batch_size=2 * 64, progress_mode="steps", num_steps=5, text_data=str(tmp_path / "s*.parquet"),
-                 tokenizer_zip=str(archive))
+                 tokenizer_zip=str(archive), text_val_data=str(tmp_path / "val.parquet"))
     tr = Trainer(cfg, torch.device("cpu"))
     rows = tr.loader.next()
     assert rows.shape == (2, 65) and int(rows[0, 0]) == tok.get_bos_token_id() and int(rows.max()) < V
@@ -107,3 +108,11 @@ def test_trainer_on_text_files(tok, tmp_path, monkeypatch):
     for _ in range(40):  # well past one epoch of the two small files
         tr.loader.next()
     assert tr.loader.packer.epoch >= 1
+    # the final evaluation scores the held-out text with its UTF-8 byte lengths
+    from trainium_frontier_b200.data.loader import make_eval_dataloader
+    from trainium_frontier_b200.eval import evaluate_bpb
+    etok = tr.eval_tokenizer()
+    x, y, _ = next(make_eval_dataloader(etok, 2, 64, "public_val", "cpu", max_stream_tokens=4096))
+    assert int(x[0, 0]) == tok.get_bos_token_id()
+    res = evaluate_bpb(tr.model, etok, 2, 64, "cpu", max_tokens=1024)
+    assert 0 < res["val_bpb"] < 100 and res["num_bytes"] > res["num_tokens"]  # multi-byte tokens

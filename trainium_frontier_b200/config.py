@@ -228,6 +228,7 @@ class RunConfig:
     epoch_shuffle_seed: int = 1234
     text_data: str = ""                # glob of parquet files with a "text" column: train on them instead
     tokenizer_zip: str = ""            # the tokenizer archive the text is tokenized with (SHA-verified)
+    text_val_data: str = ""            # glob of held-out parquet files the final evaluation scores (with --text-data)
     # ---- reference switches with a real effect here --------------------------------
     grad_bucket: bool = False          # one flat-buffer gradient all-reduce: maps to grad_sync=bucket under auto
     transposed_linear: bool = False    # [in, out] weight storage: not built (changes the checkpoint layout)

@@ -192,17 +192,38 @@ def _to_dev(bx, by, dev):
 def make_eval_dataloader(tokenizer, batch_size: int, seq_len: int, split: str,
                          device: torch.device | str, max_stream_tokens: int = 1 << 21,
                          seed: int | None = None, **_unused):
-    """Finite eval loader: a per-rank synthetic stream chunked into rows of stride
-    ``seq_len`` (reference ``prepare.py:521-585``)."""
+    """Finite eval loader: a per-rank token stream chunked into rows of stride ``seq_len``
+    (reference ``prepare.py:521-585``): the synthetic held-out stream, or, when the
+    tokenizer carries ``eval_documents(rank, world)`` (an iterable of held-out text), those
+    documents tokenized with BOS first."""
     assert batch_size > 0 and seq_len > 1
     _ddp, rank, _lr, world = get_dist_info()
     vocab = tokenizer.get_vocab_size() if tokenizer is not None else 8192
-    bos = syn.BOS_ID
-    packer = _packer(split, rank, seed, vocab)
     n_local = max(seq_len + 1, (max_stream_tokens + world - 1) // world)
-    stream_t = torch.empty(n_local, dtype=torch.int32)
-    packer.fill_stream(stream_t)
-    stream = stream_t.tolist()
+    docs_fn = getattr(tokenizer, "eval_documents", None)
+    if docs_fn is not None:
+        # held-out text: this rank's documents, BOS first, back to back
+        bos = tokenizer.get_bos_token_id()
+        stream = []
+        chunk = []
+        for s_ in docs_fn(rank, world):
+            chunk.append(s_)
+            if len(chunk) == 128:
+                for ids in tokenizer.encode(chunk, prepend=bos):
+                    stream.extend(ids)
+                chunk = []
+                if len(stream) >= n_local:
+                    break
+        if chunk and len(stream) < n_local:
+            for ids in tokenizer.encode(chunk, prepend=bos):
+                stream.extend(ids)
+        stream = stream[:n_local]
+    else:
+        bos = syn.BOS_ID
+        packer = _packer(split, rank, seed, vocab)
+        stream_t = torch.empty(n_local, dtype=torch.int32)
+        packer.fill_stream(stream_t)
+        stream = stream_t.tolist()
     dev = torch.device(device)
     bx: list[list[int]] = []
     by: list[list[int]] = []

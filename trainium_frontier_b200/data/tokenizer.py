@@ -72,6 +72,8 @@ class Tokenizer:
         self.enc = enc
         self.bos_token_id = enc.encode_single_token(BOS_TOKEN)
         self._token_bytes = None
+        # optional held-out text for evaluate_bpb: a callable (rank, world) -> iterable of str
+        self.eval_documents = None
 
     # ------------------------------------------------------------------ loading
     @classmethod

@@ -33,7 +33,9 @@ def evaluate_bpb(model: torch.nn.Module, tokenizer, batch_size: int, seq_len: in
     started = time.monotonic()
     dev = torch.device(device)
     vocab = tokenizer.get_vocab_size() if tokenizer is not None else TOKENIZER_VOCAB_SIZE
-    token_bytes = syn.get_token_bytes(dev, vocab)
+    # a text tokenizer's UTF-8 byte table, else the synthetic corpus's
+    token_bytes = (tokenizer.token_bytes().to(dev) if hasattr(tokenizer, "token_bytes")
+                   else syn.get_token_bytes(dev, vocab))
     world_size = dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
     limit = None if max_tokens is None else max(1, math.ceil(max_tokens / max(world_size, 1)))
     n_stream = stream_tokens or (max_tokens + world_size * (seq_len + 1) if max_tokens else 1 << 21)

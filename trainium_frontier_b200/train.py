@@ -86,6 +86,7 @@ class Trainer:
         self.grad_accum = cfg.total_batch_size // tokens_per_micro
         self.tokens_per_step = cfg.total_batch_size
         self.engine = TrainEngine(model, self.opt, cfg, self.device, self.grad_accum, cfg.grad_sync)
+        self.text_tok = None
         self.loader = PackedRowLoader(self.rows_per_micro, cfg.seq_len, self.device, "train",
                                       rank=rank // cfg.pp, epoch_tokens=cfg.synthetic_epoch_tokens,
                                       epoch_shuffle=cfg.epoch_shuffle,
@@ -178,7 +179,24 @@ class Trainer:
         # the model's vocabulary must be the tokenizer's (from_zip checks it)
         cache = os.environ.get("NEURON_COMPETITION_R1_CACHE_DIR", str(CACHE_DIR))
         tok = Tokenizer.from_zip(cfg.tokenizer_zip, os.path.join(cache, "tokenizer"), expected_vocab=cfg.vocab_size)
+        self.text_tok = tok
         return TextPacker(tok, sorted(glob.glob(cfg.text_data)), rank, world)
+
+    def eval_tokenizer(self):
+        """The tokenizer the post-training evaluation scores with: with ``--text-val-data``,
+        the text tokenizer over those held-out parquet files (UTF-8 byte lengths), else
+        the synthetic corpus's held-out stream."""
+        cfg = self.cfg
+        tok = getattr(self, "text_tok", None)
+        if tok is None or not cfg.text_val_data:
+            return syn.SyntheticTokenizer(cfg.vocab_size)
+        import glob
+        from .data.text_loader import parquet_documents
+        paths = sorted(glob.glob(cfg.text_val_data))
+        if not paths:
+            raise ValueError(f"--text-val-data {cfg.text_val_data!r} matches no files")
+        tok.eval_documents = lambda r, w: parquet_documents(paths, rank=r, world=w)
+        return tok
 
     def progress(self, elapsed: float) -> float:
         if self.cfg.progress_mode == "steps":
@@ -326,7 +344,7 @@ def run(cfg: RunConfig) -> dict:
         dist.barrier()
     if cfg.eval_public:
         tr.model.disable_tp()
-        tok = syn.SyntheticTokenizer(cfg.vocab_size)
+        tok = tr.eval_tokenizer()
         causal = causality_check(tr.model, tok, cfg.device_batch_size, cfg.seq_len, device)
         rows = max(1, cfg.device_batch_size * cfg.pack_factor)
         res = evaluate_bpb(tr.model, tok, rows, cfg.seq_len, device, max_tokens=cfg.eval_tokens)
