@@ -212,9 +212,25 @@ def _import_script(path: str):
 
 
 def eval_public(train_py: str, checkpoint: str, device: str = "", batch_size: int = 1, seq_len: int = 1024,
-                eval_tokens: int = 4 * 524288, timeout_seconds: int = EVAL_TIMEOUT_SECONDS) -> dict:
+                eval_tokens: int = 4 * 524288, timeout_seconds: int = EVAL_TIMEOUT_SECONDS,
+                text_val_data: str = "", tokenizer_zip: str = "", cache_dir: str | Path = CACHE_DIR) -> dict:
+    """Scores a checkpoint through the training script's own ``load_for_eval``: on the
+    synthetic held-out stream, or with ``text_val_data`` (parquet glob) on held-out text
+    tokenized with the verified ``tokenizer_zip``."""
     from .data.synthetic import SyntheticTokenizer
     from .eval import evaluate_bpb
+    tok = SyntheticTokenizer(TOKENIZER_VOCAB_SIZE)
+    if text_val_data:
+        import glob
+        from .data.text_loader import parquet_documents
+        # the model's vocabulary is checked against the tokenizer's by evaluate_bpb itself
+        tok = ensure_tokenizer(cache_dir, tokenizer_zip, expected_vocab=None)
+        if tok is None:
+            raise RuntimeError("held-out text needs --tokenizer-zip")
+        paths = sorted(glob.glob(text_val_data))
+        if not paths:
+            raise RuntimeError(f"{text_val_data!r} matches no files")
+        tok.eval_documents = lambda r, w: parquet_documents(paths, rank=r, world=w)
     mod = _import_script(train_py)
     if not hasattr(mod, "load_for_eval"):
         raise RuntimeError("the training script must define load_for_eval(checkpoint_path, device)")
@@ -231,7 +247,7 @@ def eval_public(train_py: str, checkpoint: str, device: str = "", batch_size: in
         own_pg = True
     try:
         model = mod.load_for_eval(checkpoint, dev)
-        return evaluate_bpb(model, SyntheticTokenizer(TOKENIZER_VOCAB_SIZE), batch_size, seq_len, dev,
+        return evaluate_bpb(model, tok, batch_size, seq_len, dev,
                             split="public_val", max_tokens=None if eval_tokens <= 0 else eval_tokens,
                             timeout_seconds=timeout_seconds)
     finally:
@@ -258,6 +274,9 @@ def main(argv: list[str] | None = None) -> None:
     e.add_argument("--seq-len", type=int, default=1024)
     e.add_argument("--eval-tokens", type=int, default=4 * 524288, help="0 = the whole public stream")
     e.add_argument("--timeout-seconds", type=int, default=EVAL_TIMEOUT_SECONDS)
+    e.add_argument("--text-val-data", default="", help="glob of held-out parquet text (default: synthetic stream)")
+    e.add_argument("--tokenizer-zip", default=os.environ.get("NEURON_COMPETITION_R1_TOKENIZER_PATH", ""))
+    e.add_argument("--cache-dir", default=str(CACHE_DIR))
     a = ap.parse_args(argv)
     if a.cmd == "setup":
         m = ensure_data(a.cache_dir, a.stream_tokens)
@@ -273,7 +292,8 @@ def main(argv: list[str] | None = None) -> None:
             raise SystemExit(1)
         print("check passed")
     else:
-        res = eval_public(a.train_py, a.checkpoint, a.device, a.batch_size, a.seq_len, a.eval_tokens, a.timeout_seconds)
+        res = eval_public(a.train_py, a.checkpoint, a.device, a.batch_size, a.seq_len, a.eval_tokens, a.timeout_seconds,
+                          a.text_val_data, a.tokenizer_zip, a.cache_dir)
         if int(os.environ.get("RANK", "0")) == 0:
             print(json.dumps(res, indent=2, sort_keys=True))
 
