@@ -31,7 +31,7 @@ from torch.autograd import Function
 
 from .config import RunConfig
 from .optim.muon_adamw import MuonAdamW
-from .runtime import is_dist, world
+from .runtime import world
 
 
 @dataclass

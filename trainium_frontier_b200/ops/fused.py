@@ -19,7 +19,6 @@ bf16 weight cache of ``Linear`` (``train.py:2237-2267``), parameter-free RMSNorm
 """
 from __future__ import annotations
 
-import math
 
 import torch
 from torch.autograd import Function
